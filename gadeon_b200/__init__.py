@@ -1,0 +1,23 @@
+"""gadeon_b200 -- B200-native paged KV cache for the full-attention layers of
+the Qwen3.5 Gated-DeltaNet hybrids (drop-in for leok7v/gadeon's PagePool /
+hostFlashDecode path).
+
+The compute lives in libgadeonkv.so (hand-written sm_100a CUDA behind the C
+ABI of include/gadeon_kv.h); this package is its Python binding.
+"""
+from .kv import (  # noqa: F401
+    EXPORTED,
+    GKV_ERR_BAD_SEQ,
+    GKV_ERR_CAPACITY,
+    GKV_ERR_CUDA,
+    GKV_ERR_INVALID,
+    GKV_ERR_NO_PAGES,
+    GKV_ERR_UNSUPPORTED,
+    GKV_OK,
+    LIB_PATH,
+    BlockPool,
+    GkvError,
+    PagePool,
+    host_flash_decode,
+    load_library,
+)

@@ -1,0 +1,772 @@
+// gkv_kernels.cu -- sm_100a kernels of the paged KV cache.
+//
+//   append_kernel   one CTA per touched page: appended rows, zero fill of a
+//                   fresh page, copy-on-write / clone-tail copies, block-table
+//                   entry.  Replaces PagePool.append/seed/clone's memcpys
+//                   (LLM/src/CoreML/PagedAttention.swift:85-143, :199-220) and
+//                   Metal kv_append / kv_append_batch
+//                   (LLM/metal/Kernels.metal:1446-1457, :1726-1740).
+//   attend_kernel   persistent split-K paged GQA attention for up to 16
+//                   query rows per kv head (decode: G rows; MTP verify:
+//                   n_q*G rows, causal among the drafts).  Replaces
+//                   hostFlashDecode (PagedAttention.swift:317-366), the
+//                   verify loop (LLM/src/CoreML/Engine.swift:2620-2646) and
+//                   Metal attn_head / attn_batch
+//                   (Kernels.metal:1339-1439, :1767-1793).
+//   compact_kernel  page-strided -> [KVH, len, dh] (PagePool.compact,
+//                   PagedAttention.swift:225-252).
+//
+// attend_kernel design (B200):
+//   * work unit = one TK-key tile of one (sequence, kv head); units are laid
+//     out sequence-major, kv-head-major inside; CTA c of a persistent grid
+//     takes the contiguous unit range [U*c/C, U*(c+1)/C), so every CTA moves
+//     the same number of K/V bytes whatever the context lengths;
+//   * a producer warp streams K and V page slabs with TMA
+//     (cp.async.bulk.tensor.2d, 128B swizzle, no multicast) into an
+//     NSTAGE-deep mbarrier ring; page ids come from the block table;
+//   * four consumer warps: QK^T with mma.sync m16n8k16 (fp16 in, fp32
+//     accumulate; the G (or n_q*G) query rows of the kv head form the M=16
+//     side, so every K/V byte is read once per kv head), online softmax in
+//     fp32 (exp2 domain) with the key range split across warps, P.V with the
+//     head dim split across warps;
+//   * an item split across CTAs writes (m, l, O) partials; the last CTA to
+//     finish the item (atomic counter, no spinning) merges them with the
+//     same online-softmax rule as pagedFlashBatched's host merge
+//     (PagedAttention.swift:396-409).
+#include <cuda_fp16.h>
+
+#include "gkv_kernels.cuh"
+
+namespace gkv {
+namespace {
+
+// ------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Every wait on an mbarrier is bounded: after kWaitLimitNs the waiter
+// records DEV_ERR_WAIT_TIMEOUT, raises the CTA's abort flag and gives up.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicOr(status, DEV_ERR_WAIT_TIMEOUT);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                          uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Named barrier over the consumer warps only (the producer never joins).
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// ------------------------------------------------------------ append
+__global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
+    const TouchedPage tp = p.pages[blockIdx.x];
+    const AppendEntry e = p.entries[tp.entry];
+    const int P = p.P, dh = p.dh, KVH = p.kvh;
+    const int CH = dh >> 3;  // 16-byte chunks per row
+    const int64_t page_lo = (int64_t)tp.pidx * P;
+    const int64_t row_lo = e.len_before, row_hi = (int64_t)e.len_before + e.n_new;
+    const bool whole = tp.src_pid != PAGE_EXISTING;
+    int s_lo, s_hi;
+    if (whole) {
+        s_lo = 0;
+        s_hi = P;
+    } else {
+        s_lo = (int)(max(row_lo, page_lo) - page_lo);
+        s_hi = (int)(min(row_hi, page_lo + P) - page_lo);
+    }
+    const int nslots = s_hi - s_lo;
+    const int64_t page_elems = (int64_t)KVH * P * dh;
+    const int64_t total = 2ll * KVH * nslots * CH;
+    for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+        const int c = (int)(i % CH);
+        int64_t rest = i / CH;
+        const int slot = s_lo + (int)(rest % nslots);
+        rest /= nslots;
+        const int h = (int)(rest % KVH);
+        const int kv = (int)(rest / KVH);
+        const int64_t pos = page_lo + slot;
+        const int64_t in_page = ((int64_t)h * P + slot) * dh;
+        uint4 val;
+        if (pos >= row_lo && pos < row_hi) {
+            const int64_t r = pos - row_lo;
+            const uint16_t *src = kv ? p.v_src : p.k_src;
+            const int64_t off = p.head_major ? ((int64_t)h * e.n_new + r) * dh
+                                             : (((int64_t)e.src_row0 + r) * KVH + h) * dh;
+            val = reinterpret_cast<const uint4 *>(src + off)[c];
+        } else if (tp.src_pid >= 0) {
+            const uint16_t *pool = kv ? p.v_pool : p.k_pool;
+            val = reinterpret_cast<const uint4 *>(pool + tp.src_pid * page_elems + in_page)[c];
+        } else {
+            val = make_uint4(0u, 0u, 0u, 0u);
+        }
+        uint16_t *pool = kv ? p.v_pool : p.k_pool;
+        reinterpret_cast<uint4 *>(pool + tp.pid * page_elems + in_page)[c] = val;
+    }
+    if (whole && threadIdx.x == 0)
+        p.table[(int64_t)e.seq_id * p.table_stride + tp.pidx] = tp.pid;
+}
+
+// ------------------------------------------------------------ compact
+__global__ void __launch_bounds__(256) compact_kernel(const CompactParams p) {
+    const int CH = p.dh >> 3;
+    const int64_t total = 2ll * p.kvh * p.len * CH;
+    const int64_t page_elems = (int64_t)p.kvh * p.P * p.dh;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % CH);
+        int64_t rest = i / CH;
+        const int64_t t = rest % p.len;
+        rest /= p.len;
+        const int h = (int)(rest % p.kvh);
+        const int kv = (int)(rest / p.kvh);
+        const int32_t pid = p.table[t / p.P];
+        const uint16_t *src = (kv ? p.v_pool : p.k_pool) + pid * page_elems +
+                              ((int64_t)h * p.P + t % p.P) * p.dh;
+        uint16_t *dst = (kv ? p.V : p.K) + ((int64_t)h * p.len + t) * p.dh;
+        reinterpret_cast<uint4 *>(dst)[c] = reinterpret_cast<const uint4 *>(src)[c];
+    }
+}
+
+// ------------------------------------------------------------ attend
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kRows = 16;  // query rows per (sequence, kv head) item
+
+template <int DH>
+struct Cfg {
+    static constexpr int TK = DH >= 512 ? 32 : 64;        // keys per tile
+    static constexpr int NCB = DH / 64;                    // 128-byte column blocks
+    static constexpr int CH = DH / 8;                      // 16-byte chunks per row
+    static constexpr int TILE_BYTES = TK * DH * 2;         // one K (or V) tile
+    static constexpr int NSTAGE = DH <= 128 ? 6 : 3;
+    static constexpr int KPW = TK / kConsumerWarps;        // keys per warp in QK
+    static constexpr int NT_QK = KPW / 8;                  // n8 tiles per warp in QK
+    static constexpr int DPW = DH / kConsumerWarps;        // head-dim columns per warp in PV
+    static constexpr int NT_PV = DPW / 8;
+    static constexpr bool Q_REGS = DH <= 256;              // keep Q fragments in registers
+    static constexpr int TKP = TK + 8;                     // padded P row (halves)
+    static constexpr int OFF_Q = NSTAGE * 2 * TILE_BYTES;
+    static constexpr int OFF_P = OFF_Q + kRows * DH * 2;
+    static constexpr int OFF_RED = OFF_P + kRows * TKP * 2;
+    static constexpr int OFF_BAR = OFF_RED + 2 * kConsumerWarps * kRows * 4;
+    static constexpr int OFF_FLAG = OFF_BAR + 2 * NSTAGE * 8;
+    static constexpr int SMEM = OFF_FLAG + 16;
+    static constexpr int SMEM_ALLOC = SMEM + 1024;
+    static_assert(TILE_BYTES % 1024 == 0, "tiles keep 1024-byte alignment");
+    static_assert(NT_PV % 2 == 0, "P.V loads n8 tiles in pairs");
+    static_assert(SMEM_ALLOC <= 227 * 1024, "fits one CTA per SM");
+};
+
+// Byte offset of (key t, 16-byte chunk c16) inside a K or V tile.  The tile
+// is [group][column block][BH rows][128 B]; 128B swizzle XORs the chunk with
+// the row's low three bits (every sub-tile starts 1024-byte aligned).
+__device__ __forceinline__ uint32_t tile_off(int t, int c16, int lbh, int ncb) {
+    const int g = t >> lbh, r = t & ((1 << lbh) - 1);
+    return (uint32_t)((((g * ncb + (c16 >> 3)) << lbh) + r) * 128 + (((c16 & 7) ^ (r & 7)) << 4));
+}
+
+// Q tile: [column block][16 rows][128 B], same swizzle.
+__device__ __forceinline__ uint32_t q_off(int row, int c16) {
+    return (uint32_t)(((c16 >> 3) * kRows + row) * 128 + (((c16 & 7) ^ (row & 7)) << 4));
+}
+
+// Walks work units in order: unit -> (sequence b, kv head, tile j).
+struct UnitWalker {
+    const AttendEntry *entries;
+    int n_seqs, kvh_count;
+    int b, kvh, j;
+    AttendEntry e;
+
+    __device__ void seek(int u, int n_seqs) {
+        int lo = 0, hi = n_seqs - 1;
+        while (lo < hi) {  // last b with unit_base <= u
+            const int mid = (lo + hi + 1) >> 1;
+            if (entries[mid].unit_base <= u) lo = mid;
+            else hi = mid - 1;
+        }
+        b = lo;
+        e = entries[b];
+        const int off = u - e.unit_base;
+        kvh = off / e.ntiles;
+        j = off - kvh * e.ntiles;
+    }
+    __device__ void next() {
+        if (++j < e.ntiles) return;
+        j = 0;
+        if (++kvh < kvh_count) return;
+        kvh = 0;
+        if (++b < n_seqs) e = entries[b];
+    }
+};
+
+__device__ __forceinline__ int cta_of_unit(int64_t u, int64_t units, int64_t ctas) {
+    return (int)(((u + 1) * ctas - 1) / units);
+}
+
+template <int DH, bool TMA>
+__global__ void __launch_bounds__(kThreads, 1)
+    attend_kernel(const __grid_constant__ AttendParams p, const __grid_constant__ CUtensorMap tmk,
+                  const __grid_constant__ CUtensorMap tmv) {
+    using C = Cfg<DH>;
+    constexpr int TK = C::TK, NSTAGE = C::NSTAGE;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
+    uint64_t *empty = full + NSTAGE;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_FLAG);
+    volatile int *merge_flag = abort_flag + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int64_t U = p.total_units, NC = gridDim.x;
+    const int u_begin = (int)(U * blockIdx.x / NC);
+    const int u_end = (int)(U * (blockIdx.x + 1) / NC);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
+        *merge_flag = 0;
+        fence_mbar_init();
+    }
+    // Stage buffers start zeroed so a tile slot that is never loaded holds
+    // finite values.
+    for (int i = threadIdx.x; i < NSTAGE * 2 * C::TILE_BYTES / 16; i += kThreads)
+        reinterpret_cast<uint4 *>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async();
+    __syncthreads();
+    if (u_begin >= u_end) return;
+
+    const int lP = __ffs(p.P) - 1;
+    const int lbh = TMA ? min(lP, __ffs(TK) - 1) : (__ffs(TK) - 1);  // log2 rows per tile group
+    const int KVH = p.kvh;
+    UnitWalker w{p.entries, p.n_seqs, KVH, 0, 0, 0, {}};
+    w.seek(u_begin, p.n_seqs);
+
+    if (warp == kConsumerWarps) {
+        // ================================================= producer warp
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = u_begin; u < u_end; ++u, w.next()) {
+            const int t0 = w.j * TK;
+            const int nkeys = min(TK, w.e.len - t0);
+            const int32_t *trow = p.table + (int64_t)w.e.seq_id * p.table_stride;
+            uint8_t *sK = smem + stage * 2 * C::TILE_BYTES;
+            uint8_t *sV = sK + C::TILE_BYTES;
+            if constexpr (TMA) {
+                const int ngroups = (nkeys + (1 << lbh) - 1) >> lbh;
+                int row0 = 0;
+                if (lane < ngroups) {  // table read before the wait hides its latency
+                    const int tg = t0 + (lane << lbh);
+                    int pid = __ldg(trow + (tg >> lP));
+                    if (pid < 0 || pid >= p.num_pages) {
+                        atomicOr(p.status, DEV_ERR_BAD_PAGE);
+                        pid = 0;
+                    }
+                    row0 = (pid * KVH + w.kvh) * p.P + (tg & (p.P - 1));
+                }
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) break;
+                if (lane == 0)
+                    mbar_expect_tx(&full[stage], (uint32_t)(ngroups << lbh) * DH * 2 * 2);
+                __syncwarp();
+                if (lane < ngroups) {
+#pragma unroll
+                    for (int cb = 0; cb < C::NCB; ++cb) {
+                        const uint32_t off = (uint32_t)((lane * C::NCB + cb) << lbh) * 128;
+                        tma_load_2d(smem_u32(sK) + off, &tmk, cb * 64, row0, &full[stage]);
+                        tma_load_2d(smem_u32(sV) + off, &tmv, cb * 64, row0, &full[stage]);
+                    }
+                }
+            } else {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) break;
+                const int64_t page_elems = (int64_t)KVH * p.P * DH;
+                for (int i = lane; i < nkeys * C::CH; i += 32) {
+                    const int t = i / C::CH, c16 = i - t * C::CH;
+                    const int pos = t0 + t;
+                    int pid = __ldg(trow + (pos >> lP));
+                    if (pid < 0 || pid >= p.num_pages) {
+                        atomicOr(p.status, DEV_ERR_BAD_PAGE);
+                        pid = 0;
+                    }
+                    const int64_t src =
+                        pid * page_elems + ((int64_t)w.kvh * p.P + (pos & (p.P - 1))) * DH + c16 * 8;
+                    const uint32_t off = tile_off(t, c16, lbh, C::NCB);
+                    cp_async16(smem_u32(sK) + off, p.k_pool + src);
+                    cp_async16(smem_u32(sV) + off, p.v_pool + src);
+                }
+                cp_async_wait_all();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[stage]);
+            }
+            if (++stage == NSTAGE) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+        return;
+    }
+
+    // ===================================================== consumer warps
+    const int tid = threadIdx.x;  // 0..127
+    uint8_t *sQ = smem + C::OFF_Q;
+    __half *sP = reinterpret_cast<__half *>(smem + C::OFF_P);
+    float *red_max = reinterpret_cast<float *>(smem + C::OFF_RED);
+    float *red_sum = red_max + kConsumerWarps * kRows;
+    const int G = p.G, R = p.n_q * p.G, nH = KVH * p.G;
+    const int lr = lane >> 2;  // fragment row (and row + 8)
+    const int lc = 2 * (lane & 3);
+    const int64_t pf = attend_partial_floats(DH);
+
+    float o[C::NT_PV][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    uint32_t qa[C::Q_REGS ? DH / 16 : 1][4];
+    int stage = 0;
+    uint32_t phase = 0;
+    bool item_start = true;
+    // Causal limits of this thread's two fragment rows: key t is visible to
+    // row r iff t <= len - n_q + r / G (padding rows use the last real row).
+    const int rq0 = min(lr, R - 1) / G, rq1 = min(lr + 8, R - 1) / G;
+
+    for (int u = u_begin; u < u_end; ++u) {
+        const int b = w.b, kvh = w.kvh, j = w.j, len = w.e.len;
+        if (item_start) {
+            consumer_sync();  // earlier readers of sQ are done
+            for (int i = tid; i < kRows * C::CH; i += 128) {
+                const int row = i / C::CH, c16 = i - row * C::CH;
+                uint4 val = make_uint4(0u, 0u, 0u, 0u);
+                if (row < R) {
+                    const int s = row / G, g = row - s * G;
+                    const uint16_t *src =
+                        p.q + (((int64_t)b * p.n_q + s) * nH + kvh * G + g) * DH + c16 * 8;
+                    val = *reinterpret_cast<const uint4 *>(src);
+                }
+                *reinterpret_cast<uint4 *>(sQ + q_off(row, c16)) = val;
+            }
+            consumer_sync();
+            if constexpr (C::Q_REGS) {
+#pragma unroll
+                for (int ks = 0; ks < DH / 16; ++ks) {
+                    const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    const int c16 = 2 * ks + (lane >> 4);
+                    ldsm_x4(smem_u32(sQ) + q_off(row, c16), qa[ks][0], qa[ks][1], qa[ks][2],
+                            qa[ks][3]);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < C::NT_PV; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+            m0 = m1 = -INFINITY;
+            l0 = l1 = 0.f;
+        }
+        const int t0 = j * TK;
+        const int nkeys = min(TK, len - t0);
+        uint8_t *sK = smem + stage * 2 * C::TILE_BYTES;
+        uint8_t *sV = sK + C::TILE_BYTES;
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) break;
+
+        // Rows past the sequence end may hold stale or other sequences'
+        // data; zero them in V so p = 0 never meets a non-finite value.
+        const bool partial = nkeys < TK;
+        if (partial) {
+            for (int i = tid; i < (TK - nkeys) * C::CH; i += 128) {
+                const int t = nkeys + i / C::CH, c16 = i % C::CH;
+                *reinterpret_cast<uint4 *>(sV + tile_off(t, c16, lbh, C::NCB)) =
+                    make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+
+        // ---- S = Q K^T for this warp's KPW keys
+        float s[C::NT_QK][4];
+#pragma unroll
+        for (int n = 0; n < C::NT_QK; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            if constexpr (C::Q_REGS) {
+                a0 = qa[ks][0];
+                a1 = qa[ks][1];
+                a2 = qa[ks][2];
+                a3 = qa[ks][3];
+            } else {
+                const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                ldsm_x4(smem_u32(sQ) + q_off(row, 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+            }
+            if constexpr (C::NT_QK >= 2) {
+#pragma unroll
+                for (int np = 0; np < C::NT_QK / 2; ++np) {
+                    const int key = warp * C::KPW + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+                    const int c16 = 2 * ks + ((lane >> 3) & 1);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(smem_u32(sK) + tile_off(key, c16, lbh, C::NCB), b0, b1, b2, b3);
+                    mma16816(s[2 * np], a0, a1, a2, a3, b0, b1);
+                    mma16816(s[2 * np + 1], a0, a1, a2, a3, b2, b3);
+                }
+            } else {
+                const int key = warp * C::KPW + (lane & 7);
+                const int c16 = 2 * ks + ((lane >> 3) & 1);
+                uint32_t b0, b1;
+                ldsm_x2(smem_u32(sK) + tile_off(key, c16, lbh, C::NCB), b0, b1);
+                mma16816(s[0], a0, a1, a2, a3, b0, b1);
+            }
+        }
+
+        // ---- scale, mask, online softmax (exp2 domain)
+        const int lim = len - p.n_q;  // keys <= lim are visible to every row
+        const bool masked = t0 + TK - 1 > lim;
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < C::NT_QK; ++n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float v = s[n][e] * p.scale_log2;
+                if (masked) {
+                    const int key = t0 + warp * C::KPW + n * 8 + lc + (e & 1);
+                    const int lmt = lim + ((e >> 1) ? rq1 : rq0);
+                    v = key <= lmt ? v : -INFINITY;
+                }
+                s[n][e] = v;
+            }
+            mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        if ((lane & 3) == 0) {
+            red_max[warp * kRows + lr] = mx0;
+            red_max[warp * kRows + lr + 8] = mx1;
+        }
+        consumer_sync();
+        float tm0 = red_max[lr], tm1 = red_max[lr + 8];
+#pragma unroll
+        for (int ww = 1; ww < kConsumerWarps; ++ww) {
+            tm0 = fmaxf(tm0, red_max[ww * kRows + lr]);
+            tm1 = fmaxf(tm1, red_max[ww * kRows + lr + 8]);
+        }
+        const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
+        const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+        const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+        const float c0 = fast_exp2(m0 - mu0), c1 = fast_exp2(m1 - mu1);
+        m0 = mn0;
+        m1 = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < C::NT_QK; ++n) {
+            const float p0 = fast_exp2(s[n][0] - mu0), p1 = fast_exp2(s[n][1] - mu0);
+            const float p2 = fast_exp2(s[n][2] - mu1), p3 = fast_exp2(s[n][3] - mu1);
+            ps0 += p0 + p1;
+            ps1 += p2 + p3;
+            const int kb = warp * C::KPW + n * 8 + lc;
+            *reinterpret_cast<uint32_t *>(sP + lr * C::TKP + kb) = pack_half2(p0, p1);
+            *reinterpret_cast<uint32_t *>(sP + (lr + 8) * C::TKP + kb) = pack_half2(p2, p3);
+        }
+        l0 = l0 * c0 + ps0;
+        l1 = l1 * c1 + ps1;
+#pragma unroll
+        for (int n = 0; n < C::NT_PV; ++n) {
+            o[n][0] *= c0;
+            o[n][1] *= c0;
+            o[n][2] *= c1;
+            o[n][3] *= c1;
+        }
+        consumer_sync();
+
+        // ---- O += P V for this warp's DPW head-dim columns
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+            uint32_t a0, a1, a2, a3;
+            {
+                const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int key = kk * 16 + (lane >> 4) * 8;
+                ldsm_x4(smem_u32(sP + row * C::TKP + key), a0, a1, a2, a3);
+            }
+            const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int jp = 0; jp < C::NT_PV / 2; ++jp) {
+                const int c16 = (warp * C::DPW) / 8 + jp * 2 + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(smem_u32(sV) + tile_off(key, c16, lbh, C::NCB), b0, b1, b2, b3);
+                mma16816(o[2 * jp], a0, a1, a2, a3, b0, b1);
+                mma16816(o[2 * jp + 1], a0, a1, a2, a3, b2, b3);
+            }
+        }
+        if (partial) fence_proxy_async();  // generic zeroing vs the next TMA write
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1;
+        }
+
+        // ---- item end: final output, or a partial for the merge
+        const bool last_of_item = (j == w.e.ntiles - 1) || (u == u_end - 1);
+        if (last_of_item) {
+            float ls0 = l0, ls1 = l1;
+            ls0 += __shfl_xor_sync(0xffffffffu, ls0, 1);
+            ls0 += __shfl_xor_sync(0xffffffffu, ls0, 2);
+            ls1 += __shfl_xor_sync(0xffffffffu, ls1, 1);
+            ls1 += __shfl_xor_sync(0xffffffffu, ls1, 2);
+            if ((lane & 3) == 0) {
+                red_sum[warp * kRows + lr] = ls0;
+                red_sum[warp * kRows + lr + 8] = ls1;
+            }
+            consumer_sync();
+            float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+            for (int ww = 0; ww < kConsumerWarps; ++ww) {
+                L0 += red_sum[ww * kRows + lr];
+                L1 += red_sum[ww * kRows + lr + 8];
+            }
+            const int item_first = w.e.unit_base + kvh * w.e.ntiles;
+            const int item_last = item_first + w.e.ntiles - 1;
+            const int col0 = warp * C::DPW + lc;
+            if (item_first >= u_begin && item_last < u_end) {
+                const float i0 = 1.f / L0, i1 = 1.f / L1;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int row = lr + half * 8;
+                    if (row < R) {
+                        const int s_ = row / G, g = row - s_ * G;
+                        float *dst = p.out + (((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * DH;
+                        const float inv = half ? i1 : i0;
+#pragma unroll
+                        for (int n = 0; n < C::NT_PV; ++n)
+                            *reinterpret_cast<float2 *>(dst + col0 + n * 8) =
+                                make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+                    }
+                }
+            } else {
+                const int item = b * KVH + kvh;
+                float *part = p.partials + (int64_t)(item + blockIdx.x) * pf;
+                if (warp == 0 && (lane & 3) == 0) {
+                    part[lr] = m0;
+                    part[lr + 8] = m1;
+                    part[16 + lr] = L0;
+                    part[16 + lr + 8] = L1;
+                }
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float *dst = part + 32 + (int64_t)(lr + half * 8) * DH;
+#pragma unroll
+                    for (int n = 0; n < C::NT_PV; ++n)
+                        *reinterpret_cast<float2 *>(dst + col0 + n * 8) =
+                            make_float2(o[n][2 * half], o[n][2 * half + 1]);
+                }
+                __threadfence();
+                consumer_sync();
+                const int c_first = cta_of_unit(item_first, U, NC);
+                const int c_last = cta_of_unit(item_last, U, NC);
+                if (tid == 0) {
+                    const int prev = atomicAdd(p.counters + item, 1);
+                    const int last = prev == c_last - c_first;
+                    if (last) {
+                        p.counters[item] = 0;  // ready for the next launch
+                        __threadfence();
+                    }
+                    *merge_flag = last;
+                }
+                consumer_sync();
+                if (*merge_flag) {
+                    const int nparts = c_last - c_first + 1;
+                    const float *base = p.partials + (int64_t)(item + c_first) * pf;
+                    for (int idx = tid; idx < R * DH; idx += 128) {
+                        const int row = idx / DH, d = idx - row * DH;
+                        float M = -INFINITY;
+                        for (int k = 0; k < nparts; ++k) M = fmaxf(M, __ldcg(base + k * pf + row));
+                        const float Mu = M == -INFINITY ? 0.f : M;
+                        float Ls = 0.f, Os = 0.f;
+                        for (int k = 0; k < nparts; ++k) {
+                            const float *pk = base + k * pf;
+                            const float wk = fast_exp2(__ldcg(pk + row) - Mu);
+                            Ls += __ldcg(pk + 16 + row) * wk;
+                            Os += __ldcg(pk + 32 + (int64_t)row * DH + d) * wk;
+                        }
+                        const int s_ = row / G, g = row - s_ * G;
+                        p.out[(((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * DH + d] = Os / Ls;
+                    }
+                }
+            }
+        }
+        w.next();
+        item_start = w.j == 0;
+    }
+}
+
+template <int DH, bool TMA>
+cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
+                            int grid, cudaStream_t s) {
+    auto kern = attend_kernel<DH, TMA>;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<DH>::SMEM_ALLOC);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    kern<<<grid, kThreads, Cfg<DH>::SMEM_ALLOC, s>>>(p, *tk, *tv);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_append(const AppendParams &p, cudaStream_t s) {
+    if (p.n_pages <= 0) return cudaSuccess;
+    append_kernel<<<p.n_pages, 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_compact(const CompactParams &p, cudaStream_t s) {
+    if (p.len <= 0) return cudaSuccess;
+    const int64_t total = 2ll * p.kvh * p.len * (p.dh / 8);
+    const int64_t blocks = (total + 255) / 256;
+    compact_kernel<<<(unsigned)(blocks < 65535 * 16 ? blocks : 65535 * 16), 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+int attend_tile_keys(int dh) {
+    switch (dh) {
+        case 64: return Cfg<64>::TK;
+        case 128: return Cfg<128>::TK;
+        case 256: return Cfg<256>::TK;
+        case 512: return Cfg<512>::TK;
+        default: return 0;
+    }
+}
+
+int attend_grid(int dh, int P, int units, int sm_count) {
+    (void)dh;
+    (void)P;
+    return units < sm_count ? units : sm_count;
+}
+
+cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
+                          int dh, int grid, cudaStream_t s) {
+    const bool tma = p.P >= 8;
+    switch (dh) {
+        case 64: return tma ? launch_attend_t<64, true>(p, tk, tv, grid, s)
+                            : launch_attend_t<64, false>(p, tk, tv, grid, s);
+        case 128: return tma ? launch_attend_t<128, true>(p, tk, tv, grid, s)
+                             : launch_attend_t<128, false>(p, tk, tv, grid, s);
+        case 256: return tma ? launch_attend_t<256, true>(p, tk, tv, grid, s)
+                             : launch_attend_t<256, false>(p, tk, tv, grid, s);
+        case 512: return tma ? launch_attend_t<512, true>(p, tk, tv, grid, s)
+                             : launch_attend_t<512, false>(p, tk, tv, grid, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace gkv

@@ -1,0 +1,100 @@
+// gkv_kernels.cuh -- launch parameters shared by the host pool
+// (gkv_pool.cpp) and the sm_100a kernels (gkv_kernels.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gkv {
+
+// Device status word bits (pool->d_status), read by gkv_device_status().
+enum : int {
+    DEV_ERR_WAIT_TIMEOUT = 1,  // an mbarrier wait ran out of its time limit
+    DEV_ERR_BAD_PAGE = 2,      // a block-table entry outside [0, num_pages)
+};
+
+// ---------------------------------------------------------------- append
+// One batch entry of an append / seed.
+struct AppendEntry {
+    int32_t seq_id;
+    int32_t len_before;  // positions already in the sequence
+    int32_t n_new;       // rows appended
+    int32_t src_row0;    // first source row of this entry
+};
+
+// One page the append touches.  src_pid:
+//   PAGE_EXISTING -> write only the appended rows
+//   PAGE_NEW      -> zero-fill the page, then the appended rows, set table
+//   >= 0          -> copy page src_pid (copy-on-write / clone tail), then the
+//                    appended rows, set table
+struct TouchedPage {
+    int32_t entry;
+    int32_t pidx;  // logical page index in the sequence
+    int32_t pid;   // physical page
+    int32_t src_pid;
+};
+constexpr int32_t PAGE_EXISTING = -1;
+constexpr int32_t PAGE_NEW = -2;
+
+struct AppendParams {
+    const AppendEntry *entries;
+    const TouchedPage *pages;
+    int32_t n_pages;
+    const uint16_t *k_src;  // token-major [rows, KVH, dh] or head-major [KVH, rows, dh]
+    const uint16_t *v_src;
+    int32_t head_major;     // 1: seed layout [KVH, n_new, dh]
+    uint16_t *k_pool;       // [num_pages, KVH, P, dh]
+    uint16_t *v_pool;
+    int32_t *table;         // [max_seqs, table_stride]
+    int32_t table_stride;
+    int32_t kvh, dh, P;
+};
+
+// ---------------------------------------------------------------- attend
+struct AttendEntry {
+    int32_t seq_id;
+    int32_t len;        // keys in the sequence (query rows are the last n_q)
+    int32_t unit_base;  // first work unit of this sequence (kvh-major inside)
+    int32_t ntiles;     // key tiles per kv head = ceil(len / TK)
+};
+
+struct AttendParams {
+    const AttendEntry *entries;
+    int32_t n_seqs;
+    int32_t total_units;
+    const int32_t *table;
+    int32_t table_stride;
+    const uint16_t *k_pool;  // used by the cp.async loader (P < 8)
+    const uint16_t *v_pool;
+    const uint16_t *q;       // [n_seqs, n_q, KVH*G, dh]
+    float *out;              // [n_seqs, n_q, KVH*G, dh]
+    float *partials;         // [n_items + grid, 32 + 16*dh]
+    int32_t *counters;       // [n_items], zero between launches
+    int32_t *status;         // device status word
+    int32_t n_q, G, kvh, P, num_pages;
+    float scale_log2;        // scale * log2(e)
+};
+
+// Host-side launchers (gkv_kernels.cu).
+cudaError_t launch_append(const AppendParams &p, cudaStream_t s);
+// Number of CTAs the attend launch will use for `units` work units.
+int attend_grid(int dh, int P, int units, int sm_count);
+// Floats of partial-result scratch per slot.
+__host__ __device__ inline int64_t attend_partial_floats(int dh) { return 32 + 16 * (int64_t)dh; }
+cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tmap_k,
+                          const CUtensorMap *tmap_v, int dh, int grid,
+                          cudaStream_t s);
+// Key tile length used by the attend kernel for head_dim dh.
+int attend_tile_keys(int dh);
+
+struct CompactParams {
+    const int32_t *table;  // row of the sequence
+    const uint16_t *k_pool, *v_pool;
+    uint16_t *K, *V;       // [KVH, len, dh]
+    int64_t len;
+    int32_t kvh, dh, P;
+};
+cudaError_t launch_compact(const CompactParams &p, cudaStream_t s);
+
+}  // namespace gkv

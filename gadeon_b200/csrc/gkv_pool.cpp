@@ -1,0 +1,770 @@
+// gkv_pool.cpp -- host side of libgadeonkv.so: the C ABI of include/gadeon_kv.h.
+//
+// The host owns the allocation decisions (free list, reference counts,
+// lengths, block tables); the device owns the page bytes and a copy of the
+// block tables that the kernels read.  Every mutating call validates the
+// whole batch first, then updates the host state and enqueues the matching
+// device work in stream order through a small descriptor upload.
+//
+// Allocation policy (the reference has no free list -- PagePool pages are
+// ARC objects, LLM/src/CoreML/PagedAttention.swift:25-26 -- so this is the
+// one explicit model, mirrored bit-for-bit by the CPU oracle):
+//   * initial pop order = splitmix64 Fisher-Yates permutation of the page ids;
+//   * pops happen in batch order, per sequence: copy-on-write of a shared
+//     tail page first, then one fresh page per page boundary crossed;
+//   * fresh pages are zero-filled (PagePool.zeroPage, :278-286);
+//   * truncate drops table entries last-first (:185-188) and pushes a page
+//     back when its reference count reaches zero (LIFO: next pop reuses it).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "gadeon_kv.h"
+#include "gkv_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(GKV_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define GKV_CUDA(call, what)                          \
+    do {                                              \
+        cudaError_t e_ = (call);                      \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+uint64_t splitmix64(uint64_t *s) {
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Pinned host slots + matching device slots for per-call descriptors.  A
+// slot is reused only after the event recorded behind its last use fired.
+struct Staging {
+    static constexpr int kSlots = 64;
+    size_t slot_bytes = 0;
+    uint8_t *h = nullptr;
+    uint8_t *d = nullptr;
+    cudaEvent_t ev[kSlots] = {};
+    bool used[kSlots] = {};
+    int next = 0;
+
+    void release() {
+        for (int i = 0; i < kSlots; ++i)
+            if (ev[i]) {
+                cudaEventSynchronize(ev[i]);
+                cudaEventDestroy(ev[i]);
+                ev[i] = nullptr;
+            }
+        if (h) cudaFreeHost(h);
+        if (d) cudaFree(d);
+        h = d = nullptr;
+        slot_bytes = 0;
+    }
+
+    // Returns the slot index, or -1 with the CUDA error in *err.
+    int acquire(size_t bytes, cudaError_t *err) {
+        *err = cudaSuccess;
+        if (bytes > slot_bytes) {
+            release();
+            size_t sb = 64 * 1024;
+            while (sb < bytes) sb *= 2;
+            if ((*err = cudaMallocHost(&h, sb * kSlots)) != cudaSuccess) return -1;
+            if ((*err = cudaMalloc(&d, sb * kSlots)) != cudaSuccess) return -1;
+            for (int i = 0; i < kSlots; ++i) {
+                if ((*err = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming)) != cudaSuccess)
+                    return -1;
+                used[i] = false;
+            }
+            slot_bytes = sb;
+        }
+        const int s = next;
+        next = (next + 1) % kSlots;
+        if (used[s] && (*err = cudaEventSynchronize(ev[s])) != cudaSuccess) return -1;
+        return s;
+    }
+    uint8_t *host(int s) { return h + (size_t)s * slot_bytes; }
+    uint8_t *dev(int s) { return d + (size_t)s * slot_bytes; }
+    cudaError_t upload(int s, size_t bytes, cudaStream_t st) {
+        return cudaMemcpyAsync(dev(s), host(s), bytes, cudaMemcpyHostToDevice, st);
+    }
+    cudaError_t done(int s, cudaStream_t st) {
+        used[s] = true;
+        return cudaEventRecord(ev[s], st);
+    }
+};
+
+struct Seq {
+    bool active = false;
+    int64_t len = 0;
+    std::vector<int32_t> pages;
+};
+
+}  // namespace
+
+struct gkv_pool {
+    gkv_pool_config cfg{};
+    int sm_count = 0;
+    int tile_keys = 0;
+    size_t page_elems = 0;  // KVH * P * dh halves
+    uint16_t *d_k = nullptr, *d_v = nullptr;
+    int32_t *d_table = nullptr;
+    int32_t *d_status = nullptr;
+    float *d_partials = nullptr;
+    int32_t *d_counters = nullptr;
+    CUtensorMap tmk{}, tmv{};
+    std::vector<int32_t> stack;  // free list; back() is the head
+    std::vector<int32_t> ref;
+    std::vector<Seq> seqs;
+    Staging staging;
+
+    Seq *seq(int32_t id) {
+        if (id < 0 || id >= (int32_t)seqs.size() || !seqs[id].active) return nullptr;
+        return &seqs[id];
+    }
+    const Seq *seq(int32_t id) const {
+        if (id < 0 || id >= (int32_t)seqs.size() || !seqs[id].active) return nullptr;
+        return &seqs[id];
+    }
+    int32_t pop() {
+        const int32_t pid = stack.back();
+        stack.pop_back();
+        ref[pid] = 1;
+        return pid;
+    }
+    void unref(int32_t pid) {
+        if (--ref[pid] == 0) stack.push_back(pid);
+    }
+    int64_t pages_for(int64_t len) const { return (len + cfg.page_tokens - 1) / cfg.page_tokens; }
+    // Pages an append of n rows onto s pops (shared-tail copy + new pages).
+    int64_t pages_needed(const Seq &s, int64_t n) const {
+        if (n <= 0) return 0;
+        const int64_t P = cfg.page_tokens;
+        const int64_t cow = (s.len % P != 0 && ref[s.pages.back()] > 1) ? 1 : 0;
+        return cow + pages_for(s.len + n) - (int64_t)s.pages.size();
+    }
+    int32_t new_seq_id() {
+        for (size_t i = 0; i < seqs.size(); ++i)
+            if (!seqs[i].active) return (int32_t)i;
+        if ((int32_t)seqs.size() >= cfg.max_seqs) return -1;
+        seqs.emplace_back();
+        return (int32_t)seqs.size() - 1;
+    }
+};
+
+namespace {
+
+int check_batch(const gkv_pool *pool, int32_t n, const int32_t *ids) {
+    if (n < 0 || (n > 0 && !ids)) return fail(GKV_ERR_INVALID, "bad batch (n=%d)", n);
+    std::vector<char> seen(pool->seqs.size(), 0);
+    for (int32_t i = 0; i < n; ++i) {
+        if (!pool->seq(ids[i])) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", ids[i]);
+        if (seen[ids[i]]++) return fail(GKV_ERR_INVALID, "sequence %d twice in one batch", ids[i]);
+    }
+    return GKV_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Host half of an append/seed: validates, mutates the bookkeeping, and fills
+// the descriptor (entries + touched pages).  Nothing is mutated on failure.
+int plan_append(gkv_pool *pool, int32_t n, const int32_t *ids, const int32_t *n_new,
+                std::vector<gkv::AppendEntry> &entries, std::vector<gkv::TouchedPage> &pages) {
+    const int64_t P = pool->cfg.page_tokens;
+    int64_t need = 0;
+    for (int32_t i = 0; i < n; ++i) {
+        if (n_new[i] < 0) return fail(GKV_ERR_INVALID, "n_new[%d] = %d", i, n_new[i]);
+        const Seq &s = *pool->seq(ids[i]);
+        if (pool->pages_for(s.len + n_new[i]) > pool->cfg.max_pages_per_seq)
+            return fail(GKV_ERR_CAPACITY, "sequence %d would exceed %d pages", ids[i],
+                        pool->cfg.max_pages_per_seq);
+        if (s.len + n_new[i] > INT32_MAX)
+            return fail(GKV_ERR_CAPACITY, "sequence %d length overflow", ids[i]);
+        need += pool->pages_needed(s, n_new[i]);
+    }
+    if (need > (int64_t)pool->stack.size())
+        return fail(GKV_ERR_NO_PAGES, "append needs %lld pages, %zu free", (long long)need,
+                    pool->stack.size());
+    int32_t row0 = 0;
+    entries.clear();
+    pages.clear();
+    for (int32_t i = 0; i < n; ++i) {
+        Seq &s = *pool->seq(ids[i]);
+        entries.push_back({ids[i], (int32_t)s.len, n_new[i], row0});
+        row0 += n_new[i];
+        if (n_new[i] == 0) continue;
+        if (s.len % P != 0) {
+            const int32_t tail = s.pages.back();
+            const int32_t pidx = (int32_t)s.pages.size() - 1;
+            if (pool->ref[tail] > 1) {  // copy-on-write of a shared tail
+                const int32_t pid = pool->pop();
+                pool->ref[tail]--;
+                s.pages.back() = pid;
+                pages.push_back({i, pidx, pid, tail});
+            } else {
+                pages.push_back({i, pidx, tail, gkv::PAGE_EXISTING});
+            }
+        }
+        const int64_t want = pool->pages_for(s.len + n_new[i]);
+        while ((int64_t)s.pages.size() < want) {
+            const int32_t pid = pool->pop();
+            pages.push_back({i, (int32_t)s.pages.size(), pid, gkv::PAGE_NEW});
+            s.pages.push_back(pid);
+        }
+        s.len += n_new[i];
+    }
+    return GKV_OK;
+}
+
+// Uploads entries+pages and launches the append kernel.
+int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
+                   const std::vector<gkv::TouchedPage> &pages, const void *k, const void *v,
+                   int head_major, cudaStream_t st) {
+    if (pages.empty()) return GKV_OK;
+    const size_t eb = entries.size() * sizeof(gkv::AppendEntry);
+    const size_t pb = pages.size() * sizeof(gkv::TouchedPage);
+    cudaError_t err;
+    const int slot = pool->staging.acquire(eb + pb, &err);
+    if (slot < 0) return cuda_fail(err, "descriptor staging");
+    memcpy(pool->staging.host(slot), entries.data(), eb);
+    memcpy(pool->staging.host(slot) + eb, pages.data(), pb);
+    GKV_CUDA(pool->staging.upload(slot, eb + pb, st), "descriptor upload");
+    gkv::AppendParams p{};
+    p.entries = reinterpret_cast<const gkv::AppendEntry *>(pool->staging.dev(slot));
+    p.pages = reinterpret_cast<const gkv::TouchedPage *>(pool->staging.dev(slot) + eb);
+    p.n_pages = (int32_t)pages.size();
+    p.k_src = static_cast<const uint16_t *>(k);
+    p.v_src = static_cast<const uint16_t *>(v);
+    p.head_major = head_major;
+    p.k_pool = pool->d_k;
+    p.v_pool = pool->d_v;
+    p.table = pool->d_table;
+    p.table_stride = pool->cfg.max_pages_per_seq;
+    p.kvh = pool->cfg.kv_heads;
+    p.dh = pool->cfg.head_dim;
+    p.P = pool->cfg.page_tokens;
+    GKV_CUDA(gkv::launch_append(p, st), "append kernel launch");
+    GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
+    return GKV_OK;
+}
+
+// Validation shared by gkv_attend / gkv_append_attend (after the append).
+int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
+                 const void *q, const float *out) {
+    if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
+    if ((int64_t)n_q * group > 16)
+        return fail(GKV_ERR_UNSUPPORTED, "n_q*group = %d query rows per kv head (max 16)",
+                    n_q * group);
+    if (n > 0 && (!q || !out)) return fail(GKV_ERR_INVALID, "null q/out");
+    if (!aligned16(q) || !aligned16(out)) return fail(GKV_ERR_INVALID, "q/out not 16-byte aligned");
+    for (int32_t i = 0; i < n; ++i)
+        if (pool->seq(ids[i])->len < n_q)
+            return fail(GKV_ERR_BAD_SEQ, "sequence %d has %lld < n_q=%d positions", ids[i],
+                        (long long)pool->seq(ids[i])->len, n_q);
+    return GKV_OK;
+}
+
+int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
+                   const void *q, float *out, float scale, cudaStream_t st) {
+    if (n == 0) return GKV_OK;
+    const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
+    cudaError_t err;
+    const size_t bytes = (size_t)n * sizeof(gkv::AttendEntry);
+    const int slot = pool->staging.acquire(bytes, &err);
+    if (slot < 0) return cuda_fail(err, "descriptor staging");
+    auto *ent = reinterpret_cast<gkv::AttendEntry *>(pool->staging.host(slot));
+    int64_t units = 0;
+    for (int32_t i = 0; i < n; ++i) {
+        const Seq &s = *pool->seq(ids[i]);
+        const int32_t ntiles = (int32_t)((s.len + TK - 1) / TK);
+        ent[i] = {ids[i], (int32_t)s.len, (int32_t)units, ntiles};
+        units += (int64_t)KVH * ntiles;
+    }
+    if (units > INT32_MAX) return fail(GKV_ERR_CAPACITY, "too many key tiles in one call");
+    GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
+    gkv::AttendParams p{};
+    p.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
+    p.n_seqs = n;
+    p.total_units = (int32_t)units;
+    p.table = pool->d_table;
+    p.table_stride = pool->cfg.max_pages_per_seq;
+    p.k_pool = pool->d_k;
+    p.v_pool = pool->d_v;
+    p.q = static_cast<const uint16_t *>(q);
+    p.out = out;
+    p.partials = pool->d_partials;
+    p.counters = pool->d_counters;
+    p.status = pool->d_status;
+    p.n_q = n_q;
+    p.G = group;
+    p.kvh = KVH;
+    p.P = pool->cfg.page_tokens;
+    p.num_pages = pool->cfg.num_pages;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    const int grid = gkv::attend_grid(pool->cfg.head_dim, p.P, (int)units, pool->sm_count);
+    GKV_CUDA(gkv::launch_attend(p, &pool->tmk, &pool->tmv, pool->cfg.head_dim, grid, st),
+             "attend kernel launch");
+    GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
+    return GKV_OK;
+}
+
+void free_device(gkv_pool *p) {
+    p->staging.release();
+    cudaFree(p->d_k);
+    cudaFree(p->d_v);
+    cudaFree(p->d_table);
+    cudaFree(p->d_status);
+    cudaFree(p->d_partials);
+    cudaFree(p->d_counters);
+    p->d_k = p->d_v = nullptr;
+    p->d_table = p->d_status = p->d_counters = nullptr;
+    p->d_partials = nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *gkv_last_error(void) { return g_last_error.c_str(); }
+
+const char *gkv_version(void) { return "gadeon-kv-b200 0.1 (sm_100a)"; }
+
+int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out) {
+    if (!cfg || !out) return fail(GKV_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const gkv_pool_config c = *cfg;
+    if (c.kv_heads < 1 || c.kv_heads > 64) return fail(GKV_ERR_INVALID, "kv_heads=%d", c.kv_heads);
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256 && c.head_dim != 512)
+        return fail(GKV_ERR_UNSUPPORTED, "head_dim=%d (64/128/256/512)", c.head_dim);
+    if (!is_pow2(c.page_tokens) || c.page_tokens > 16384)
+        return fail(GKV_ERR_INVALID, "page_tokens=%d (power of two <= 16384)", c.page_tokens);
+    if (c.num_pages < 1 || c.max_seqs < 1 || c.max_pages_per_seq < 1)
+        return fail(GKV_ERR_INVALID, "num_pages/max_seqs/max_pages_per_seq must be >= 1");
+    if ((int64_t)c.num_pages * c.kv_heads * c.page_tokens >= INT32_MAX)
+        return fail(GKV_ERR_CAPACITY, "num_pages*kv_heads*page_tokens rows exceed 2^31");
+    if ((int64_t)c.max_pages_per_seq * c.page_tokens > INT32_MAX)
+        return fail(GKV_ERR_CAPACITY, "max context exceeds 2^31 positions");
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(GKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver)");
+    int ndev = 0;
+    GKV_CUDA(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+    if (c.device < 0 || c.device >= ndev) return fail(GKV_ERR_INVALID, "device %d", c.device);
+    DeviceGuard guard(c.device);
+    cudaDeviceProp prop;
+    GKV_CUDA(cudaGetDeviceProperties(&prop, c.device), "cudaGetDeviceProperties");
+    if (prop.major < 10)
+        return fail(GKV_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a",
+                    c.device, prop.major, prop.minor);
+
+    gkv_pool *p = new gkv_pool();
+    p->cfg = c;
+    p->sm_count = prop.multiProcessorCount;
+    p->tile_keys = gkv::attend_tile_keys(c.head_dim);
+    p->page_elems = (size_t)c.kv_heads * c.page_tokens * c.head_dim;
+    const size_t page_bytes = p->page_elems * 2;
+    const size_t items = (size_t)c.max_seqs * c.kv_heads;
+    cudaError_t e;
+#define GKV_ALLOC(ptr, bytes)                                       \
+    if ((e = cudaMalloc(&(ptr), (bytes))) != cudaSuccess) {         \
+        free_device(p);                                             \
+        delete p;                                                   \
+        return cuda_fail(e, "cudaMalloc " #ptr);                    \
+    }
+    GKV_ALLOC(p->d_k, page_bytes * c.num_pages);
+    GKV_ALLOC(p->d_v, page_bytes * c.num_pages);
+    GKV_ALLOC(p->d_table, sizeof(int32_t) * (size_t)c.max_seqs * c.max_pages_per_seq);
+    GKV_ALLOC(p->d_status, sizeof(int32_t));
+    GKV_ALLOC(p->d_partials,
+              sizeof(float) * (items + p->sm_count) * gkv::attend_partial_floats(c.head_dim));
+    GKV_ALLOC(p->d_counters, sizeof(int32_t) * items);
+#undef GKV_ALLOC
+    if ((e = cudaMemset(p->d_table, 0xff, sizeof(int32_t) * (size_t)c.max_seqs *
+                                              c.max_pages_per_seq)) != cudaSuccess ||
+        (e = cudaMemset(p->d_status, 0, sizeof(int32_t))) != cudaSuccess ||
+        (e = cudaMemset(p->d_counters, 0, sizeof(int32_t) * items)) != cudaSuccess ||
+        (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        free_device(p);
+        delete p;
+        return cuda_fail(e, "pool initialisation");
+    }
+    // TMA views of the pools: rows of head_dim halves, one row per
+    // (page, kv head, slot); boxes of 64 columns x BH rows, 128B swizzle.
+    const int bh = std::min(c.page_tokens, p->tile_keys);
+    if (c.page_tokens >= 8) {
+        const cuuint64_t dims[2] = {(cuuint64_t)c.head_dim,
+                                    (cuuint64_t)c.num_pages * c.kv_heads * c.page_tokens};
+        const cuuint64_t strides[1] = {(cuuint64_t)c.head_dim * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)bh};
+        const cuuint32_t estr[2] = {1, 1};
+        for (int t = 0; t < 2; ++t) {
+            CUresult r = enc(t == 0 ? &p->tmk : &p->tmv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                             t == 0 ? (void *)p->d_k : (void *)p->d_v, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) {
+                free_device(p);
+                delete p;
+                return fail(GKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+            }
+        }
+    }
+    // Free list: pops yield the seeded permutation in order.
+    std::vector<int32_t> perm(c.num_pages);
+    for (int32_t i = 0; i < c.num_pages; ++i) perm[i] = i;
+    uint64_t st = c.seed;
+    for (int32_t i = c.num_pages - 1; i > 0; --i) {
+        const int32_t j = (int32_t)(splitmix64(&st) % (uint64_t)(i + 1));
+        std::swap(perm[i], perm[j]);
+    }
+    p->stack.assign(perm.rbegin(), perm.rend());
+    p->ref.assign(c.num_pages, 0);
+    *out = p;
+    return GKV_OK;
+}
+
+int gkv_pool_destroy(gkv_pool *pool) {
+    if (!pool) return GKV_OK;
+    {
+        DeviceGuard guard(pool->cfg.device);
+        cudaDeviceSynchronize();
+        free_device(pool);
+    }
+    delete pool;
+    return GKV_OK;
+}
+
+int gkv_seq_create(gkv_pool *pool, int32_t *seq_id) {
+    if (!pool || !seq_id) return fail(GKV_ERR_INVALID, "null argument");
+    const int32_t id = pool->new_seq_id();
+    if (id < 0) return fail(GKV_ERR_CAPACITY, "max_seqs=%d reached", pool->cfg.max_seqs);
+    pool->seqs[id] = Seq();
+    pool->seqs[id].active = true;
+    *seq_id = id;
+    return GKV_OK;
+}
+
+int gkv_seq_release(gkv_pool *pool, int32_t seq_id) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    while (!s->pages.empty()) {
+        pool->unref(s->pages.back());
+        s->pages.pop_back();
+    }
+    s->len = 0;
+    s->active = false;
+    return GKV_OK;
+}
+
+int gkv_seq_length(const gkv_pool *pool, int32_t seq_id, int64_t *length) {
+    if (!pool || !length) return fail(GKV_ERR_INVALID, "null argument");
+    const Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    *length = s->len;
+    return GKV_OK;
+}
+
+int gkv_seq_page_count(const gkv_pool *pool, int32_t seq_id, int32_t *pages) {
+    if (!pool || !pages) return fail(GKV_ERR_INVALID, "null argument");
+    const Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    *pages = (int32_t)s->pages.size();
+    return GKV_OK;
+}
+
+int gkv_free_page_count(const gkv_pool *pool, int32_t *pages) {
+    if (!pool || !pages) return fail(GKV_ERR_INVALID, "null argument");
+    *pages = (int32_t)pool->stack.size();
+    return GKV_OK;
+}
+
+int gkv_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int32_t *n_new,
+               const void *k, const void *v, void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    if (n_seqs > 0 && !n_new) return fail(GKV_ERR_INVALID, "null n_new");
+    int64_t rows = 0;
+    for (int32_t i = 0; i < n_seqs; ++i) rows += std::max(n_new[i], 0);
+    if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
+    if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
+    DeviceGuard guard(pool->cfg.device);
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    rc = plan_append(pool, n_seqs, seq_ids, n_new, entries, pages);
+    if (rc) return rc;
+    return enqueue_append(pool, entries, pages, k, v, 0, static_cast<cudaStream_t>(stream));
+}
+
+int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64_t count,
+             void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    if (s->len != 0) return fail(GKV_ERR_BAD_SEQ, "seed needs an empty sequence (%d has %lld)",
+                                 seq_id, (long long)s->len);
+    if (count < 0 || count > INT32_MAX) return fail(GKV_ERR_INVALID, "count=%lld", (long long)count);
+    if (count > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    DeviceGuard guard(pool->cfg.device);
+    const int32_t n = (int32_t)count;
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    int rc = plan_append(pool, 1, &seq_id, &n, entries, pages);
+    if (rc) return rc;
+    return enqueue_append(pool, entries, pages, K, V, 1, static_cast<cudaStream_t>(stream));
+}
+
+int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q,
+               int32_t group, const void *q, float *out, float scale, void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    rc = check_attend(pool, n_seqs, seq_ids, n_q, group, q, out);
+    if (rc) return rc;
+    DeviceGuard guard(pool->cfg.device);
+    return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q,
+                      int32_t group, const void *k, const void *v, const void *q, float *out,
+                      float scale, void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    if (n_q < 1 || group < 1 || (int64_t)n_q * group > 16)
+        return fail(n_q < 1 || group < 1 ? GKV_ERR_INVALID : GKV_ERR_UNSUPPORTED,
+                    "n_q=%d group=%d (n_q*group <= 16)", n_q, group);
+    if (n_seqs > 0 && (!k || !v || !q || !out)) return fail(GKV_ERR_INVALID, "null k/v/q/out");
+    if (!aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(out))
+        return fail(GKV_ERR_INVALID, "k/v/q/out not 16-byte aligned");
+    DeviceGuard guard(pool->cfg.device);
+    std::vector<int32_t> n_new(n_seqs, n_q);
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
+    if (rc) return rc;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = enqueue_append(pool, entries, pages, k, v, 0, st);
+    if (rc) return rc;
+    return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st);
+}
+
+int gkv_truncate(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int64_t *new_len) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    if (n_seqs > 0 && !new_len) return fail(GKV_ERR_INVALID, "null new_len");
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        const Seq &s = *pool->seq(seq_ids[i]);
+        if (new_len[i] < 0 || new_len[i] > s.len)
+            return fail(GKV_ERR_BAD_SEQ, "truncate sequence %d to %lld (length %lld)", seq_ids[i],
+                        (long long)new_len[i], (long long)s.len);
+    }
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        Seq &s = *pool->seq(seq_ids[i]);
+        s.len = new_len[i];
+        const int64_t need = pool->pages_for(s.len);
+        while ((int64_t)s.pages.size() > need) {
+            pool->unref(s.pages.back());
+            s.pages.pop_back();
+        }
+    }
+    return GKV_OK;
+}
+
+int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream) {
+    if (!pool || !dst) return fail(GKV_ERR_INVALID, "null argument");
+    if (!pool->seq(src)) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", src);
+    const bool partial = pool->seq(src)->len % pool->cfg.page_tokens != 0;
+    if (partial && pool->stack.empty()) return fail(GKV_ERR_NO_PAGES, "clone needs 1 free page");
+    const int32_t id = pool->new_seq_id();
+    if (id < 0) return fail(GKV_ERR_CAPACITY, "max_seqs=%d reached", pool->cfg.max_seqs);
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const Seq &s = *pool->seq(src);
+    Seq c;
+    c.active = true;
+    c.len = s.len;
+    c.pages = s.pages;
+    const size_t stride = pool->cfg.max_pages_per_seq;
+    if (!c.pages.empty()) {
+        cudaError_t e = cudaMemcpyAsync(pool->d_table + id * stride, pool->d_table + src * stride,
+                                        sizeof(int32_t) * c.pages.size(),
+                                        cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "clone table copy");
+    }
+    for (int32_t pid : c.pages) pool->ref[pid]++;
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    if (partial) {
+        const int32_t old = c.pages.back();
+        const int32_t pid = pool->pop();
+        pool->ref[old]--;
+        c.pages.back() = pid;
+        entries.push_back({id, (int32_t)c.len, 0, 0});
+        pages.push_back({0, (int32_t)c.pages.size() - 1, pid, old});
+    }
+    pool->seqs[id] = std::move(c);
+    *dst = id;
+    return enqueue_append(pool, entries, pages, nullptr, nullptr, 0, st);
+}
+
+int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    const Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    if (s->len > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    DeviceGuard guard(pool->cfg.device);
+    gkv::CompactParams p{};
+    p.table = pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq;
+    p.k_pool = pool->d_k;
+    p.v_pool = pool->d_v;
+    p.K = static_cast<uint16_t *>(K);
+    p.V = static_cast<uint16_t *>(V);
+    p.len = s->len;
+    p.kvh = pool->cfg.kv_heads;
+    p.dh = pool->cfg.head_dim;
+    p.P = pool->cfg.page_tokens;
+    GKV_CUDA(gkv::launch_compact(p, static_cast<cudaStream_t>(stream)), "compact kernel launch");
+    return GKV_OK;
+}
+
+int gkv_from_compact(gkv_pool *pool, const void *K, const void *V, int64_t length,
+                     int32_t *seq_id, void *stream) {
+    if (!pool || !seq_id) return fail(GKV_ERR_INVALID, "null argument");
+    if (length < 0) return fail(GKV_ERR_INVALID, "length=%lld", (long long)length);
+    if (pool->pages_for(length) > (int64_t)pool->stack.size())
+        return fail(GKV_ERR_NO_PAGES, "fromCompact needs %lld pages",
+                    (long long)pool->pages_for(length));
+    int32_t id;
+    int rc = gkv_seq_create(pool, &id);
+    if (rc) return rc;
+    rc = gkv_seed(pool, id, K, V, length, stream);
+    if (rc) {
+        gkv_seq_release(pool, id);
+        return rc;
+    }
+    *seq_id = id;
+    return GKV_OK;
+}
+
+int gkv_export_table(gkv_pool *pool, int32_t seq_id, int32_t *pages_out, int32_t cap,
+                     int32_t *n_pages) {
+    if (!pool || !n_pages) return fail(GKV_ERR_INVALID, "null argument");
+    const Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    const int32_t n = (int32_t)s->pages.size();
+    *n_pages = n;
+    if (!pages_out || n == 0) return GKV_OK;
+    if (cap < n) return fail(GKV_ERR_INVALID, "cap %d < %d pages", cap, n);
+    DeviceGuard guard(pool->cfg.device);
+    GKV_CUDA(cudaDeviceSynchronize(), "synchronize");
+    GKV_CUDA(cudaMemcpy(pages_out, pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq,
+                        sizeof(int32_t) * n, cudaMemcpyDeviceToHost),
+             "table copy");
+    return GKV_OK;
+}
+
+int gkv_export_free_list(const gkv_pool *pool, int32_t *out, int32_t cap, int32_t *n) {
+    if (!pool || !n) return fail(GKV_ERR_INVALID, "null argument");
+    const int32_t m = (int32_t)pool->stack.size();
+    *n = m;
+    if (!out) return GKV_OK;
+    if (cap < m) return fail(GKV_ERR_INVALID, "cap %d < %d free pages", cap, m);
+    for (int32_t i = 0; i < m; ++i) out[i] = pool->stack[m - 1 - i];
+    return GKV_OK;
+}
+
+int gkv_page_refcount(const gkv_pool *pool, int32_t page_id, int32_t *ref) {
+    if (!pool || !ref) return fail(GKV_ERR_INVALID, "null argument");
+    if (page_id < 0 || page_id >= pool->cfg.num_pages)
+        return fail(GKV_ERR_INVALID, "page %d", page_id);
+    *ref = pool->ref[page_id];
+    return GKV_OK;
+}
+
+int gkv_export_page(gkv_pool *pool, int32_t page_id, void *k_host, void *v_host) {
+    if (!pool || !k_host || !v_host) return fail(GKV_ERR_INVALID, "null argument");
+    if (page_id < 0 || page_id >= pool->cfg.num_pages)
+        return fail(GKV_ERR_INVALID, "page %d", page_id);
+    DeviceGuard guard(pool->cfg.device);
+    const size_t bytes = pool->page_elems * 2;
+    GKV_CUDA(cudaDeviceSynchronize(), "synchronize");
+    GKV_CUDA(cudaMemcpy(k_host, pool->d_k + page_id * pool->page_elems, bytes,
+                        cudaMemcpyDeviceToHost),
+             "page copy");
+    GKV_CUDA(cudaMemcpy(v_host, pool->d_v + page_id * pool->page_elems, bytes,
+                        cudaMemcpyDeviceToHost),
+             "page copy");
+    return GKV_OK;
+}
+
+int gkv_device_status(gkv_pool *pool, int32_t *status) {
+    if (!pool || !status) return fail(GKV_ERR_INVALID, "null argument");
+    DeviceGuard guard(pool->cfg.device);
+    GKV_CUDA(cudaDeviceSynchronize(), "synchronize");
+    GKV_CUDA(cudaMemcpy(status, pool->d_status, sizeof(int32_t), cudaMemcpyDeviceToHost),
+             "status copy");
+    return GKV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,374 @@
+"""Python binding of libgadeonkv.so (include/gadeon_kv.h) over ctypes.
+
+Two layers:
+
+* :class:`BlockPool` -- one attention layer's physical page pool on one GPU
+  (``gkv_pool``): batched append / attend / truncate / clone / compact over
+  many sequences at once, the shape a batching server drives.
+* :class:`PagePool` -- the reference's per-sequence cache object
+  (leok7v/gadeon ``PagePool``, LLM/src/CoreML/PagedAttention.swift:21-287):
+  ``append(k, v)``, ``seed``, ``truncate(to)``, ``clone()``, ``compact()``,
+  ``from_compact``, ``length``, ``page_count``; and :func:`host_flash_decode`,
+  the drop-in for ``hostFlashDecode(q:pool:G:)`` (:317-366).
+
+Device tensors are torch CUDA tensors (torch is the device-memory and stream
+plumbing); fp16 data is passed as ``torch.float16`` or as raw ``int16``/
+``uint16`` bit patterns.  Failures raise :class:`GkvError`, the counterpart of
+the reference's ``throws`` (allocation) and ``precondition`` (shape) paths.
+There is no CPU fallback: without the built library or a GPU every call
+fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+from typing import Iterable, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgadeonkv.so")
+
+GKV_OK = 0
+GKV_ERR_INVALID = 1
+GKV_ERR_NO_PAGES = 2
+GKV_ERR_CUDA = 3
+GKV_ERR_BAD_SEQ = 4
+GKV_ERR_UNSUPPORTED = 5
+GKV_ERR_CAPACITY = 6
+
+# Every entry point include/gadeon_kv.h declares.
+EXPORTED = (
+    "gkv_last_error", "gkv_version", "gkv_pool_create", "gkv_pool_destroy", "gkv_seq_create",
+    "gkv_seq_release", "gkv_seq_length", "gkv_seq_page_count", "gkv_free_page_count",
+    "gkv_append", "gkv_seed", "gkv_attend", "gkv_append_attend", "gkv_truncate",
+    "gkv_clone_seq", "gkv_compact_seq", "gkv_from_compact", "gkv_export_table",
+    "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
+)
+
+
+class GkvError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"gkv error {code}: {message}")
+        self.code = code
+
+
+class _PoolConfig(C.Structure):
+    _fields_ = [
+        ("device", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
+        ("page_tokens", C.c_int32), ("num_pages", C.c_int32), ("max_seqs", C.c_int32),
+        ("max_pages_per_seq", C.c_int32), ("seed", C.c_uint64),
+    ]
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Load libgadeonkv.so and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is not built: run `python -m gadeon_b200.build`")
+    L = C.CDLL(path)
+    P = C.c_void_p
+    i32, i64, f32 = C.c_int32, C.c_int64, C.c_float
+    i32p, i64p = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
+    sig = {
+        "gkv_last_error": (C.c_char_p, []),
+        "gkv_version": (C.c_char_p, []),
+        "gkv_pool_create": (C.c_int, [C.POINTER(_PoolConfig), C.POINTER(P)]),
+        "gkv_pool_destroy": (C.c_int, [P]),
+        "gkv_seq_create": (C.c_int, [P, i32p]),
+        "gkv_seq_release": (C.c_int, [P, i32]),
+        "gkv_seq_length": (C.c_int, [P, i32, i64p]),
+        "gkv_seq_page_count": (C.c_int, [P, i32, i32p]),
+        "gkv_free_page_count": (C.c_int, [P, i32p]),
+        "gkv_append": (C.c_int, [P, i32, i32p, i32p, P, P, P]),
+        "gkv_seed": (C.c_int, [P, i32, P, P, i64, P]),
+        "gkv_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, P]),
+        "gkv_append_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, P]),
+        "gkv_truncate": (C.c_int, [P, i32, i32p, i64p]),
+        "gkv_clone_seq": (C.c_int, [P, i32, i32p, P]),
+        "gkv_compact_seq": (C.c_int, [P, i32, P, P, P]),
+        "gkv_from_compact": (C.c_int, [P, P, P, i64, i32p, P]),
+        "gkv_export_table": (C.c_int, [P, i32, i32p, i32, i32p]),
+        "gkv_export_free_list": (C.c_int, [P, i32p, i32, i32p]),
+        "gkv_page_refcount": (C.c_int, [P, i32, i32p]),
+        "gkv_export_page": (C.c_int, [P, i32, P, P]),
+        "gkv_device_status": (C.c_int, [P, i32p]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != GKV_OK:
+        raise GkvError(rc, _lib.gkv_last_error().decode())
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
+
+
+def _i64(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int64).reshape(-1))
+
+
+def _p32(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def _p64(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int64))
+
+
+def _dev_ptr(t) -> Optional[int]:
+    """Device address of a contiguous torch CUDA tensor (or None)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU")
+    if not t.is_contiguous():
+        raise GkvError(GKV_ERR_INVALID, "tensor must be contiguous")
+    return t.data_ptr()
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+class BlockPool:
+    """One full-attention layer's page pool on one GPU (``gkv_pool``)."""
+
+    def __init__(self, kv_heads: int, head_dim: int, page_tokens: int, num_pages: int,
+                 max_seqs: int, max_pages_per_seq: int, seed: int = 0, device: int = 0):
+        L = load_library()
+        self.kv_heads, self.head_dim, self.page_tokens = kv_heads, head_dim, page_tokens
+        self.num_pages, self.max_seqs, self.max_pages_per_seq = num_pages, max_seqs, max_pages_per_seq
+        self.device = device
+        cfg = _PoolConfig(device, kv_heads, head_dim, page_tokens, num_pages, max_seqs,
+                          max_pages_per_seq, seed & (2**64 - 1))
+        h = C.c_void_p()
+        _check(L.gkv_pool_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+
+    # ------------------------------------------------------------ lifetime
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.gkv_pool_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ------------------------------------------------------------ sequences
+    def seq_create(self) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_seq_create(self._h, C.byref(out)))
+        return out.value
+
+    def seq_release(self, seq: int):
+        _check(_lib.gkv_seq_release(self._h, seq))
+
+    def length(self, seq: int) -> int:
+        out = C.c_int64()
+        _check(_lib.gkv_seq_length(self._h, seq, C.byref(out)))
+        return out.value
+
+    def page_count(self, seq: int) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_seq_page_count(self._h, seq, C.byref(out)))
+        return out.value
+
+    def free_page_count(self) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_free_page_count(self._h, C.byref(out)))
+        return out.value
+
+    # ------------------------------------------------------------ hot path
+    def append(self, seq_ids: Sequence[int], n_new: Sequence[int], k, v, stream=None):
+        """k, v: token-major [sum(n_new), kv_heads, head_dim] fp16 on the GPU."""
+        ids, nn = _i32(seq_ids), _i32(n_new)
+        _check(_lib.gkv_append(self._h, len(ids), _p32(ids), _p32(nn), _dev_ptr(k), _dev_ptr(v),
+                               _stream_ptr(stream)))
+
+    def seed(self, seq: int, K, V, count: int, stream=None):
+        """K, V: head-major [kv_heads, count, head_dim] fp16; the sequence must be empty."""
+        _check(_lib.gkv_seed(self._h, seq, _dev_ptr(K), _dev_ptr(V), count, _stream_ptr(stream)))
+
+    def attend(self, seq_ids: Sequence[int], n_q: int, group: int, q, out=None,
+               scale: Optional[float] = None, stream=None):
+        """q: [n, n_q, kv_heads*group, head_dim] fp16; returns fp32 of the same shape.
+        Row r of a sequence sees keys [0, length - n_q + r]."""
+        import torch
+        ids = _i32(seq_ids)
+        if out is None:
+            out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+        if scale is None:
+            scale = self.head_dim ** -0.5
+        _check(_lib.gkv_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(q),
+                               _dev_ptr(out), float(scale), _stream_ptr(stream)))
+        return out
+
+    def append_attend(self, seq_ids: Sequence[int], n_q: int, group: int, k, v, q, out=None,
+                      scale: Optional[float] = None, stream=None):
+        """Append n_q rows per sequence, then attend those n_q query rows."""
+        import torch
+        ids = _i32(seq_ids)
+        if out is None:
+            out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+        if scale is None:
+            scale = self.head_dim ** -0.5
+        _check(_lib.gkv_append_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(k),
+                                      _dev_ptr(v), _dev_ptr(q), _dev_ptr(out), float(scale),
+                                      _stream_ptr(stream)))
+        return out
+
+    def truncate(self, seq_ids: Sequence[int], new_len: Sequence[int]):
+        ids, nl = _i32(seq_ids), _i64(new_len)
+        _check(_lib.gkv_truncate(self._h, len(ids), _p32(ids), _p64(nl)))
+
+    def clone(self, seq: int, stream=None) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_clone_seq(self._h, seq, C.byref(out), _stream_ptr(stream)))
+        return out.value
+
+    def compact(self, seq: int, stream=None):
+        """(K, V) head-major [kv_heads, length, head_dim] fp16 device tensors."""
+        import torch
+        n = self.length(seq)
+        dev = torch.device("cuda", self.device)
+        K = torch.empty((self.kv_heads, n, self.head_dim), dtype=torch.float16, device=dev)
+        V = torch.empty_like(K)
+        _check(_lib.gkv_compact_seq(self._h, seq, _dev_ptr(K), _dev_ptr(V), _stream_ptr(stream)))
+        return K, V
+
+    def from_compact(self, K, V, length: int, stream=None) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_from_compact(self._h, _dev_ptr(K), _dev_ptr(V), length, C.byref(out),
+                                     _stream_ptr(stream)))
+        return out.value
+
+    # ------------------------------------------------------------ state export
+    def export_table(self, seq: int) -> np.ndarray:
+        n = C.c_int32()
+        _check(_lib.gkv_export_table(self._h, seq, None, 0, C.byref(n)))
+        out = np.empty(n.value, dtype=np.int32)
+        if n.value:
+            _check(_lib.gkv_export_table(self._h, seq, _p32(out), n.value, C.byref(n)))
+        return out
+
+    def export_free_list(self) -> np.ndarray:
+        n = C.c_int32()
+        _check(_lib.gkv_export_free_list(self._h, None, 0, C.byref(n)))
+        out = np.empty(n.value, dtype=np.int32)
+        if n.value:
+            _check(_lib.gkv_export_free_list(self._h, _p32(out), n.value, C.byref(n)))
+        return out
+
+    def page_refcount(self, pid: int) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_page_refcount(self._h, pid, C.byref(out)))
+        return out.value
+
+    def export_page(self, pid: int):
+        """(K, V) of one physical page as uint16 [kv_heads, P, head_dim]."""
+        shape = (self.kv_heads, self.page_tokens, self.head_dim)
+        K = np.empty(shape, dtype=np.uint16)
+        V = np.empty(shape, dtype=np.uint16)
+        _check(_lib.gkv_export_page(self._h, pid, K.ctypes.data, V.ctypes.data))
+        return K, V
+
+    def device_status(self) -> int:
+        out = C.c_int32()
+        _check(_lib.gkv_device_status(self._h, C.byref(out)))
+        return out.value
+
+
+class PagePool:
+    """The reference's per-layer, per-sequence cache object
+    (``PagePool``, PagedAttention.swift:21-287) as a view of one sequence of a
+    :class:`BlockPool`.  ``P``, ``kv_heads`` and ``dh`` mirror ``P``,
+    ``kvHeads`` and ``dh`` (:22-24)."""
+
+    def __init__(self, block_pool: BlockPool, seq_id: Optional[int] = None):
+        self.block_pool = block_pool
+        self.seq_id = block_pool.seq_create() if seq_id is None else seq_id
+
+    @property
+    def P(self) -> int:
+        return self.block_pool.page_tokens
+
+    @property
+    def kv_heads(self) -> int:
+        return self.block_pool.kv_heads
+
+    @property
+    def dh(self) -> int:
+        return self.block_pool.head_dim
+
+    @property
+    def length(self) -> int:
+        return self.block_pool.length(self.seq_id)
+
+    @property
+    def page_count(self) -> int:
+        return self.block_pool.page_count(self.seq_id)
+
+    def append(self, k, v, stream=None):
+        """One position's K and V, [kv_heads, head_dim] fp16 each (:85-94)."""
+        self.block_pool.append([self.seq_id], [1], k, v, stream)
+
+    def seed(self, K, V, count: int, stream=None):
+        """[kv_heads, count, head_dim] fp16 into fresh pages (:99-112)."""
+        self.block_pool.seed(self.seq_id, K, V, count, stream)
+
+    def truncate(self, to: int):
+        """truncate(to:) (:181-189)."""
+        self.block_pool.truncate([self.seq_id], [to])
+
+    def clone(self, stream=None) -> "PagePool":
+        """clone() (:199-210): shares full pages, copies a partial tail."""
+        return PagePool(self.block_pool, self.block_pool.clone(self.seq_id, stream))
+
+    def compact(self, stream=None):
+        """compact() (:225-252): (k, v) [kv_heads, length, head_dim] fp16."""
+        return self.block_pool.compact(self.seq_id, stream)
+
+    @staticmethod
+    def from_compact(block_pool: BlockPool, k, v, length: int, stream=None) -> "PagePool":
+        """fromCompact(k:v:length:P:kvHeads:dh:) (:256-264)."""
+        return PagePool(block_pool, block_pool.from_compact(k, v, length, stream))
+
+    def release(self):
+        self.block_pool.seq_release(self.seq_id)
+
+
+def host_flash_decode(q, pool: PagePool, G: int, stream=None):
+    """``hostFlashDecode(q:pool:G:)`` (PagedAttention.swift:317-366) on the GPU:
+    q [kv_heads, G, head_dim] fp16 -> [kv_heads*G*head_dim] fp32, the newest
+    query attending every one of the pool's ``length`` keys with
+    scale = head_dim^-0.5."""
+    bp = pool.block_pool
+    qq = q.reshape(1, 1, bp.kv_heads * G, bp.head_dim)
+    out = bp.attend([pool.seq_id], 1, G, qq, scale=bp.head_dim ** -0.5, stream=stream)
+    return out.reshape(-1)

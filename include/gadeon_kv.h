@@ -1,0 +1,167 @@
+/*
+ * gadeon_kv.h -- C ABI of the B200 paged KV cache (libgadeonkv.so).
+ *
+ * One gkv_pool is the physical page pool of ONE full-attention layer on ONE
+ * GPU: K and V pages of [kv_heads, page_tokens, head_dim] fp16, a block table
+ * per sequence, and a seeded LIFO free list.  A sequence inside a pool plays
+ * the role of the reference's per-layer PagePool
+ * (leok7v/gadeon LLM/src/CoreML/PagedAttention.swift:21-287); the attend
+ * entry points replace hostFlashDecode (:317-366), the causal verify loop
+ * (LLM/src/CoreML/Engine.swift:2620-2646) and the batched prefill flash
+ * (PagedAttention.swift:376-495), and on the Metal side MetalKVPool
+ * (LLM/src/Metal/MetalKVPool.swift:20-126) with the kernels kv_append,
+ * kv_append_batch, attn_head, attn_batch, attn_batch_mm
+ * (LLM/metal/Kernels.metal:1265-1457, :1721-2014).
+ *
+ * Conventions
+ *   - Every call returns a status (GKV_OK == 0); gkv_last_error() gives the
+ *     calling thread's message for its last failure.  A failing call leaves
+ *     the pool unchanged (validation happens before any mutation).
+ *   - K/V/Q and outputs are DEVICE pointers on the pool's GPU; id and length
+ *     arrays are HOST pointers.  `stream` is a cudaStream_t (NULL = the
+ *     legacy default stream).  Work is enqueued asynchronously.
+ *   - Host bookkeeping (lengths, block tables, free list) is updated when the
+ *     call returns; the device copy of the tables is updated in stream order.
+ *   - A pool is not thread-safe: serialise calls on one pool (the reference
+ *     serialises them inside one Swift actor, Engine.swift:41) and issue all
+ *     of its work on one stream, or order the streams yourself.
+ *   - fp16 values are IEEE binary16 bit patterns; attention accumulates in
+ *     fp32 and writes fp32.
+ */
+#ifndef GADEON_KV_H
+#define GADEON_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gkv_pool gkv_pool;
+
+enum gkv_status {
+    GKV_OK = 0,
+    GKV_ERR_INVALID = 1,     /* bad argument, shape or geometry */
+    GKV_ERR_NO_PAGES = 2,    /* free list exhausted (pool left unchanged) */
+    GKV_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+    GKV_ERR_BAD_SEQ = 4,     /* unknown/released sequence, or length out of range */
+    GKV_ERR_UNSUPPORTED = 5, /* geometry with no kernel in this build */
+    GKV_ERR_CAPACITY = 6     /* max_seqs or max_pages_per_seq exceeded */
+};
+
+/* Message for the calling thread's last failing call ("" if none). */
+const char *gkv_last_error(void);
+/* Library version string. */
+const char *gkv_version(void);
+
+typedef struct gkv_pool_config {
+    int32_t device;            /* CUDA device ordinal */
+    int32_t kv_heads;          /* KVH (2 or 4 for Qwen3.5 hybrids) */
+    int32_t head_dim;          /* dh: 64, 128, 256 or 512 */
+    int32_t page_tokens;       /* P: power of two, 1..16384 */
+    int32_t num_pages;         /* physical pages in this pool */
+    int32_t max_seqs;          /* block-table rows */
+    int32_t max_pages_per_seq; /* block-table row length (context <= this * P) */
+    uint64_t seed;             /* free-list permutation seed */
+} gkv_pool_config;
+
+/* Create a pool (PagePool.init(P:kvHeads:dh:), PagedAttention.swift:40;
+ * MetalKVPool.init, MetalKVPool.swift:34).  The free list's pop order is the
+ * splitmix64 Fisher-Yates permutation of 0..num_pages-1 for `seed`. */
+int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out);
+int gkv_pool_destroy(gkv_pool *pool);
+
+/* A new empty sequence; ids are the lowest unused id. */
+int gkv_seq_create(gkv_pool *pool, int32_t *seq_id);
+/* Drop every page of the sequence (last page first) and retire its id. */
+int gkv_seq_release(gkv_pool *pool, int32_t seq_id);
+/* PagePool.length / pageCount (PagedAttention.swift:27, :79). */
+int gkv_seq_length(const gkv_pool *pool, int32_t seq_id, int64_t *length);
+int gkv_seq_page_count(const gkv_pool *pool, int32_t seq_id, int32_t *pages);
+int gkv_free_page_count(const gkv_pool *pool, int32_t *pages);
+
+/* Batched append (PagePool.append(k:v:), PagedAttention.swift:85-94, called
+ * per row by Engine.stepHidden :1921, batchedAttn :1797-1800 and verifyAttn
+ * :2629-2630; Metal kv_append / kv_append_batch, Kernels.metal:1446-1457,
+ * :1726-1740).  Sequence seq_ids[i] takes n_new[i] rows; k and v are
+ * token-major [sum(n_new), kv_heads, head_dim] fp16, rows in batch order.
+ * A page is allocated (and zero-filled) whenever a row lands on slot 0. */
+int gkv_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+               const int32_t *n_new, const void *k, const void *v,
+               void *stream);
+
+/* PagePool.seed(K:V:count:) (PagedAttention.swift:99-112): bulk-load an
+ * EMPTY sequence from head-major [kv_heads, count, head_dim] fp16. */
+int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V,
+             int64_t count, void *stream);
+
+/* Paged GQA attention over the block tables (hostFlashDecode,
+ * PagedAttention.swift:317-366; causal verify Engine.swift:2620-2646; Metal
+ * attn_head / attn_batch, Kernels.metal:1423-1439, :1767-1793).
+ * Each sequence's n_q query rows are its LAST n_q positions (append them
+ * first): row r sees keys [0, length - n_q + r].  n_q == 1 is single-token
+ * decode (the newest query sees every key, like hostFlashDecode).
+ * q: [n_seqs, n_q, kv_heads*group, head_dim] fp16 (head h = kvh*group + g,
+ * PagedAttention.swift:331-332); out: same shape, fp32.
+ * scale multiplies q.k (hostFlashDecode uses head_dim^-0.5, :321). */
+int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+               int32_t n_q, int32_t group, const void *q, float *out,
+               float scale, void *stream);
+
+/* One decode / verify step in one call: gkv_append of n_q rows per
+ * sequence followed by gkv_attend of those n_q rows. */
+int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                      int32_t n_q, int32_t group, const void *k,
+                      const void *v, const void *q, float *out, float scale,
+                      void *stream);
+
+/* PagePool.truncate(to:) for a batch (PagedAttention.swift:181-189; the
+ * rollback of Engine.decodeSpecStep :2787, :2792): lengths drop to
+ * new_len[i]; whole pages past ceil(new_len/P) leave the table last-first and
+ * return to the free list when no clone shares them.  The kept tail keeps
+ * its stale rows.  Host bookkeeping only: no device work is enqueued. */
+int gkv_truncate(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                 const int64_t *new_len);
+
+/* PagePool.clone() (PagedAttention.swift:199-210; MetalKVPool.snapshot,
+ * MetalKVPool.swift:102-109): a new sequence sharing every page of `src`,
+ * with a private copy of a partially filled tail page. */
+int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream);
+
+/* PagePool.compact() (PagedAttention.swift:225-252): K and V as head-major
+ * [kv_heads, length, head_dim] fp16 device buffers. */
+int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V,
+                    void *stream);
+
+/* PagePool.fromCompact (PagedAttention.swift:256-264): a new sequence seeded
+ * from head-major [kv_heads, length, head_dim] fp16 device buffers. */
+int gkv_from_compact(gkv_pool *pool, const void *K, const void *V,
+                     int64_t length, int32_t *seq_id, void *stream);
+
+/* ---- state export, for parity checks and debugging (synchronous) ---- */
+
+/* The sequence's block table as held ON THE DEVICE (first `pages` entries;
+ * waits for the device).  cap = room in `pages_out`. */
+int gkv_export_table(gkv_pool *pool, int32_t seq_id, int32_t *pages_out,
+                     int32_t cap, int32_t *n_pages);
+/* The free list in pop order (head first). */
+int gkv_export_free_list(const gkv_pool *pool, int32_t *out, int32_t cap,
+                         int32_t *n);
+/* Reference count of a physical page (0 = free). */
+int gkv_page_refcount(const gkv_pool *pool, int32_t page_id, int32_t *ref);
+/* Copy one physical page's K and V ([kv_heads, P, head_dim] fp16 each) to
+ * host memory (waits for the device). */
+int gkv_export_page(gkv_pool *pool, int32_t page_id, void *k_host,
+                    void *v_host);
+/* Waits for the device and returns the pool's device status word: 0, or
+ * bit 1 = a kernel's bounded wait ran out, bit 2 = a block-table entry was
+ * outside the pool.  No reference counterpart (the reference's device
+ * errors surface through Metal command buffers, MetalGolden.swift:384). */
+int gkv_device_status(gkv_pool *pool, int32_t *status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GADEON_KV_H */

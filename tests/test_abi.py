@@ -1,0 +1,74 @@
+"""CPU tests of the C ABI boundary (no GPU, no compute): the library loads,
+exports every entry point include/gadeon_kv.h declares, and rejects bad
+geometry before touching the device."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gadeon_kv.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gkv_[a-z_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from gadeon_b200 import build, kv
+    build.build()
+    return kv.load_library()
+
+
+def test_header_matches_binding():
+    from gadeon_b200 import kv
+    assert declared_symbols() == sorted(kv.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", os.path.join(ROOT, "gadeon_b200", "libgadeonkv.so")],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (gkv_\w+)", out))
+    assert set(declared_symbols()) <= exported
+
+
+def test_version_and_error_string(lib):
+    assert b"sm_100a" in lib.gkv_version()
+    assert isinstance(lib.gkv_last_error(), bytes)
+
+
+def test_header_compiles_as_c():
+    src = "#include \"gadeon_kv.h\"\nint main(void){gkv_pool_config c={0};(void)c;return 0;}\n"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER),
+                        "-x", "c", "-", "-fsyntax-only"], input=src, text=True, capture_output=True)
+    assert r.returncode == 0, r.stderr
+
+
+@pytest.mark.parametrize("field,value,code", [
+    ("head_dim", 96, 5),      # GKV_ERR_UNSUPPORTED
+    ("page_tokens", 12, 1),   # not a power of two -> GKV_ERR_INVALID
+    ("page_tokens", 32768, 1),
+    ("kv_heads", 0, 1),
+    ("num_pages", 0, 1),
+])
+def test_pool_create_rejects_geometry(lib, field, value, code):
+    from gadeon_b200.kv import _PoolConfig
+    cfg = _PoolConfig(0, 2, 256, 16, 64, 4, 64, 1)
+    setattr(cfg, field, value)
+    h = C.c_void_p()
+    assert lib.gkv_pool_create(C.byref(cfg), C.byref(h)) == code
+    assert not h.value
+    assert len(lib.gkv_last_error()) > 0
+
+
+def test_null_arguments(lib):
+    assert lib.gkv_pool_create(None, None) == 1
+    assert lib.gkv_seq_create(None, None) == 1
+    assert lib.gkv_pool_destroy(None) == 0
