@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""bench.py -- KV append + paged GQA decode attention on B200.
+
+Default workload (per GPU): 64 sequences with contexts
+~U[1024, 32768], 6 full-attention layers (one page pool each), nH=8, KVH=2,
+dh=256, 16-token pages scattered by a seeded permutation over a pool of
+1.25x the pages.  One step = for every layer, append one K/V row per
+sequence and run paged decode attention for every sequence.
+
+  value   appended+attended tokens/s of the whole job (sequences x GPUs per
+          step time), inputs resident in HBM, timed with CUDA events, max
+          over ranks;
+  e2e     the same through the public C-ABI call with pinned HOST q/k/v
+          copied in and outputs copied out inside the timed region;
+  roofline  the attend kernel: algorithmic bytes / CUDA-event time per
+          launch vs the measured HBM copy bandwidth;
+  cpu_baseline  the oracle's restatement of hostFlashDecode on a bounded
+          sample of the same workload, one host thread.
+
+`--impl reference` times the reference's CPU path (the oracle port: the
+reference is Swift over Apple frameworks and cannot be built here) with all
+host threads on a bounded sample of the same workload.
+
+Multi-GPU (torchrun): weak scaling -- every rank runs its own 64 sequences
+with its own pools; no collective on the hot path.  The NCCL output gather
+is timed separately (gather_ms_per_step) after the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+from gadeon_b200.workload import CONFIGS, contexts, decode_bytes, pool_pages  # noqa: E402
+
+METRIC = "KV append+attend tok/s (paged GQA decode, config 2)"
+UNIT = "tok/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=20251201)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    # profiling knobs: shrink the workload (ncu captures of one launch);
+    # a line measured with them is not the config-2 number
+    ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
+    ap.add_argument("--layers", type=int, default=None, help="layers (default: config 2's 6)")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 50 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.file.read())) if len(r) >= 9]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_sample(seed: int, n_seqs: int, steps: int, threads: int, cfg, ctx_all):
+    """Time the oracle (hostFlashDecode restatement) on a bounded sample:
+    n_seqs sequences drawn from the job's contexts, one layer, `steps`
+    decode steps of append-one + attend.  Returns (seconds per sequence-
+    layer-step normalised to the job's mean context, sample description)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    pick = rng.choice(len(ctx_all), size=min(n_seqs, len(ctx_all)), replace=False)
+    ctx = [int(ctx_all[i]) for i in pick]
+    kvh, dh, G, P = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.page_tokens
+    pool = O.OraclePool(kvh, dh, P, pool_pages(ctx, P, steps + 4), seed)
+    ids = []
+    for c in ctx:
+        s = pool.seq_create()
+        K = rng.standard_normal((kvh, c, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+        V = rng.standard_normal((kvh, c, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+        pool.seed(s, K, V, c)
+        ids.append(s)
+    scale = dh ** -0.5
+    times = []
+    for step in range(steps + 1):
+        k = rng.standard_normal((len(ids), kvh, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+        q = rng.standard_normal((len(ids), 1, kvh * G, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+        t0 = time.perf_counter()
+        pool.append(ids, [1] * len(ids), k, k)
+        pool.attend_causal(ids, 1, q, G, scale, n_threads=threads)
+        dt = time.perf_counter() - t0
+        if step > 0:  # step 0 builds the fp32 mirror (floats32's first call)
+            times.append(dt)
+    sample_tokens = sum(ctx) + len(ctx) * (steps / 2 + 1)
+    per_token_key = statistics.mean(times) / sample_tokens  # seconds per attended key
+    desc = (f"{len(ctx)} of the job's sequences (ctx sum {sum(ctx)}), 1 layer, {steps} decode steps "
+            f"after a mirror-building step; time scaled by attended keys to the full step")
+    return per_token_key, desc, sum(times)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the oracle port of the reference's CPU path with all
+    host threads, each step a bounded sample of the job's step."""
+    if rank != 0:
+        return
+    cfg = CONFIGS[2]
+    ctx_all = np.concatenate([contexts(2, args.seed + 1000 * r, cfg.seqs) for r in range(world)])
+    threads = os.cpu_count() or 1
+    steps = args.warmup + args.steps
+    per_key, desc, cpu_s = cpu_sample(args.seed + 7, 16, steps, threads, cfg, ctx_all)
+    job_keys = float(ctx_all.sum()) * cfg.layers
+    step_s = per_key * job_keys
+    value = len(ctx_all) / step_s
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 storage)", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "config2 decode step: 64 seqs/GPU x 6 layers, ctx ~U[1024,32768], "
+                               "nH=8 KVH=2 dh=256 P=16", "seqs": int(len(ctx_all)), "layers": cfg.layers},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc + f"; every step repeats the sample ({cpu_s:.1f} s CPU total)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    from gadeon_b200 import BlockPool
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[2]
+    L, S, KVH, dh, P, G, nH = cfg.layers, cfg.seqs, cfg.kv_heads, cfg.head_dim, cfg.page_tokens, cfg.group, cfg.n_heads
+    L = args.layers or L
+    S = args.seqs or S
+    W, K = args.warmup, args.steps
+    ctx = contexts(2, args.seed + 1000 * rank, S)
+    steps_total = W + K + (0 if args.no_e2e else K) + 2
+    max_pps = int(math.ceil((int(ctx.max()) + steps_total) / P)) + 2
+    n_pages = pool_pages(ctx, P, steps_total)
+
+    # ---- pools, seeded contexts (device RNG, seeded per rank and layer)
+    pools, ids = [], []
+    scratch = torch.empty(KVH * int(ctx.max()) * dh * 2, dtype=torch.float16, device=dev)
+    gen = torch.Generator(device=dev)
+    for layer in range(L):
+        pool = BlockPool(KVH, dh, P, n_pages, S + 1, max_pps, seed=(args.seed * 1_000_003 + rank * 4099 + layer),
+                         device=local)
+        gen.manual_seed(args.seed * 7919 + rank * 131 + layer)
+        lids = []
+        for c in ctx:
+            c = int(c)
+            s = pool.seq_create()
+            buf = scratch[: 2 * KVH * c * dh]
+            torch.randn(buf.shape, generator=gen, device=dev, dtype=torch.float16, out=buf)
+            kv = buf.view(2, KVH, c, dh)
+            pool.seed(s, kv[0], kv[1], c)
+            lids.append(s)
+        pools.append(pool)
+        ids.append(lids)
+    del scratch
+    # per-step inputs for warm-up + timed steps
+    NS = W + K
+    q_all = torch.randn((NS, L, S, 1, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    k_all = torch.randn((NS, L, S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    v_all = torch.randn((NS, L, S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
+    ones = [1] * S
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+
+    def step(i, timed_idx=None):
+        for layer in range(L):
+            pools[layer].append(ids[layer], ones, k_all[i, layer], v_all[i, layer])
+            if timed_idx is not None:
+                ev[timed_idx * L + layer][0].record()
+            pools[layer].attend(ids[layer], 1, G, q_all[i, layer], out=outs[layer])
+            if timed_idx is not None:
+                ev[timed_idx * L + layer][1].record()
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]
+                              if os.environ.get("CUDA_VISIBLE_DEVICES") else local))
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    start.record()
+    for i in range(K):
+        step(W + i, i)
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end) / K
+    attend_ms = [a.elapsed_time(b) for a, b in ev]
+    attend_avg_ms = statistics.mean(attend_ms)
+    # algorithmic bytes of each timed attend launch (contexts after its append)
+    bytes_per_launch = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K))
+    hbm_peak, peak_kind = peaks()
+    achieved = bytes_per_launch / (attend_avg_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public call with host buffers
+    e2e = None
+    if not args.no_e2e:
+        qh = q_all[W:].cpu().pin_memory()
+        kh = k_all[W:].cpu().pin_memory()
+        vh = v_all[W:].cpu().pin_memory()
+        oh = torch.empty((K, L, S, 1, nH, dh), dtype=torch.float32).pin_memory()
+        qd, kd, vd = torch.empty_like(q_all[0, 0]), torch.empty_like(k_all[0, 0]), torch.empty_like(v_all[0, 0])
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(K):
+            for layer in range(L):
+                qd.copy_(qh[i, layer], non_blocking=True)
+                kd.copy_(kh[i, layer], non_blocking=True)
+                vd.copy_(vh[i, layer], non_blocking=True)
+                pools[layer].append_attend(ids[layer], 1, G, kd, vd, qd, out=outs[layer])
+                oh[i, layer].copy_(outs[layer], non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / K
+        h2d = L * (qd.numel() + kd.numel() + vd.numel()) * 2
+        d2h = L * outs[0].numel() * 4
+        e2e = [e2e_ms, h2d, d2h]
+
+    # ---- NCCL output gather (not on the hot path; timed separately)
+    gather_ms = None
+    if world > 1:
+        flat = torch.cat([o.reshape(-1) for o in outs])
+        gathered = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
+        for _ in range(3):
+            dist.all_gather_into_tensor(gathered, flat)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(K):
+            dist.all_gather_into_tensor(gathered, flat)
+        g1.record()
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1) / K
+
+    # ---- max over ranks
+    vals = torch.tensor([ms, e2e[0] if e2e else 0.0, gather_ms or 0.0, attend_avg_ms], device=dev,
+                        dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms_max, gather_max, attend_max = vals.tolist()
+    for p in pools:
+        st = p.device_status()
+        assert st == 0, f"device status {st}"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        per_key, desc, cpu_s = cpu_sample(args.seed + 7, 16, 6, 1, cfg, ctx)
+        job_keys = float(ctx.sum()) * L
+        cpu_step = per_key * job_keys
+        cpu = {"value": S / cpu_step, "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": desc + f" ({cpu_s:.1f} s of CPU time)"}
+
+    if rank != 0:
+        return
+    tokens = S * world
+    line = {
+        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {
+            "workload": (f"config2 decode step: {S} seqs/GPU x {L} layers, append 1 + paged GQA decode attend"
+                         + ("" if (S, L) == (cfg.seqs, cfg.layers) else " (REDUCED profiling case)")),
+            "seqs_per_gpu": S, "layers": L, "n_heads": nH, "kv_heads": KVH, "head_dim": dh,
+            "page_tokens": P, "ctx": "U[1024,32768] seeded per rank", "ctx_mean": float(ctx.mean()),
+            "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)" % (float(ctx.sum()) * L * KVH * dh * 4 / 1e9),
+            "parallelism": f"dp{world} (sequences sharded, no hot-path collective)",
+        },
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "attend_kernel<256,TMA>", "bytes_per_launch": bytes_per_launch,
+                     "launch_ms": attend_avg_ms, "launch_ms_max_rank": attend_max},
+        "cpu_baseline": cpu,
+        "e2e": ({"value": tokens / (e2e_ms_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": e2e[1],
+                 "d2h_bytes_per_step": e2e[2], "ms_per_step": e2e_ms_max} if e2e else None),
+        "gpu_launches": K * L * 2,
+        "clocks": clk,
+    }
+    if gather_ms is not None:
+        line["gather_ms_per_step"] = gather_max
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

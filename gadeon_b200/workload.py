@@ -1,0 +1,102 @@
+"""Synthetic workloads of the five BASELINE configurations and the
+token-balanced sharding of sequences across GPUs.
+
+Contexts and page permutations are drawn from documented seeds; K/V/Q values
+are N(0,1) cast to fp16.  Each GPU owns a private pool per layer, seeded
+per (GPU, layer), and no data crosses GPUs on the hot path.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+from typing import List, Sequence
+
+import numpy as np
+
+
+@dataclasses.dataclass(frozen=True)
+class Config:
+    name: str
+    seqs: int          # sequences in the whole job (per GPU for weak-scaled configs)
+    layers: int
+    n_heads: int
+    kv_heads: int
+    head_dim: int
+    page_tokens: int
+    n_q: int           # query rows per sequence per step (1 = decode, 4 = MTP verify)
+    description: str
+
+    @property
+    def group(self) -> int:
+        return self.n_heads // self.kv_heads
+
+
+CONFIGS = {
+    1: Config("config1", 1, 1, 8, 2, 256, 16, 1,
+              "single layer, B=1, 512-token prefill append then decode (ctx 513..640)"),
+    2: Config("config2", 64, 6, 8, 2, 256, 16, 1,
+              "batched decode, ctx ~U[1024,32768], 6 layers, nH=8, KVH=2, dh=256, P=16"),
+    3: Config("config3", 128, 1, 16, 4, 256, 16, 4,
+              "MTP verify: 4 drafts appended + causal attend, truncate to len+U{0..4}, ctx 8192"),
+    4: Config("config4", 32, 8, 16, 4, 256, 16, 4096,
+              "prefill chunk: 4096 new tokens over 16384 prior, 8 layers"),
+    5: Config("config5", 512, 8, 16, 4, 256, 16, 1,
+              "long-context sharded decode, ctx log-U[4096,131072], 8 layers, 512 seqs / job"),
+}
+
+
+def contexts(cfg_id: int, seed: int, n: int) -> np.ndarray:
+    """Context lengths of config cfg_id drawn from `seed`."""
+    rng = np.random.default_rng(seed)
+    if cfg_id == 1:
+        return np.full(n, 512, dtype=np.int64)
+    if cfg_id == 2:
+        return rng.integers(1024, 32768, size=n, endpoint=True).astype(np.int64)
+    if cfg_id == 3:
+        return np.full(n, 8192, dtype=np.int64)
+    if cfg_id == 4:
+        return np.full(n, 16384, dtype=np.int64)
+    if cfg_id == 5:
+        return np.exp(rng.uniform(math.log(4096), math.log(131072), size=n)).astype(np.int64)
+    raise ValueError(cfg_id)
+
+
+def lpt_partition(tokens: Sequence[int], parts: int) -> List[List[int]]:
+    """Greedy longest-processing-time partition: sequences by context
+    descending, each to the currently least-loaded part (ties -> lowest
+    index).  Returns the sequence indices of every part, ascending."""
+    order = sorted(range(len(tokens)), key=lambda i: (-int(tokens[i]), i))
+    load = [0] * parts
+    out: List[List[int]] = [[] for _ in range(parts)]
+    for i in order:
+        p = min(range(parts), key=lambda r: (load[r], r))
+        out[p].append(i)
+        load[p] += int(tokens[i])
+    return [sorted(o) for o in out]
+
+
+def pool_pages(ctx: Sequence[int], page_tokens: int, growth_tokens: int, factor: float = 1.25) -> int:
+    """Physical pages for a layer pool: `factor` x the pages the contexts
+    occupy, plus room for `growth_tokens` more per sequence."""
+    need = sum((int(c) + page_tokens - 1) // page_tokens for c in ctx)
+    grow = len(ctx) * ((growth_tokens + page_tokens - 1) // page_tokens + 1)
+    return int(math.ceil(need * factor)) + grow
+
+
+def decode_bytes(ctx_after: Sequence[int], cfg: Config, out_bytes: int = 4) -> int:
+    """Algorithmic HBM bytes of one attend launch (one layer) over sequences
+    whose contexts (after the append) are ctx_after: each K and V byte read
+    once, q read, out written, block-table entries read."""
+    kv_row = cfg.kv_heads * cfg.head_dim * 2
+    total = 0
+    for c in ctx_after:
+        c = int(c)
+        total += c * kv_row * 2
+        total += cfg.n_q * cfg.n_heads * cfg.head_dim * (2 + out_bytes)
+        total += 4 * ((c + cfg.page_tokens - 1) // cfg.page_tokens)
+    return total
+
+
+def append_bytes(n_rows: int, cfg: Config) -> int:
+    """Bytes one append moves: rows read + written, K and V."""
+    return n_rows * cfg.kv_heads * cfg.head_dim * 2 * 2 * 2
