@@ -97,4 +97,11 @@ struct CompactParams {
 };
 cudaError_t launch_compact(const CompactParams &p, cudaStream_t s);
 
+// Host helpers for gkv_attend_noalloc (gkv_pool.cpp): record the calling
+// thread's gkv_last_error() message and return `code`; encode the attend
+// kernel's TMA view of a caller-owned K or V page array.
+int report_error(int code, const char *fmt, ...);
+int encode_page_tensor_map(CUtensorMap *map, const void *pages, int num_pages, int kv_heads,
+                           int page_tokens, int head_dim);
+
 }  // namespace gkv

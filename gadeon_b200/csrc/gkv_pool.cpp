@@ -378,6 +378,38 @@ void free_device(gkv_pool *p) {
 
 }  // namespace
 
+namespace gkv {
+
+int report_error(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int encode_page_tensor_map(CUtensorMap *map, const void *pages, int num_pages, int kv_heads,
+                           int page_tokens, int head_dim) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return report_error(GKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const int bh = std::min(page_tokens, attend_tile_keys(head_dim));
+    const cuuint64_t dims[2] = {(cuuint64_t)head_dim,
+                                (cuuint64_t)num_pages * kv_heads * page_tokens};
+    const cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)bh};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(pages), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return report_error(GKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GKV_OK;
+}
+
+}  // namespace gkv
+
 extern "C" {
 
 const char *gkv_last_error(void) { return g_last_error.c_str(); }

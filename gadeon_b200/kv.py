@@ -45,6 +45,7 @@ EXPORTED = (
     "gkv_append", "gkv_seed", "gkv_attend", "gkv_append_attend", "gkv_truncate",
     "gkv_clone_seq", "gkv_compact_seq", "gkv_from_compact", "gkv_export_table",
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
+    "gkv_attend_noalloc",
 )
 
 
@@ -99,6 +100,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_page_refcount": (C.c_int, [P, i32, i32p]),
         "gkv_export_page": (C.c_int, [P, i32, P, P]),
         "gkv_device_status": (C.c_int, [P, i32p]),
+        "gkv_attend_noalloc": (C.c_int, [P, P, i32, i32, i32, i32, P, i32, i32, i32p, i32, i32, P, P,
+                                         f32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

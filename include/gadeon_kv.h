@@ -139,6 +139,34 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V,
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V,
                      int64_t length, int32_t *seq_id, void *stream);
 
+/* Size of the library's static scratch array used by gkv_attend_noalloc
+ * (held on every GPU that loads the library until the process exits), and
+ * the largest batch that entry point takes. */
+#define GKV_NOALLOC_SCRATCH_BYTES 8388608u
+#define GKV_NOALLOC_MAX_SEQS 1024
+
+/* Paged GQA decode / verify attention that allocates nothing.  No
+ * counterpart in the reference.  For callers that own all device memory
+ * and cannot call cudaMalloc while serving (an engine with one arena
+ * reserved at start-up, or a language binding with its own allocator): the
+ * K/V pages ([num_pages][kv_heads][page_tokens][head_dim] fp16 each), the
+ * block table (device int32, row i = batch entry i, table_stride entries)
+ * and q/out are the caller's; seq_lens is a HOST array of the n_seqs
+ * lengths.  q, out, n_q, group and scale mean what they mean for
+ * gkv_attend, and the results match it.  The kernel's scratch lives in one
+ * static __device__ array of GKV_NOALLOC_SCRATCH_BYTES; a call that needs
+ * more (too many sequences x kv heads for head_dim) or has more than
+ * GKV_NOALLOC_MAX_SEQS sequences fails with GKV_ERR_CAPACITY.  The first
+ * call on each device looks up that array's device address (set-up), so
+ * make that first call before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race. */
+int gkv_attend_noalloc(const void *k_pages, const void *v_pages,
+                       int32_t num_pages, int32_t kv_heads, int32_t head_dim,
+                       int32_t page_tokens, const int32_t *block_table,
+                       int32_t table_stride, int32_t n_seqs,
+                       const int32_t *seq_lens, int32_t n_q, int32_t group,
+                       const void *q, float *out, float scale, void *stream);
+
 /* ---- state export, for parity checks and debugging (synchronous) ---- */
 
 /* The sequence's block table as held ON THE DEVICE (first `pages` entries;
