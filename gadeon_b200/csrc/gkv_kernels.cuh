@@ -88,6 +88,28 @@ cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tmap_k,
 // Key tile length used by the attend kernel for head_dim dh.
 int attend_tile_keys(int dh);
 
+// ---------------------------------------------------------------- chunk
+// Causal attention for many query rows per (sequence, kv head): prefill
+// chunks and wide verify batches (n_q * G > 16).  One CTA per block of
+// `qtok` query tokens x G heads (<= 128 rows = one tcgen05 M tile).
+struct ChunkParams {
+    const AttendEntry *entries;  // seq_id, len (unit fields unused)
+    int32_t n_seqs;
+    const int32_t *table;
+    int32_t table_stride;
+    const uint16_t *q;  // [n_seqs, n_q, KVH*G, dh]
+    float *out;         // [n_seqs, n_q, KVH*G, dh]
+    int32_t *status;
+    int32_t n_q, G, kvh, P, num_pages;
+    int32_t qtok;       // query tokens per CTA
+    int32_t n_qblocks;  // ceil(n_q / qtok)
+    float scale_log2;
+};
+// True when the chunk kernel handles (dh, P, G).
+bool chunk_supported(int dh, int P, int G);
+cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tmap_k,
+                         const CUtensorMap *tmap_v, int dh, cudaStream_t s);
+
 struct CompactParams {
     const int32_t *table;  // row of the sequence
     const uint16_t *k_pool, *v_pool;

@@ -307,9 +307,12 @@ int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
 int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
                  const void *q, const float *out) {
     if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
-    if ((int64_t)n_q * group > 16)
-        return fail(GKV_ERR_UNSUPPORTED, "n_q*group = %d query rows per kv head (max 16)",
-                    n_q * group);
+    if ((int64_t)n_q * group > 16 &&
+        !gkv::chunk_supported(pool->cfg.head_dim, pool->cfg.page_tokens, group))
+        return fail(GKV_ERR_UNSUPPORTED,
+                    "n_q*group = %lld rows per kv head needs the chunk kernel (head_dim <= 256, "
+                    "page_tokens >= 8)",
+                    (long long)n_q * group);
     if (n > 0 && (!q || !out)) return fail(GKV_ERR_INVALID, "null q/out");
     if (!aligned16(q) || !aligned16(out)) return fail(GKV_ERR_INVALID, "q/out not 16-byte aligned");
     for (int32_t i = 0; i < n; ++i)
@@ -334,6 +337,29 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         const int32_t ntiles = (int32_t)((s.len + TK - 1) / TK);
         ent[i] = {ids[i], (int32_t)s.len, (int32_t)units, ntiles};
         units += (int64_t)KVH * ntiles;
+    }
+    if ((int64_t)n_q * group > 16) {  // many rows per kv head: tcgen05 chunk kernel
+        GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
+        gkv::ChunkParams c{};
+        c.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
+        c.n_seqs = n;
+        c.table = pool->d_table;
+        c.table_stride = pool->cfg.max_pages_per_seq;
+        c.q = static_cast<const uint16_t *>(q);
+        c.out = out;
+        c.status = pool->d_status;
+        c.n_q = n_q;
+        c.G = group;
+        c.kvh = KVH;
+        c.P = pool->cfg.page_tokens;
+        c.num_pages = pool->cfg.num_pages;
+        c.qtok = 128 / group;
+        c.n_qblocks = (n_q + c.qtok - 1) / c.qtok;
+        c.scale_log2 = scale * 1.4426950408889634f;
+        GKV_CUDA(gkv::launch_chunk(c, &pool->tmk, &pool->tmv, pool->cfg.head_dim, st),
+                 "chunk kernel launch");
+        GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
+        return GKV_OK;
     }
     if (units > INT32_MAX) return fail(GKV_ERR_CAPACITY, "too many key tiles in one call");
     GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
