@@ -64,6 +64,9 @@ def parse_args():
     # a line measured with them is not the config-2 number
     ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: config 2's 6)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                    help="BASELINE config: 2 decode (default, the headline), 3 MTP verify+rollback, "
+                         "4 prefill chunk, 5 long-context sharded decode")
     return ap.parse_args()
 
 
@@ -75,6 +78,22 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak(sustained: bool):
+    """Dense bf16 tensor peak (TFLOP/s): burst for a kernel timed alone,
+    sustained for one timed inside a long step."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
+    except Exception:
+        return (1400.0 if sustained else 1590.0), "fallback"
+
+
+def gpu_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(vis.split(",")[local]) if vis else local
 
 
 class ClockSampler:
@@ -360,12 +379,311 @@ def run_ours(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- configs 3-5
+
+def make_pools(torch, cfg, ctx, L, rank, seed, growth, local, factor=1.25, distinct=True):
+    """One BlockPool per layer (its own seeded page permutation); sequence i
+    seeded with ctx[i] rows of N(0,1) fp16 from torch's seeded device RNG.
+    distinct=False draws one random buffer per layer and seeds every
+    sequence from its prefix (values do not change the memory traffic)."""
+    from gadeon_b200 import BlockPool
+    KVH, dh, P = cfg.kv_heads, cfg.head_dim, cfg.page_tokens
+    dev = torch.device("cuda", local)
+    cmax = int(max(ctx))
+    max_pps = int(math.ceil((cmax + growth) / P)) + 2
+    n_pages = pool_pages(ctx, P, growth, factor)
+    scratch = torch.empty(2 * KVH * cmax * dh, dtype=torch.float16, device=dev)
+    gen = torch.Generator(device=dev)
+    pools, ids = [], []
+    for layer in range(L):
+        pool = BlockPool(KVH, dh, P, n_pages, len(ctx) + 1, max_pps,
+                         seed=(seed * 1_000_003 + rank * 4099 + layer), device=local)
+        gen.manual_seed(seed * 7919 + rank * 131 + layer)
+        if not distinct:
+            torch.randn(scratch.shape, generator=gen, device=dev, dtype=torch.float16, out=scratch)
+        lids = []
+        for c in ctx:
+            c = int(c)
+            sid = pool.seq_create()
+            buf = scratch[: 2 * KVH * c * dh]
+            if distinct:
+                torch.randn(buf.shape, generator=gen, device=dev, dtype=torch.float16, out=buf)
+            kv = buf.view(2, KVH, c, dh)
+            pool.seed(sid, kv[0], kv[1], c)
+            lids.append(sid)
+        pools.append(pool)
+        ids.append(lids)
+    del scratch
+    torch.cuda.synchronize()
+    return pools, ids, gen
+
+
+def timed_loop(torch, dist, world, W, K, step, local):
+    """W untimed steps, then K steps between barrier+synchronize brackets,
+    clocks sampled meanwhile; returns (ms per step max over ranks, clocks)."""
+    for i in range(W):
+        step(i, None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record()
+    for i in range(K):
+        step(W + i, i)
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end) / K
+    t = torch.tensor([ms], device=torch.device("cuda", local), dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), clk
+
+
+def max_over_ranks(torch, dist, world, local, x):
+    t = torch.tensor([x], device=torch.device("cuda", local), dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_config3(args, rank, world, local):
+    """Config 3: MTP verify + rollback.  128 sequences at context 8192 (per
+    GPU), nH=16, KVH=4, dh=256, P=16, one layer.  A step appends 4 draft
+    rows per sequence, attends them causally (16 query rows per kv head),
+    then truncates to len + accepted, accepted ~ U{0..4} from a seeded RNG."""
+    import torch
+    import torch.distributed as dist
+    cfg = CONFIGS[3]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    S, L = args.seqs or cfg.seqs, args.layers or cfg.layers
+    KVH, dh, G, nH, nq = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads, cfg.n_q
+    W, K = max(args.warmup, 3), max(args.steps, 64)
+    ctx = contexts(3, args.seed + 1000 * rank, S)
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, (W + K) * nq + 8, local)
+    rng = np.random.default_rng(args.seed + 17 * rank)
+    acc = rng.integers(0, nq + 1, size=(W + K, S))
+    q = torch.randn((S, nq, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    kk = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    vv = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    out = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
+    lens = ctx.copy()
+    lens_at = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+    fours = [nq] * S
+
+    def step(i, ti):
+        nonlocal lens
+        for layer in range(L):
+            pools[layer].append(ids[layer], fours, kk, vv)
+            if ti is not None:
+                ev[ti * L + layer][0].record()
+            pools[layer].attend(ids[layer], nq, G, q, out=out)
+            if ti is not None:
+                ev[ti * L + layer][1].record()
+        if ti is not None:
+            lens_at.append(lens + nq)
+        lens = lens + acc[i]
+        for layer in range(L):
+            pools[layer].truncate(ids[layer], lens)
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    launch_ms = max_over_ranks(torch, dist, world, local, launch_ms)
+    bpl = statistics.mean(decode_bytes(la, cfg) for la in lens_at)
+    hbm, kind = peaks()
+    for p in pools:
+        assert p.device_status() == 0
+    if rank != 0:
+        return
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "MTP verify+rollback: draft tokens verified/s (config 3)",
+        "value": S * nq * world / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {"workload": f"config3: {S} seqs/GPU at ctx 8192, {L} layer, 4 drafts appended + causal "
+                               "attend (16 rows/kv head, split-K mma.sync kernel), truncate to len+U{0..4}",
+                   "kv_heads": KVH, "n_heads": nH, "head_dim": dh, "page_tokens": cfg.page_tokens,
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA> (n_q=4)",
+                     "bytes_per_launch": bpl, "launch_ms": launch_ms},
+        "accepted_draft_tok_per_s": float(acc[W:].sum() * world / (K * ms * 1e-3)),
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * L * 2, "clocks": clk}), flush=True)
+
+
+def chunk_flops(ctx_before, n_q, cfg):
+    """QK^T + P.V flops of one chunk launch: row s of a sequence sees
+    ctx_before + s + 1 keys, for every query head."""
+    f = 0.0
+    for c in ctx_before:
+        keys = n_q * (int(c) + 1) + n_q * (n_q - 1) / 2
+        f += cfg.n_heads * keys * cfg.head_dim * 4
+    return f
+
+
+def run_config4(args, rank, world, local):
+    """Config 4: prefill-chunk ingest.  32 sequences (per GPU) with a seeded
+    16384-token context each ingest a 4096-token chunk per layer (append +
+    causal chunk attention on the tcgen05 kernel), 8 layers, nH=16, KVH=4,
+    dh=256, P=16; the chunk is truncated away after each step so every step
+    has the same shape."""
+    import torch
+    import torch.distributed as dist
+    cfg = CONFIGS[4]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    S, L = args.seqs or cfg.seqs, args.layers or cfg.layers
+    KVH, dh, G, nH, nq = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads, cfg.n_q
+    W, K = max(args.warmup, 3), min(args.steps, 5)
+    ctx = contexts(4, args.seed + 1000 * rank, S)
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, nq + 16, local, distinct=False)
+    q = torch.randn((S, nq, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    kk = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    vv = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    out = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+    rows = [nq] * S
+
+    def step(i, ti):
+        for layer in range(L):
+            pools[layer].append(ids[layer], rows, kk, vv)
+            if ti is not None:
+                ev[ti * L + layer][0].record()
+            pools[layer].attend(ids[layer], nq, G, q, out=out)
+            if ti is not None:
+                ev[ti * L + layer][1].record()
+            pools[layer].truncate(ids[layer], ctx)
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
+    fl = chunk_flops(ctx, nq, cfg)
+    peak, kind = tensor_peak(sustained=True)
+    for p in pools:
+        assert p.device_status() == 0
+    if rank != 0:
+        return
+    achieved = fl / (launch_ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "prefill chunk ingest tok/s (config 4)", "value": S * nq * world / (ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 x fp16 -> fp32 (tcgen05 kind::f16)",
+        "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {"workload": f"config4: {S} seqs/GPU x {L} layers, 16384-token context + 4096-token chunk "
+                               "(append + causal chunk attention)", "kv_heads": KVH, "n_heads": nH,
+                   "head_dim": dh, "page_tokens": cfg.page_tokens, "l2": "inputs larger than L2"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
+                     "traffic": None, "kernel": "chunk_kernel<256>", "flops_per_launch": fl,
+                     "launch_ms": launch_ms},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * L * 2, "clocks": clk}), flush=True)
+
+
+def run_config5(args, rank, world, local):
+    """Config 5: long-context sharded decode.  The job is 512 sequences with
+    contexts log-uniform in [4096, 131072] (8 layers, nH=16, KVH=4, dh=256,
+    P=16, ~0.6 TB of KV).  Sequences are token-balanced over 8 shards (greedy
+    LPT); rank r runs shard r % 8 -- the whole job at 8 GPUs, the per-GPU
+    shard of the 8-way partition at 1/2/4 GPUs (weak scaling).  One step =
+    per layer append 1 + decode attend; no collective on the hot path."""
+    import torch
+    import torch.distributed as dist
+    from gadeon_b200.workload import lpt_partition
+    cfg = CONFIGS[5]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = args.layers or cfg.layers
+    KVH, dh, G, nH = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads
+    W, K = max(args.warmup, 3), min(args.steps, 50)
+    job = contexts(5, args.seed, cfg.seqs)
+    shards = lpt_partition(job, 8)
+    mine = shards[rank % 8]
+    if args.seqs:
+        mine = mine[: args.seqs]
+    ctx = job[mine]
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, W + K + 4, local, factor=1.02,
+                                 distinct=False)
+    S = len(ctx)
+    q = torch.randn((S, 1, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    kk = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    vv = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+    ones = [1] * S
+
+    def step(i, ti):
+        for layer in range(L):
+            pools[layer].append(ids[layer], ones, kk, vv)
+            if ti is not None:
+                ev[ti * L + layer][0].record()
+            pools[layer].attend(ids[layer], 1, G, q, out=outs[layer])
+            if ti is not None:
+                ev[ti * L + layer][1].record()
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
+    bpl = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K))
+    hbm, kind = peaks()
+    gather_ms = None
+    if world > 1:
+        flat = torch.cat([o.reshape(-1) for o in outs])
+        n_max = int(max_over_ranks(torch, dist, world, local, flat.numel()))
+        padded = torch.zeros(n_max, dtype=flat.dtype, device=dev)
+        padded[: flat.numel()] = flat
+        gathered = torch.empty(world * n_max, dtype=flat.dtype, device=dev)
+        dist.all_gather_into_tensor(gathered, padded)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(10):
+            dist.all_gather_into_tensor(gathered, padded)
+        g1.record()
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(torch, dist, world, local, g0.elapsed_time(g1) / 10)
+    tok_sum = max_over_ranks(torch, dist, world, local, float(ctx.sum()))
+    for p in pools:
+        assert p.device_status() == 0
+    if rank != 0:
+        return
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
+    loads = [int(job[s].sum()) for s in shards]
+    print(json.dumps({
+        "metric": "long-context sharded decode tok/s (config 5)", "value": S * world / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak" if world < 8 else "strong (full job)", "vs_baseline": None,
+        "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {"workload": f"config5: shard {rank % 8} of an 8-way LPT partition of 512 seqs "
+                               f"(ctx log-U[4096,131072]); {S} seqs/GPU x {L} layers",
+                   "kv_gb_per_gpu": float(ctx.sum()) * L * KVH * dh * 4 / 1e9,
+                   "shard_tokens_max_over_mean": max(loads) / (sum(loads) / len(loads)),
+                   "max_rank_shard_tokens": tok_sum, "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA>",
+                     "bytes_per_launch": bpl, "launch_ms": launch_ms},
+        "gather_ms_per_step": gather_ms, "cpu_baseline": None, "e2e": None, "gpu_launches": K * L * 2,
+        "clocks": clk}), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.config != 2:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "reference arm is measured on config 2"}))
+            return
         run_reference(args, rank, world)
         return
     if world > 1:
@@ -375,7 +693,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        run_ours(args, rank, world, local)
+        runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5}[args.config]
+        runner(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
