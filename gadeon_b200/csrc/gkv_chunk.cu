@@ -11,24 +11,29 @@
 //
 // One CTA owns one (sequence, kv head, block of qtok = 128/G query tokens):
 // its M = 128 rows are the qtok tokens x G query heads of the kv head, so
-// every K/V tile it stages feeds all G heads.  Warp roles:
-//   warps 0-3  softmax: thread r owns row r.  It reads its S row from tensor
-//              memory, applies the causal mask and the online softmax (exp2
-//              domain), writes P (fp16) to shared memory for the P.V MMA.
-//              The running max is raised only when it grows by more than
-//              2^8; only then is that row of O rescaled in tensor memory.
-//   warp 4     TMA loads of K tiles (64 keys; box = one page's rows) into an
-//              NS-stage ring.
-//   warp 5     TMA loads of V tiles into their own NS-stage ring.
+// every K/V tile it stages feeds all G heads.  Keys are walked in tiles of
+// 128 (two 64-key halves).  Warp roles:
+//   warps 0-3  softmax: thread r owns row r.  It stages its Q row in tensor
+//              memory (the A operand of Q K^T), reads its S row (128 keys)
+//              from tensor memory, applies the causal mask and the online
+//              softmax (exp2 domain), writes P (fp16) to shared memory for
+//              the P.V MMA.  The running max is raised only when it grows by
+//              more than 2^8; only then is that row of O rescaled in tensor
+//              memory.
+//   warp 4     TMA loads of K halves into a 4-stage ring whose stages are
+//              stacked per 64-column block, so the two halves of a tile form
+//              one 128-row operand with a uniform stride.
+//   warp 5     TMA loads of V halves into a 2-stage ring.
 //   warp 6     owns tensor memory; one thread issues S = Q K^T
-//              (tcgen05.mma M=128, N=64) into a double-buffered S, and
-//              O += P V (N = dh, V read MN-major) into the fp32 O
-//              accumulator that stays in tensor memory for the whole loop.
-// Q is staged once in shared memory (128B swizzle, K-major); P is double
-// buffered, so the softmax of tile j overlaps P.V of tile j-1 and Q K^T of
-// tile j+1 on the tensor core.  Completion flows through mbarriers:
-// tcgen05.commit for tensor-core work, TMA transaction counts for loads.
-// Every wait is bounded; a timeout raises the device status word.
+//              (tcgen05.mma M=128, N=128) and O += P V (N = dh, V read
+//              MN-major, eight K=16 steps) into the fp32 O accumulator that
+//              stays in tensor memory for the whole loop.
+// Measured on B200: an N=64 tcgen05.mma costs as long as an N=128 one, so Q K^T
+// runs with N=128.  S is single-buffered (softmax releases it as soon as it
+// has read its row), so Q K^T of tile j+1 overlaps the softmax of tile j.
+// Completion flows through mbarriers: tcgen05.commit for tensor-core work,
+// TMA transaction counts for loads.  Every wait is bounded; a timeout raises
+// the device status word.
 #include <cuda_fp16.h>
 
 #include "gkv_kernels.cuh"
@@ -42,27 +47,32 @@ using namespace ptx;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kChunkThreads = (kSoftmaxWarps + 3) * 32;
 constexpr int kKWarp = 4, kVWarp = 5, kMmaWarp = 6;
-constexpr int kChunkRows = 128;  // tcgen05 M
-constexpr int kChunkKeys = 64;   // keys per tile (tcgen05 N of QK^T)
+constexpr int kChunkRows = 128;   // tcgen05 M
+constexpr int kHalf = 64;         // keys per TMA stage
+constexpr int kTile = 2 * kHalf;  // keys per tile (tcgen05 N of Q K^T)
+constexpr int kKStages = 4;       // K ring: two tiles of two halves
+constexpr int kVStages = 2;       // V ring: the two halves of one tile
 constexpr uint32_t kTmemMaxCols = 512;  // tensor memory columns per SM
 
 template <int DH>
 struct ChunkCfg {
     static constexpr int NCB = DH / 64;
-    static constexpr int NS = DH >= 256 ? 2 : (DH >= 128 ? 3 : 4);  // K and V ring stages
-    static constexpr int Q_BYTES = kChunkRows * DH * 2;
-    static constexpr int KT_BYTES = kChunkKeys * DH * 2;
-    static constexpr int P_BYTES = kChunkRows * kChunkKeys * 2;
-    static constexpr int OFF_K = Q_BYTES;
-    static constexpr int OFF_V = OFF_K + NS * KT_BYTES;
-    static constexpr int OFF_P = OFF_V + NS * KT_BYTES;
-    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-    static constexpr int NBARS = 4 * NS + 8;
+    static constexpr int HALF_BYTES = kHalf * DH * 2;               // one 64-key stage
+    static constexpr int KCB_STRIDE = kKStages * kHalf * 128;       // K column-block stride
+    static constexpr int P_BYTES = kChunkRows * kTile * 2;          // two 64-key atoms
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = OFF_K + kKStages * HALF_BYTES;
+    static constexpr int OFF_P = OFF_V + kVStages * HALF_BYTES;
+    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    static constexpr int NBARS = 2 + 2 + 2 + 2 + 4;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
-    static constexpr uint32_t O_COL = 2 * kChunkKeys;
-    // S[2] + O columns, rounded up to the power of two tcgen05.alloc takes
-    static constexpr uint32_t TMEM_COLS = O_COL + DH <= 256 ? 256 : 512;
-    static_assert(O_COL + DH <= TMEM_COLS, "S and O fit tensor memory");
+    // Tensor memory: S (128 fp32 columns), O (dh fp32 columns), Q (dh fp16 =
+    // dh/2 columns, the A operand of Q K^T).
+    static constexpr uint32_t O_COL = kTile;
+    static constexpr uint32_t Q_COL = O_COL + DH;
+    static constexpr uint32_t USED_COLS = Q_COL + DH / 2;
+    static constexpr uint32_t TMEM_COLS = USED_COLS <= 256 ? 256 : 512;
+    static_assert(USED_COLS <= TMEM_COLS, "S, O and Q fit tensor memory");
     // Co-resident CTAs must not ask for more than the SM's 512 columns,
     // else tcgen05.alloc would wait for a neighbour to finish: pad the
     // shared-memory request so at most 512 / TMEM_COLS CTAs fit on an SM.
@@ -76,20 +86,19 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     chunk_kernel(const __grid_constant__ ChunkParams p, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv) {
     using C = ChunkCfg<DH>;
-    constexpr int TK = kChunkKeys, M = kChunkRows, NS = C::NS;
+    constexpr int M = kChunkRows, TT = kTile, H = kHalf;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-    uint64_t *k_full = bars;              // [NS] TMA -> MMA
-    uint64_t *k_empty = bars + NS;        // [NS] MMA commit -> K loader
-    uint64_t *v_full = bars + 2 * NS;     // [NS]
-    uint64_t *v_empty = bars + 3 * NS;    // [NS]
-    uint64_t *s_full = bars + 4 * NS;     // [2] MMA commit -> softmax
-    uint64_t *s_free = s_full + 2;        // [2] softmax warps -> MMA
-    uint64_t *p_full = s_full + 4;        // [2] softmax warps -> MMA
-    uint64_t *p_free = s_full + 6;        // [2] MMA commit (P.V done) -> softmax
+    uint64_t *k_full = bars;        // [2] per tile slot: TMA -> MMA
+    uint64_t *k_empty = bars + 2;   // [2] MMA commit -> K loader
+    uint64_t *v_full = bars + 4;    // [2] per V stage
+    uint64_t *v_empty = bars + 6;   // [2]
+    uint64_t *s_full = bars + 8;    // MMA commit -> softmax
+    uint64_t *s_free = bars + 9;    // softmax warps -> MMA
+    uint64_t *p_full = bars + 10;   // softmax warps -> MMA
+    uint64_t *p_free = bars + 11;   // MMA commit (P.V done) -> softmax
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -101,21 +110,14 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     const int p0 = e.len - p.n_q;
     const int t_lo = qb * p.qtok, t_hi = min(p.n_q, t_lo + p.qtok);
     const int kend = p0 + t_hi;  // keys [0, kend) feed this block
-    const int nt = (kend + TK - 1) / TK;
+    const int nt = (kend + TT - 1) / TT;
 
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&k_full[s], 1);
-            mbar_init(&k_empty[s], 1);
-            mbar_init(&v_full[s], 1);
-            mbar_init(&v_empty[s], 1);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], kSoftmaxWarps);
-            mbar_init(&p_full[i], kSoftmaxWarps);
-            mbar_init(&p_free[i], 1);
-        }
+        for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, kSoftmaxWarps);
+        mbar_init(p_full, kSoftmaxWarps);
+        mbar_init(p_free, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -126,40 +128,50 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     // K/V stages start zeroed so never-loaded slots hold finite values.
     for (int i = tid; i < (C::OFF_P - C::OFF_K) / 16; i += kChunkThreads)
         reinterpret_cast<uint4 *>(smem + C::OFF_K)[i] = make_uint4(0u, 0u, 0u, 0u);
-    // Q rows: row r = token t_lo + r / G, head kvh*G + r % G; padding rows zero.
-    for (int i = tid; i < M * (DH / 8); i += kChunkThreads) {
-        const int r = i / (DH / 8), c16 = i % (DH / 8);
-        const int t = r / G, g = r - t * G, tok = t_lo + t;
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (t < p.qtok && tok < t_hi)
-            val = *reinterpret_cast<const uint4 *>(
-                p.q + (((int64_t)b * p.n_q + tok) * nH + kvh * G + g) * DH + c16 * 8);
-        *reinterpret_cast<uint4 *>(sQ + ((c16 >> 3) * M + r) * 128 + (((c16 & 7) ^ (r & 7)) << 4)) =
-            val;
-    }
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Q into tensor memory: softmax thread r writes row r = token t_lo + r/G,
+    // head kvh*G + r%G as dh/2 packed fp16 pairs (padding rows zero).
+    if (warp < kSoftmaxWarps) {
+        const int t = tid / G, g = tid - t * G, tok = t_lo + t;
+        const bool valid = t < p.qtok && tok < t_hi;
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            p.q + (((int64_t)b * p.n_q + (valid ? tok : 0)) * nH + kvh * G + g) * DH);
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + C::Q_COL;
+#pragma unroll 1
+        for (int c0 = 0; c0 < DH / 2; c0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint4 x = valid ? src[c0 / 4 + i] : make_uint4(0u, 0u, 0u, 0u);
+                v[4 * i] = __uint_as_float(x.x);
+                v[4 * i + 1] = __uint_as_float(x.y);
+                v[4 * i + 2] = __uint_as_float(x.z);
+                v[4 * i + 3] = __uint_as_float(x.w);
+            }
+            tmem_st32(trow + c0, v);
+        }
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp == kKWarp || warp == kVWarp) {
         // ============================================ TMA producers (lane 0)
         if (lane == 0) {
             const bool is_k = warp == kKWarp;
             const CUtensorMap *map = is_k ? &tmk : &tmv;
-            uint64_t *full = is_k ? k_full : v_full;
-            uint64_t *empty = is_k ? k_empty : v_empty;
-            uint8_t *ring = smem + (is_k ? C::OFF_K : C::OFF_V);
             const int lP = __ffs(p.P) - 1;
-            const int bh = min(p.P, TK);
+            const int bh = min(p.P, H);
             const int32_t *trow = p.table + (int64_t)e.seq_id * p.table_stride;
-            for (int j = 0; j < nt; ++j) {
-                const int s = j % NS;
-                if (j >= NS && !mbar_wait(&empty[s], ((j / NS) - 1) & 1, abort_flag, p.status)) break;
-                const int t0 = j * TK;
-                const int ngroups = (min(TK, kend - t0) + bh - 1) / bh;
-                mbar_expect_tx(&full[s], (uint32_t)(ngroups * bh * DH * 2));
+            // one 64-key half: rows [t0, t0+H) of the sequence into dst
+            // (row stride 128 B, column blocks cb_stride apart)
+            auto load_half = [&](uint8_t *dst, int cb_stride, uint64_t *bar, int t0) {
+                const int ngroups = (max(0, min(H, kend - t0)) + bh - 1) / bh;
                 for (int g = 0; g < ngroups; ++g) {
                     const int tg = t0 + g * bh;
                     int pid = __ldg(trow + (tg >> lP));
@@ -170,50 +182,76 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                     const int row0 = (pid * KVH + kvh) * p.P + (tg & (p.P - 1));
 #pragma unroll
                     for (int cb = 0; cb < C::NCB; ++cb)
-                        tma_load_2d(smem_u32(ring + s * C::KT_BYTES) + (uint32_t)(cb * TK * 128 + g * bh * 128),
-                                    map, cb * 64, row0, &full[s]);
+                        tma_load_2d(smem_u32(dst) + (uint32_t)(cb * cb_stride + g * bh * 128), map, cb * 64,
+                                    row0, bar);
+                }
+                return ngroups * bh * DH * 2;
+            };
+            auto half_bytes = [&](int t0) { return ((max(0, min(H, kend - t0)) + bh - 1) / bh) * bh * DH * 2; };
+            for (int j = 0; j < nt; ++j) {
+                if (is_k) {
+                    const int slot = j & 1;
+                    if (j >= 2 && !mbar_wait(&k_empty[slot], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
+                    const int t0 = j * TT;
+                    mbar_expect_tx(&k_full[slot], (uint32_t)(half_bytes(t0) + half_bytes(t0 + H)));
+                    for (int h = 0; h < 2; ++h)
+                        load_half(smem + C::OFF_K + (slot * 2 + h) * H * 128, C::KCB_STRIDE, &k_full[slot],
+                                  t0 + h * H);
+                } else {
+                    bool ok = true;
+                    for (int h = 0; h < 2 && ok; ++h) {
+                        if (j >= 1 && !mbar_wait(&v_empty[h], (j - 1) & 1, abort_flag, p.status)) ok = false;
+                        if (!ok) break;
+                        const int t0 = j * TT + h * H;
+                        mbar_expect_tx(&v_full[h], (uint32_t)half_bytes(t0));
+                        load_half(smem + C::OFF_V + h * C::HALF_BYTES, H * 128, &v_full[h], t0);
+                    }
+                    if (!ok) break;
                 }
             }
         }
     } else if (warp == kMmaWarp) {
         // ============================================ MMA issue (lane 0)
         if (lane == 0) {
-            constexpr uint32_t IDESC_QK = umma_idesc_f16(M, TK, 0);
+            constexpr uint32_t IDESC_QK = umma_idesc_f16(M, TT, 0);
             constexpr uint32_t IDESC_PV = umma_idesc_f16(M, DH, 1);
             auto issue_pv = [&](int i) -> bool {
-                if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, abort_flag, p.status)) return false;
-                if (!mbar_wait(&v_full[i % NS], (i / NS) & 1, abort_flag, p.status)) return false;
-                tc_fence_after();
-                const uint32_t sV = smem_u32(smem + C::OFF_V + (i % NS) * C::KT_BYTES);
-                const uint32_t sP = smem_u32(smem + C::OFF_P + (i & 1) * C::P_BYTES);
+                if (!mbar_wait(p_full, i & 1, abort_flag, p.status)) return false;
+                const int halves = min(2, (kend - i * TT + H - 1) / H);
+                for (int h = 0; h < halves; ++h) {
+                    if (!mbar_wait(&v_full[h], i & 1, abort_flag, p.status)) return false;
+                    tc_fence_after();
+                    const uint32_t sV = smem_u32(smem + C::OFF_V + h * C::HALF_BYTES);
+                    const uint32_t sP = smem_u32(smem + C::OFF_P + h * M * 128);
 #pragma unroll
-                for (int kk = 0; kk < TK / 16; ++kk) {
-                    const uint64_t a = umma_desc_sw128(sP + kk * 32, 16, 1024);
-                    // V is MN-major: 64-column blocks TK*128 bytes apart (LBO),
-                    // 8-key groups 1024 bytes apart (SBO).
-                    const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, TK * 128, 1024);
-                    umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < H / 16; ++kk) {
+                        const uint64_t a = umma_desc_sw128(sP + kk * 32, 16, 1024);
+                        // V is MN-major: 64-column blocks H*128 bytes apart
+                        // (LBO), 8-key groups 1024 bytes apart (SBO).
+                        const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, H * 128, 1024);
+                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || h > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&v_empty[h]);
                 }
-                umma_commit(&p_free[i & 1]);
-                umma_commit(&v_empty[i % NS]);
+                if (halves < 2) umma_commit(&v_empty[1]);  // the unloaded half's stage is free too
+                umma_commit(p_free);
                 return true;
             };
             bool ok = true;
             for (int j = 0; j < nt && ok; ++j) {
-                ok = mbar_wait(&k_full[j % NS], (j / NS) & 1, abort_flag, p.status) &&
-                     (j < 2 || mbar_wait(&s_free[j & 1], ((j - 2) >> 1) & 1, abort_flag, p.status));
+                ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, abort_flag, p.status) &&
+                     (j < 1 || mbar_wait(s_free, (j - 1) & 1, abort_flag, p.status));
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t sK = smem_u32(smem + C::OFF_K + (j % NS) * C::KT_BYTES);
+                const uint32_t sK = smem_u32(smem + C::OFF_K + (j & 1) * 2 * H * 128);
 #pragma unroll
-                for (int ks = 0; ks < DH / 16; ++ks) {
-                    const uint64_t a =
-                        umma_desc_sw128(smem_u32(sQ) + (ks >> 2) * M * 128 + (ks & 3) * 32, 16, 1024);
-                    const uint64_t bd = umma_desc_sw128(sK + (ks >> 2) * TK * 128 + (ks & 3) * 32, 16, 1024);
-                    umma_f16(tmem + (uint32_t)((j & 1) * TK), a, bd, IDESC_QK, ks > 0);
+                for (int ks = 0; ks < DH / 16; ++ks) {  // A = Q from tensor memory, 8 columns per K=16
+                    const uint64_t bd =
+                        umma_desc_sw128(sK + (ks >> 2) * C::KCB_STRIDE + (ks & 3) * 32, 16, 1024);
+                    umma_f16_ts(tmem, tmem + C::Q_COL + ks * 8, bd, IDESC_QK, ks > 0);
                 }
-                umma_commit(&s_full[j & 1]);
-                umma_commit(&k_empty[j % NS]);
+                umma_commit(s_full);
+                umma_commit(&k_empty[j & 1]);
                 if (j >= 1) ok = issue_pv(j - 1);
             }
             if (ok) issue_pv(nt - 1);
@@ -226,37 +264,44 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         const bool row_valid = tr < p.qtok && tok < t_hi;
         const int lim = row_valid ? p0 + tok : p0;  // last visible key
         const int all_visible = p0 + t_lo;           // keys <= this are visible to every row
+        const float sl = p.scale_log2;
+        const float sgn = sl >= 0.f ? 1.f : -1.f;
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
-            const int sb = j & 1;
-            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, p.status)) {
+            if (!mbar_wait(s_full, j & 1, abort_flag, p.status)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sa[32], sc[32];  // keys t0..t0+31 and t0+32..t0+63
-            tmem_ld32(tmem_row + (uint32_t)(sb * TK), sa);
-            tmem_ld32(tmem_row + (uint32_t)(sb * TK + 32), sc);
+            float s[TT];  // this row's 128 raw scores
+#pragma unroll
+            for (int q4 = 0; q4 < TT / 32; ++q4) {
+                float (&part)[32] = *reinterpret_cast<float (*)[32]>(&s[q4 * 32]);
+                tmem_ld32(tmem_row + (uint32_t)(q4 * 32), part);
+            }
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[sb]);
+            if (lane == 0) mbar_arrive(s_free);
 
-            const int t0 = j * TK;
-            const bool masked = t0 + TK - 1 > all_visible;
-            float mt = -INFINITY;
+            const int t0 = j * TT;
+            if (t0 + TT - 1 > all_visible) {
+                // masked keys become -inf * sign(scale) so scale * s = -inf
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                float va = sa[c] * p.scale_log2, vc = sc[c] * p.scale_log2;
-                if (masked) {
-                    if (t0 + c > lim) va = -INFINITY;
-                    if (t0 + 32 + c > lim) vc = -INFINITY;
-                }
-                sa[c] = va;
-                sc[c] = vc;
-                mt = fmaxf(mt, fmaxf(va, vc));
+                for (int c = 0; c < TT; ++c)
+                    if (t0 + c > lim) s[c] = -INFINITY * sgn;
             }
+            // extreme of the raw scores (max for scale > 0), 8 chains
+            float ex[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ex[u] = s[u] * sgn;
+#pragma unroll
+            for (int c = 8; c < TT; ++c) ex[c & 7] = fmaxf(ex[c & 7], s[c] * sgn);
+            const float e01 = fmaxf(ex[0], ex[1]), e23 = fmaxf(ex[2], ex[3]);
+            const float e45 = fmaxf(ex[4], ex[5]), e67 = fmaxf(ex[6], ex[7]);
+            const float ext = fmaxf(fmaxf(e01, e23), fmaxf(e45, e67)) * sgn;
+            const float mt = ext == -INFINITY * sgn ? -INFINITY : ext * sl;
             const float m_new = fmaxf(m_ref, mt);
             const bool raise = m_new > m_ref + 8.f;  // lazy: keep m_ref unless it grew by > 2^8
             float factor = 1.f;
@@ -264,70 +309,72 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 factor = m_ref == -INFINITY ? 0.f : fast_exp2(m_ref - m_new);
                 m_ref = m_new;
             }
-            const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-            if (j >= 1 && __any_sync(0xffffffffu, raise)) {
-                // O rows move to the new max: wait for P.V of tile j-1 first.
-                if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status)) {
+            const float nmu = m_ref == -INFINITY ? 0.f : -m_ref;
+            if (j >= 1) {
+                // P.V of tile j-1 must be done before P is rewritten or O rescaled.
+                if (!mbar_wait(p_free, (j - 1) & 1, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                if (__any_sync(0xffffffffu, raise)) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < DH; c0 += 32) {
-                    float o[32];
-                    tmem_ld32(tmem_row + C::O_COL + c0, o);
-                    tmem_wait_ld();
+                    for (int c0 = 0; c0 < DH; c0 += 32) {
+                        float o[32];
+                        tmem_ld32(tmem_row + C::O_COL + c0, o);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= factor;
-                    tmem_st32(tmem_row + C::O_COL + c0, o);
+                        for (int i = 0; i < 32; ++i) o[i] *= factor;
+                        tmem_st32(tmem_row + C::O_COL + c0, o);
+                    }
+                    tmem_wait_st();
                 }
-                tmem_wait_st();
             }
-            // P buffer sb was read by P.V of tile j-2.
-            if (j >= 2 && !mbar_wait(&p_free[sb], ((j - 2) >> 1) & 1, abort_flag, p.status)) {
-                ok = false;
-                break;
-            }
-            uint8_t *sP = smem + C::OFF_P + sb * C::P_BYTES;
-            float ps = 0.f;
+            uint8_t *sP = smem + C::OFF_P;
+            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int ch = 0; ch < TK / 8; ++ch) {
+            for (int ch = 0; ch < TT / 8; ++ch) {  // 16-byte chunks of 8 keys
                 uint32_t w4[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const int c = (ch & 3) * 8 + 2 * u;
-                    const float x0 = ch < 4 ? sa[c] : sc[c];
-                    const float x1 = ch < 4 ? sa[c + 1] : sc[c + 1];
-                    const float a0 = fast_exp2(x0 - mu), a1 = fast_exp2(x1 - mu);
-                    ps += a0 + a1;
+                    const float a0 = fast_exp2(fmaf(s[ch * 8 + 2 * u], sl, nmu));
+                    const float a1 = fast_exp2(fmaf(s[ch * 8 + 2 * u + 1], sl, nmu));
+                    ps[(2 * u) & 7] += a0;
+                    ps[(2 * u + 1) & 7] += a1;
                     w4[u] = pack_half2(a0, a1);
                 }
-                *reinterpret_cast<uint4 *>(sP + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                // P atom (ch / 8) holds keys 64*(ch/8) .. +63 of all rows
+                *reinterpret_cast<uint4 *>(sP + (ch >> 3) * M * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) =
                     make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            l = l * factor + ps;
-            const int nkeys = min(TK, kend - t0);
-            if (nkeys < TK) {
+            l = l * factor + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+            const int nkeys = min(TT, kend - t0);
+            if (nkeys < TT) {
                 // last tile: rows past the block's end may hold stale data;
-                // P is 0 there, zero this warp's share of V too so 0*V stays 0.
-                if (!mbar_wait(&v_full[j % NS], (j / NS) & 1, abort_flag, p.status)) {
-                    ok = false;
-                    break;
+                // P is 0 there, zero V too so 0 * V stays 0.
+                for (int h = 0; h < 2; ++h) {
+                    const int valid_h = nkeys - h * H;
+                    if (valid_h <= 0 || valid_h >= H) continue;
+                    if (!mbar_wait(&v_full[h], j & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sV = smem + C::OFF_V + h * C::HALF_BYTES;
+                    for (int i = tid; i < (H - valid_h) * (DH / 8); i += kSoftmaxWarps * 32) {
+                        const int key = valid_h + i / (DH / 8), c16 = i % (DH / 8);
+                        *reinterpret_cast<uint4 *>(sV + ((c16 >> 3) * H + key) * 128 +
+                                                   (((c16 & 7) ^ (key & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+                    }
                 }
-                uint8_t *sV = smem + C::OFF_V + (j % NS) * C::KT_BYTES;
-                for (int i = tid; i < (TK - nkeys) * (DH / 8); i += kSoftmaxWarps * 32) {
-                    const int key = nkeys + i / (DH / 8), c16 = i % (DH / 8);
-                    *reinterpret_cast<uint4 *>(sV + ((c16 >> 3) * TK + key) * 128 +
-                                               (((c16 & 7) ^ (key & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-                }
+                if (!ok) break;
             }
             fence_proxy_async();  // P (and V zeroing) written by threads -> tensor core
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[sb]);
+            if (lane == 0) mbar_arrive(p_full);
         }
         // ---- epilogue: O / l for valid rows once the last P.V is done
-        if (ok && mbar_wait(&p_free[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, p.status)) {
+        if (ok && mbar_wait(p_free, (nt - 1) & 1, abort_flag, p.status)) {
             tc_fence_after();
             const float inv = 1.f / l;
             float *dst =

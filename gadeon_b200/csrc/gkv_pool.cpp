@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -636,6 +637,7 @@ int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n
     if (rc) return rc;
     rc = check_attend(pool, n_seqs, seq_ids, n_q, group, q, out);
     if (rc) return rc;
+    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
     DeviceGuard guard(pool->cfg.device);
     return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale,
                           static_cast<cudaStream_t>(stream));
@@ -647,12 +649,17 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
     if (!pool) return fail(GKV_ERR_INVALID, "null pool");
     int rc = check_batch(pool, n_seqs, seq_ids);
     if (rc) return rc;
-    if (n_q < 1 || group < 1 || (int64_t)n_q * group > 16)
-        return fail(n_q < 1 || group < 1 ? GKV_ERR_INVALID : GKV_ERR_UNSUPPORTED,
-                    "n_q=%d group=%d (n_q*group <= 16)", n_q, group);
+    if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
+    if ((int64_t)n_q * group > 16 &&
+        !gkv::chunk_supported(pool->cfg.head_dim, pool->cfg.page_tokens, group))
+        return fail(GKV_ERR_UNSUPPORTED,
+                    "n_q*group = %lld rows per kv head needs the chunk kernel (head_dim <= 256, "
+                    "page_tokens >= 8)",
+                    (long long)n_q * group);
     if (n_seqs > 0 && (!k || !v || !q || !out)) return fail(GKV_ERR_INVALID, "null k/v/q/out");
     if (!aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(out))
         return fail(GKV_ERR_INVALID, "k/v/q/out not 16-byte aligned");
+    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
     DeviceGuard guard(pool->cfg.device);
     std::vector<int32_t> n_new(n_seqs, n_q);
     std::vector<gkv::AppendEntry> entries;

@@ -143,6 +143,20 @@ def _dev_ptr(t) -> Optional[int]:
     return t.data_ptr()
 
 
+def _check_shape(name, t, shape, dtypes):
+    """The C ABI takes raw device pointers; refuse a tensor whose size or type
+    differs from what the kernel will read or write."""
+    if t is None:
+        return
+    if tuple(t.shape) != tuple(shape) and t.numel() != int(np.prod(shape)):
+        raise GkvError(GKV_ERR_INVALID, f"{name}: shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if str(t.dtype).replace("torch.", "") not in dtypes:
+        raise GkvError(GKV_ERR_INVALID, f"{name}: dtype {t.dtype}, expected one of {dtypes}")
+
+
+_F16 = ("float16", "int16", "uint16")
+
+
 def _stream_ptr(stream) -> Optional[int]:
     import torch
     if stream is None:
@@ -211,11 +225,16 @@ class BlockPool:
     def append(self, seq_ids: Sequence[int], n_new: Sequence[int], k, v, stream=None):
         """k, v: token-major [sum(n_new), kv_heads, head_dim] fp16 on the GPU."""
         ids, nn = _i32(seq_ids), _i32(n_new)
+        rows = int(np.maximum(nn, 0).sum())
+        for name, t in (("k", k), ("v", v)):
+            _check_shape(name, t, (rows, self.kv_heads, self.head_dim), _F16)
         _check(_lib.gkv_append(self._h, len(ids), _p32(ids), _p32(nn), _dev_ptr(k), _dev_ptr(v),
                                _stream_ptr(stream)))
 
     def seed(self, seq: int, K, V, count: int, stream=None):
         """K, V: head-major [kv_heads, count, head_dim] fp16; the sequence must be empty."""
+        for name, t in (("K", K), ("V", V)):
+            _check_shape(name, t, (self.kv_heads, count, self.head_dim), _F16)
         _check(_lib.gkv_seed(self._h, seq, _dev_ptr(K), _dev_ptr(V), count, _stream_ptr(stream)))
 
     def attend(self, seq_ids: Sequence[int], n_q: int, group: int, q, out=None,
@@ -224,8 +243,11 @@ class BlockPool:
         Row r of a sequence sees keys [0, length - n_q + r]."""
         import torch
         ids = _i32(seq_ids)
+        qshape = (len(ids), n_q, self.kv_heads * group, self.head_dim)
+        _check_shape("q", q, qshape, _F16)
         if out is None:
-            out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+            out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+        _check_shape("out", out, qshape, ("float32",))
         if scale is None:
             scale = self.head_dim ** -0.5
         _check(_lib.gkv_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(q),
@@ -237,8 +259,13 @@ class BlockPool:
         """Append n_q rows per sequence, then attend those n_q query rows."""
         import torch
         ids = _i32(seq_ids)
+        qshape = (len(ids), n_q, self.kv_heads * group, self.head_dim)
+        _check_shape("q", q, qshape, _F16)
+        for name, t in (("k", k), ("v", v)):
+            _check_shape(name, t, (len(ids) * n_q, self.kv_heads, self.head_dim), _F16)
         if out is None:
-            out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+            out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+        _check_shape("out", out, qshape, ("float32",))
         if scale is None:
             scale = self.head_dim ** -0.5
         _check(_lib.gkv_append_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(k),
@@ -266,6 +293,8 @@ class BlockPool:
         return K, V
 
     def from_compact(self, K, V, length: int, stream=None) -> int:
+        for name, t in (("K", K), ("V", V)):
+            _check_shape(name, t, (self.kv_heads, length, self.head_dim), _F16)
         out = C.c_int32()
         _check(_lib.gkv_from_compact(self._h, _dev_ptr(K), _dev_ptr(V), length, C.byref(out),
                                      _stream_ptr(stream)))

@@ -104,12 +104,16 @@ int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V,
  * decode (the newest query sees every key, like hostFlashDecode).
  * q: [n_seqs, n_q, kv_heads*group, head_dim] fp16 (head h = kvh*group + g,
  * PagedAttention.swift:331-332); out: same shape, fp32.
- * scale multiplies q.k (hostFlashDecode uses head_dim^-0.5, :321). */
+ * scale multiplies q.k (hostFlashDecode uses head_dim^-0.5, :321); it must
+ * be finite and non-zero.  Up to 16 rows per kv head (n_q*group <= 16) run
+ * the split-K decode/verify kernel; more rows (prefill chunks) run the
+ * tensor-core chunk kernel, which needs head_dim <= 256 and page_tokens >= 8
+ * (else GKV_ERR_UNSUPPORTED). */
 int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                int32_t n_q, int32_t group, const void *q, float *out,
                float scale, void *stream);
 
-/* One decode / verify step in one call: gkv_append of n_q rows per
+/* One decode / verify / chunk step in one call: gkv_append of n_q rows per
  * sequence followed by gkv_attend of those n_q rows. */
 int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                       int32_t n_q, int32_t group, const void *k,

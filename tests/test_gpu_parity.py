@@ -262,12 +262,20 @@ def test_bad_arguments(cuda, oracle):
         (lambda: pr.gpu.truncate([99], [0]), GKV_ERR_BAD_SEQ),
         (lambda: pr.gpu.attend([s], 4, 4, q), GKV_ERR_BAD_SEQ),       # len 3 < n_q 4
         (lambda: pr.gpu.attend([s, s], 1, 4, q), GKV_ERR_INVALID),     # duplicate id
-        (lambda: pr.gpu.attend([s], 3, 8, q), GKV_ERR_UNSUPPORTED),    # 24 rows per kv head
+        (lambda: pr.gpu.attend([s], 1, 4, q, scale=0.0), GKV_ERR_INVALID),
     ]:
         with pytest.raises(GkvError) as ei:
             call()
         assert ei.value.code == code
     pr.check_state()
+    # more than 16 rows per kv head needs the chunk kernel, which needs P >= 8
+    small = Pair(cuda, oracle, kvh=2, dh=128, P=4, num_pages=10)
+    t = small.new_seq()
+    small.append([t], [5])
+    q5 = dev_f16(cuda, oracle.normal_f16(1, 2, (1, 5, 8, 128)))
+    with pytest.raises(GkvError) as ei:
+        small.gpu.attend([t], 5, 4, q5)
+    assert ei.value.code == GKV_ERR_UNSUPPORTED
 
 
 def test_anti_vacuity_table_matters(cuda, oracle):
