@@ -1,0 +1,60 @@
+"""Sequence sharding across the GPUs of one node, and the output gather.
+
+The paged-KV path shards by sequence: every GPU owns private page pools (one
+per layer) for the sequences assigned to it, and the hot path has no
+cross-GPU traffic.  The only collective is the gather of attention outputs
+after a step, which goes over NCCL (NVLink) on GPUs and gloo in the CPU
+tests.  The reference runs on one device and has no counterpart
+(leok7v/gadeon has no multi-device code).
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import numpy as np
+
+from .workload import lpt_partition
+
+
+def assign(tokens: Sequence[int], world: int) -> List[List[int]]:
+    """Token-balanced assignment of job sequences to `world` ranks (greedy
+    LPT: contexts descending, each to the least-loaded rank)."""
+    return lpt_partition(tokens, world)
+
+
+def imbalance(tokens: Sequence[int], shards: List[List[int]]) -> float:
+    """max / mean tokens per rank (1.0 = perfectly balanced)."""
+    loads = [sum(int(tokens[i]) for i in s) for s in shards]
+    mean = sum(loads) / len(loads)
+    return max(loads) / mean if mean else 1.0
+
+
+def gather_outputs(local, shards: List[List[int]], rank: int, group=None):
+    """All-gather every rank's per-sequence outputs (rows in the order of
+    its shard) and return them in job order: a tensor [n_job, *row_shape].
+
+    Ranks hold different numbers of sequences, so each pads to the largest
+    shard before one all_gather_into_tensor (NCCL) / all_gather (gloo)."""
+    import torch
+    import torch.distributed as dist
+
+    world = len(shards)
+    n_max = max(len(s) for s in shards)
+    row_shape = tuple(local.shape[1:])
+    assert local.shape[0] == len(shards[rank]), (local.shape, len(shards[rank]))
+    padded = torch.zeros((n_max,) + row_shape, dtype=local.dtype, device=local.device)
+    padded[: local.shape[0]] = local
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world * n_max,) + row_shape, dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(out, padded, group=group)
+        parts = list(out.view((world, n_max) + row_shape))
+    else:
+        parts = [torch.empty_like(padded) for _ in range(world)]
+        dist.all_gather(parts, padded, group=group)
+    n_job = sum(len(s) for s in shards)
+    job = torch.empty((n_job,) + row_shape, dtype=local.dtype, device=local.device)
+    for r, s in enumerate(shards):
+        if s:
+            idx = torch.as_tensor(np.asarray(s, dtype=np.int64), device=local.device)
+            job[idx] = parts[r][: len(s)]
+    return job

@@ -1,0 +1,95 @@
+"""Multi-process host logic of the sequence-sharded path on CPU (gloo,
+world size 2): token-balanced assignment, the padded output gather back to
+job order, and failure detection when a rank dies before the collective
+(the failure is made on the host; no GPU is involved)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from gadeon_b200.shard import assign, imbalance
+from gadeon_b200.workload import contexts
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def test_assign_is_a_token_balanced_partition():
+    tokens = contexts(5, 123, 512)
+    for world in (1, 2, 4, 8):
+        shards = assign(tokens, world)
+        flat = sorted(i for s in shards for i in s)
+        assert flat == list(range(512))
+        assert imbalance(tokens, shards) < 1.01
+    # LPT places the longest context first, on rank 0
+    shards = assign([5, 9, 1, 7], 2)
+    assert 1 in shards[0] and shards == [[1, 2], [0, 3]]
+
+
+def _worker(rank, world, port, fail_rank, q):
+    import torch
+    import torch.distributed as dist
+
+    from gadeon_b200.shard import gather_outputs
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    tokens = [100, 900, 50, 400, 300, 700, 20]
+    shards = assign(tokens, world)
+    # each sequence's "attention output" row encodes its job index
+    local = torch.tensor([[float(i), float(i) * 2] for i in shards[rank]], dtype=torch.float32)
+    try:
+        if rank == fail_rank:
+            raise RuntimeError("rank failed before the gather")
+        job = gather_outputs(local, shards, rank)
+        q.put((rank, "ok", job.numpy().tolist()))
+    except Exception as e:  # the surviving rank must see an error, not hang
+        q.put((rank, "error", type(e).__name__))
+    finally:
+        if rank == fail_rank:
+            q.close()
+            q.join_thread()  # deliver the report before the hard exit
+            os._exit(0)  # leave without the collective
+        dist.destroy_process_group()
+
+
+def _run(world, fail_rank):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, status, payload = q.get(timeout=120)
+        results[rank] = (status, payload)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+def test_gather_outputs_job_order_gloo():
+    res = _run(2, fail_rank=-1)
+    want = [[float(i), float(i) * 2] for i in range(7)]
+    for rank in range(2):
+        status, job = res[rank]
+        assert status == "ok"
+        assert job == want
+
+
+def test_dead_rank_is_detected_by_the_collective():
+    res = _run(2, fail_rank=1)
+    assert res[1][0] == "error"
+    assert res[0][0] == "error", res  # the gather fails instead of hanging
