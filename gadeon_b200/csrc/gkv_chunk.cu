@@ -20,7 +20,7 @@
 //              the P.V MMA.  The running max is raised only when it grows by
 //              more than 2^8; only then is that row of O rescaled in tensor
 //              memory.
-//   warp 4     TMA loads of K halves into a 4-stage ring whose stages are
+//   warp 4     TMA loads of K halves (one lane per page) into a 4-stage ring whose stages are
 //              stacked per 64-column block, so the two halves of a tile form
 //              one 128-row operand with a uniform stride.
 //   warp 5     TMA loads of V halves into a 2-stage ring.
@@ -161,54 +161,66 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     tc_fence_after();
 
     if (warp == kKWarp || warp == kVWarp) {
-        // ============================================ TMA producers (lane 0)
-        if (lane == 0) {
-            const bool is_k = warp == kKWarp;
-            const CUtensorMap *map = is_k ? &tmk : &tmv;
-            const int lP = __ffs(p.P) - 1;
-            const int bh = min(p.P, H);
-            const int32_t *trow = p.table + (int64_t)e.seq_id * p.table_stride;
-            // one 64-key half: rows [t0, t0+H) of the sequence into dst
-            // (row stride 128 B, column blocks cb_stride apart)
-            auto load_half = [&](uint8_t *dst, int cb_stride, uint64_t *bar, int t0) {
-                const int ngroups = (max(0, min(H, kend - t0)) + bh - 1) / bh;
-                for (int g = 0; g < ngroups; ++g) {
-                    const int tg = t0 + g * bh;
-                    int pid = __ldg(trow + (tg >> lP));
-                    if (pid < 0 || pid >= p.num_pages) {
-                        atomicOr(p.status, DEV_ERR_BAD_PAGE);
-                        pid = 0;
-                    }
-                    const int row0 = (pid * KVH + kvh) * p.P + (tg & (p.P - 1));
-#pragma unroll
-                    for (int cb = 0; cb < C::NCB; ++cb)
-                        tma_load_2d(smem_u32(dst) + (uint32_t)(cb * cb_stride + g * bh * 128), map, cb * 64,
-                                    row0, bar);
+        // ============================================ TMA producers
+        // Lane i of the warp owns page group i of a 128-key tile (group =
+        // min(P, 64) keys of one page; half h = i / gph).  Every lane reads its
+        // block-table entry before the slot wait, in parallel, so the table
+        // latency is paid once per tile instead of once per page; then each
+        // lane issues its own group's boxes.
+        const bool is_k = warp == kKWarp;
+        const CUtensorMap *map = is_k ? &tmk : &tmv;
+        const int lP = __ffs(p.P) - 1;
+        const int bh = min(p.P, H);
+        const int gph = H / bh;  // page groups per 64-key half (<= 8: P >= 8)
+        const int32_t *trow = p.table + (int64_t)e.seq_id * p.table_stride;
+        auto half_bytes = [&](int t0) { return ((max(0, min(H, kend - t0)) + bh - 1) / bh) * bh * DH * 2; };
+        const int h_lane = lane / gph, g_lane = lane % gph;
+        for (int j = 0; j < nt; ++j) {
+            const int t0 = j * TT;
+            const int tg = t0 + h_lane * H + g_lane * bh;
+            const bool mine = lane < 2 * gph && tg < kend;
+            int row0 = 0;
+            if (mine) {
+                int pid = __ldg(trow + (tg >> lP));
+                if (pid < 0 || pid >= p.num_pages) {
+                    atomicOr(p.status, DEV_ERR_BAD_PAGE);
+                    pid = 0;
                 }
-                return ngroups * bh * DH * 2;
-            };
-            auto half_bytes = [&](int t0) { return ((max(0, min(H, kend - t0)) + bh - 1) / bh) * bh * DH * 2; };
-            for (int j = 0; j < nt; ++j) {
+                row0 = (pid * KVH + kvh) * p.P + (tg & (p.P - 1));
+            }
+            bool ok = true;
+            if (lane == 0) {
                 if (is_k) {
                     const int slot = j & 1;
-                    if (j >= 2 && !mbar_wait(&k_empty[slot], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
-                    const int t0 = j * TT;
-                    mbar_expect_tx(&k_full[slot], (uint32_t)(half_bytes(t0) + half_bytes(t0 + H)));
-                    for (int h = 0; h < 2; ++h)
-                        load_half(smem + C::OFF_K + (slot * 2 + h) * H * 128, C::KCB_STRIDE, &k_full[slot],
-                                  t0 + h * H);
+                    if (j >= 2) ok = mbar_wait(&k_empty[slot], ((j >> 1) - 1) & 1, abort_flag, p.status);
+                    if (ok) mbar_expect_tx(&k_full[slot], (uint32_t)(half_bytes(t0) + half_bytes(t0 + H)));
                 } else {
-                    bool ok = true;
                     for (int h = 0; h < 2 && ok; ++h) {
-                        if (j >= 1 && !mbar_wait(&v_empty[h], (j - 1) & 1, abort_flag, p.status)) ok = false;
-                        if (!ok) break;
-                        const int t0 = j * TT + h * H;
-                        mbar_expect_tx(&v_full[h], (uint32_t)half_bytes(t0));
-                        load_half(smem + C::OFF_V + h * C::HALF_BYTES, H * 128, &v_full[h], t0);
+                        if (j >= 1) ok = mbar_wait(&v_empty[h], (j - 1) & 1, abort_flag, p.status);
+                        if (ok) mbar_expect_tx(&v_full[h], (uint32_t)half_bytes(t0 + h * H));
                     }
-                    if (!ok) break;
                 }
             }
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            if (mine) {
+                uint8_t *dst;
+                int cb_stride;
+                uint64_t *bar;
+                if (is_k) {
+                    dst = smem + C::OFF_K + ((j & 1) * 2 + h_lane) * H * 128;
+                    cb_stride = C::KCB_STRIDE;
+                    bar = &k_full[j & 1];
+                } else {
+                    dst = smem + C::OFF_V + h_lane * C::HALF_BYTES;
+                    cb_stride = H * 128;
+                    bar = &v_full[h_lane];
+                }
+#pragma unroll
+                for (int cb = 0; cb < C::NCB; ++cb)
+                    tma_load_2d(smem_u32(dst) + (uint32_t)(cb * cb_stride + g_lane * bh * 128), map, cb * 64,
+                                row0, bar);
+            }
+            __syncwarp();
         }
     } else if (warp == kMmaWarp) {
         // ============================================ MMA issue (lane 0)
