@@ -189,7 +189,7 @@ __device__ __forceinline__ int cta_of_unit(int64_t u, int64_t units, int64_t cta
     return (int)(((u + 1) * ctas - 1) / units);
 }
 
-template <int DH, bool TMA>
+template <int DH, bool TMA, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ AttendParams p, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv) {
@@ -231,6 +231,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     UnitWalker w{p.entries, p.n_seqs, KVH, 0, 0, 0, {}};
     w.seek(u_begin, p.n_seqs);
 
+    if constexpr (FUSED) {
+        // Fused decode append, before any TMA is in flight: for every item
+        // whose last key tile (it holds the new row, position len-1) this CTA
+        // owns, write that kv head's row -- and zero the rest of its slab when
+        // the page is fresh (PagePool.zeroPage) -- then fence the stores
+        // against the TMA reads that follow.
+        UnitWalker a = w;
+        int u = u_begin;
+        while (u < u_end) {
+            const int item_last = a.e.unit_base + a.kvh * a.e.ntiles + a.e.ntiles - 1;
+            if (item_last < u_end) {
+                const FusedTail ft = p.tails[a.b];
+                const int slot = (a.e.len - 1) & (p.P - 1);
+                const int64_t slab = ((int64_t)ft.pid * KVH + a.kvh) * p.P * DH;
+                uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
+                uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
+                const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                const int rows = ft.fresh ? p.P : 1;
+                for (int i = threadIdx.x; i < rows * C::CH; i += kThreads) {
+                    const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
+                    const bool mine = row == slot;
+                    kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
+                    vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
+                }
+                if (ft.fresh && a.kvh == 0 && threadIdx.x == 0)
+                    p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx] = ft.pid;
+            }
+            // next item
+            u = item_last + 1;
+            a.j = a.e.ntiles - 1;
+            a.next();
+        }
+        fence_proxy_async_global();
+        __syncthreads();
+    }
+
     if (warp == kConsumerWarps) {
         // ================================================= producer warp
         int stage = 0;
@@ -243,10 +280,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t *sV = sK + C::TILE_BYTES;
             if constexpr (TMA) {
                 const int ngroups = (nkeys + (1 << lbh) - 1) >> lbh;
+                // fused decode append: the last tile of an item holds the new
+                // row (position len-1); its page id comes from the descriptor,
+                // since the table entry of a fresh page may be written by
+                // another CTA's prologue
+                const bool fuse_here = FUSED && w.j == w.e.ntiles - 1;
+                FusedTail ft{};
+                if constexpr (FUSED) {
+                    if (fuse_here) ft = p.tails[w.b];
+                }
                 int row0 = 0;
                 if (lane < ngroups) {  // table read before the wait hides its latency
                     const int tg = t0 + (lane << lbh);
-                    int pid = __ldg(trow + (tg >> lP));
+                    int pid;
+                    if (fuse_here && (tg >> lP) == ft.pidx) pid = ft.pid;
+                    else pid = __ldg(trow + (tg >> lP));
                     if (pid < 0 || pid >= p.num_pages) {
                         atomicOr(p.status, DEV_ERR_BAD_PAGE);
                         pid = 0;
@@ -580,10 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int DH, bool TMA>
+template <int DH, bool TMA, bool FUSED = false>
 cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                             int grid, cudaStream_t s) {
-    auto kern = attend_kernel<DH, TMA>;
+    auto kern = attend_kernel<DH, TMA, FUSED>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -635,9 +683,11 @@ cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tk, const CU
     switch (dh) {
         case 64: return tma ? launch_attend_t<64, true>(p, tk, tv, grid, s)
                             : launch_attend_t<64, false>(p, tk, tv, grid, s);
-        case 128: return tma ? launch_attend_t<128, true>(p, tk, tv, grid, s)
+        case 128: return tma ? (p.tails ? launch_attend_t<128, true, true>(p, tk, tv, grid, s)
+                                        : launch_attend_t<128, true>(p, tk, tv, grid, s))
                              : launch_attend_t<128, false>(p, tk, tv, grid, s);
-        case 256: return tma ? launch_attend_t<256, true>(p, tk, tv, grid, s)
+        case 256: return tma ? (p.tails ? launch_attend_t<256, true, true>(p, tk, tv, grid, s)
+                                        : launch_attend_t<256, true>(p, tk, tv, grid, s))
                              : launch_attend_t<256, false>(p, tk, tv, grid, s);
         case 512: return tma ? launch_attend_t<512, true>(p, tk, tv, grid, s)
                              : launch_attend_t<512, false>(p, tk, tv, grid, s);

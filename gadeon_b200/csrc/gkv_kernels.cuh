@@ -59,10 +59,25 @@ struct AttendEntry {
     int32_t ntiles;     // key tiles per kv head = ceil(len / TK)
 };
 
+// Fused decode append: where sequence b's new row (position len-1) goes.
+struct FusedTail {
+    int32_t pid;   // physical page holding position len-1
+    int32_t pidx;  // its logical index in the sequence
+    int32_t fresh; // 1: the page was just allocated (zero-fill + table entry)
+    int32_t pad;
+};
+
 struct AttendParams {
     const AttendEntry *entries;
     int32_t n_seqs;
     int32_t total_units;
+    // fused decode append (null when the rows were appended beforehand):
+    // k_new/v_new [n_seqs, KVH, dh] fp16, written into the pool before the
+    // last key tile of each (sequence, kv head) is loaded
+    const FusedTail *tails;
+    const uint16_t *k_new, *v_new;
+    uint16_t *k_pool_w, *v_pool_w;
+    int32_t *table_w;
     const int32_t *table;
     int32_t table_stride;
     const uint16_t *k_pool;  // used by the cp.async loader (P < 8)

@@ -323,12 +323,17 @@ int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_
     return GKV_OK;
 }
 
+// tails != null: single-token decode with the append fused into the attend
+// kernel (k_new / v_new hold each sequence's new row).
 int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
-                   const void *q, float *out, float scale, cudaStream_t st) {
+                   const void *q, float *out, float scale, cudaStream_t st,
+                   const gkv::FusedTail *tails = nullptr, const void *k_new = nullptr,
+                   const void *v_new = nullptr) {
     if (n == 0) return GKV_OK;
     const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
     cudaError_t err;
-    const size_t bytes = (size_t)n * sizeof(gkv::AttendEntry);
+    const size_t ebytes = ((size_t)n * sizeof(gkv::AttendEntry) + 255) & ~size_t(255);
+    const size_t bytes = tails ? ebytes + (size_t)n * sizeof(gkv::FusedTail) : (size_t)n * sizeof(gkv::AttendEntry);
     const int slot = pool->staging.acquire(bytes, &err);
     if (slot < 0) return cuda_fail(err, "descriptor staging");
     auto *ent = reinterpret_cast<gkv::AttendEntry *>(pool->staging.host(slot));
@@ -363,9 +368,18 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         return GKV_OK;
     }
     if (units > INT32_MAX) return fail(GKV_ERR_CAPACITY, "too many key tiles in one call");
+    if (tails) memcpy(pool->staging.host(slot) + ebytes, tails, (size_t)n * sizeof(gkv::FusedTail));
     GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
     gkv::AttendParams p{};
     p.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
+    if (tails) {
+        p.tails = reinterpret_cast<const gkv::FusedTail *>(pool->staging.dev(slot) + ebytes);
+        p.k_new = static_cast<const uint16_t *>(k_new);
+        p.v_new = static_cast<const uint16_t *>(v_new);
+        p.k_pool_w = pool->d_k;
+        p.v_pool_w = pool->d_v;
+        p.table_w = pool->d_table;
+    }
     p.n_seqs = n;
     p.total_units = (int32_t)units;
     p.table = pool->d_table;
@@ -667,6 +681,19 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Single-token decode with TMA-staged pages and no shared tail page: the
+    // append rides inside the attend kernel (one launch per layer).  Each
+    // sequence then touched exactly one page, in batch order.
+    bool fuse = n_q == 1 && pool->cfg.page_tokens >= 8 &&
+                (pool->cfg.head_dim == 128 || pool->cfg.head_dim == 256) && (int32_t)pages.size() == n_seqs;
+    for (size_t i = 0; fuse && i < pages.size(); ++i)
+        fuse = pages[i].entry == (int32_t)i && pages[i].src_pid < 0;
+    if (fuse) {
+        std::vector<gkv::FusedTail> tails(n_seqs);
+        for (int32_t i = 0; i < n_seqs; ++i)
+            tails[i] = {pages[i].pid, pages[i].pidx, pages[i].src_pid == gkv::PAGE_NEW ? 1 : 0, 0};
+        return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st, tails.data(), k, v);
+    }
     rc = enqueue_append(pool, entries, pages, k, v, 0, st);
     if (rc) return rc;
     return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st);

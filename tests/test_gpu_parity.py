@@ -131,6 +131,32 @@ def test_config1_prefill_then_decode(cuda, oracle):
     assert pr.gpu.length(s) == 640
 
 
+@pytest.mark.parametrize("P,dh", [(8, 256), (16, 256), (16, 128), (64, 256), (128, 128)])
+def test_fused_decode_append(cuda, oracle, P, dh):
+    """gkv_append_attend with n_q = 1 writes the new rows inside the attend
+    kernel: page contents, tables and free list stay bit-exact step after
+    step, across fresh pages and pages larger than the key tile; a shared
+    (cloned) tail page falls back to the two-kernel path."""
+    torch = cuda
+    G = 4
+    pr = Pair(cuda, oracle, kvh=2, dh=dh, P=P, num_pages=600, seed=31)
+    ids = [pr.new_seq() for _ in range(5)]
+    pr.append(ids, [1, P - 1, P, 3 * P + 2, 700])
+    for step in range(2 * P + 3):
+        if step == 5:  # share a partial tail: the next append copies it first
+            c = pr.gpu.clone(ids[3])
+            assert pr.orc.clone(ids[3]) == c
+            pr.seqs.append(c)
+            ids.append(c)
+        k, v = pr.rows(len(ids))
+        q = oracle.normal_f16(17, step, (len(ids), 1, 2 * G, dh))
+        got = pr.gpu.append_attend(ids, 1, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+        assert pr.orc.append(ids, [1] * len(ids), k, v) == 0
+        want = pr.orc.attend_causal(ids, 1, q, G, dh ** -0.5)
+        assert_attn_close(got.cpu().numpy(), want, f"fused step {step}")
+        pr.check_state(pages=(step % 4 == 0 or step > 2 * P))
+
+
 def test_batched_ragged_decode(cuda, oracle):
     """Config-2 shape (nH=8, KVH=2, dh=256, P=16) with ragged contexts that
     split across many CTAs (the partial-merge path) and tiny ones."""
