@@ -64,9 +64,10 @@ def parse_args():
     # a line measured with them is not the config-2 number
     ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: config 2's 6)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6],
                     help="BASELINE config: 2 decode (default, the headline), 3 MTP verify+rollback, "
-                         "4 prefill chunk, 5 long-context sharded decode")
+                         "4 prefill chunk, 5 long-context sharded decode; 6 = the GDN state rollback "
+                         "that runs beside config 3's truncate")
     return ap.parse_args()
 
 
@@ -621,20 +622,18 @@ def run_config5(args, rank, world, local):
     vv = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
-    ones = [1] * S
-
     def step(i, ti):
+        # one public call per layer: the append rides inside the attend kernel
         for layer in range(L):
-            pools[layer].append(ids[layer], ones, kk, vv)
             if ti is not None:
                 ev[ti * L + layer][0].record()
-            pools[layer].attend(ids[layer], 1, G, q, out=outs[layer])
+            pools[layer].append_attend(ids[layer], 1, G, kk, vv, q, out=outs[layer])
             if ti is not None:
                 ev[ti * L + layer][1].record()
 
     ms, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
-    bpl = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K))
+    bpl = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K)) + append_bytes(S, cfg)
     hbm, kind = peaks()
     gather_ms = None
     if world > 1:
@@ -670,10 +669,87 @@ def run_config5(args, rank, world, local):
                    "shard_tokens_max_over_mean": max(loads) / (sum(loads) / len(loads)),
                    "max_rank_shard_tokens": tok_sum, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA>",
+                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append>",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms},
-        "gather_ms_per_step": gather_ms, "cpu_baseline": None, "e2e": None, "gpu_launches": K * L * 2,
+        "gather_ms_per_step": gather_ms, "cpu_baseline": None, "e2e": None, "gpu_launches": K * L,
         "clocks": clk}), flush=True)
+
+
+def run_config6(args, rank, world, local):
+    """GDN rollback beside config 3: per step, every one of 128 sequences
+    (per GPU) rolls back the recurrent state and conv tail of its 3 GDN
+    layers to an accepted length m ~ U{1..5} (seeded).  One state launch and
+    one conv launch cover all (sequence, layer) items; fp32 state, inputs
+    far larger than L2."""
+    import torch
+    import torch.distributed as dist
+    import gadeon_b200 as gk
+    from gadeon_b200.workload import GDN, rollback_bytes
+    g = GDN
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = (args.seqs or g.seqs) * (args.layers or g.layers)
+    H, D, Cw, CD, T = g.value_heads, g.head_dim, g.chunk, g.conv_dim, g.taps
+    W, K = max(args.warmup, 3), max(args.steps, 50)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 31 * rank)
+    s0 = torch.randn((n, H, D, D), generator=gen, device=dev) * 0.1
+    out = torch.empty_like(s0)
+    kk = torch.randn((n, H, Cw, D), generator=gen, device=dev) / math.sqrt(D)
+    delta = torch.randn((n, H, Cw, D), generator=gen, device=dev) * 0.5
+    gcum = torch.cumsum(-torch.rand((n, H, Cw), generator=gen, device=dev) * 0.7, dim=-1)
+    proj = torch.randn((n, Cw, CD), generator=gen, device=dev)
+    pre = torch.randn((n, CD, T), generator=gen, device=dev)
+    conv = torch.empty_like(pre)
+    rng = np.random.default_rng(args.seed + 17 * rank)
+    ms_acc = rng.integers(1, Cw + 1, size=(W + K, n)).astype(np.int32)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+
+    def step(i, ti):
+        if ti is not None:
+            ev[ti][0].record()
+        gk.mtp_rollback(ms_acc[i], s0, delta, kk, gcum, out=out)
+        if ti is not None:
+            ev[ti][1].record()
+        gk.conv_rollback(ms_acc[i], proj, pre, out=conv)
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
+    bpl = statistics.mean(rollback_bytes(ms_acc[W + i], g)[0] for i in range(K))
+    step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g)) for i in range(K))
+    hbm, kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        ns = 8
+        a = [x[:ns].cpu().numpy() for x in (s0, delta, kk, gcum)]
+        mm = ms_acc[0, :ns]
+        O.mtp_rollback(mm, *a)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0:
+            O.mtp_rollback(mm, *a)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        cpu = {"value": ns / g.layers / dt, "unit": "seq/s", "cores": 1, "kind": "port",
+               "sample": f"{ns} (sequence, layer) state rollbacks of the same shapes, oracle restatement of "
+                         f"MtpRollback.stateAfter, one thread, {reps} repetitions"}
+    if rank != 0:
+        return
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
+    seqs = n // (args.layers or g.layers)
+    print(json.dumps({
+        "metric": "GDN MTP rollback: sequences rolled back/s (all GDN layers of one attention block)",
+        "value": seqs * world / (ms * 1e-3), "unit": "seq/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded torch.randn state, keys, deltas; gates = negative cumsums)",
+        "config": {"workload": f"config6: {seqs} seqs/GPU x {n // seqs} GDN layers; value heads {H}, "
+                               f"DK=DV={D}, C={Cw}, conv {CD}x{T} taps; m ~ U{{1..{Cw}}}",
+                   "step_bytes": step_bytes, "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None, "kernel": "mtp_rollback_kernel",
+                     "bytes_per_launch": bpl, "launch_ms": launch_ms},
+        "step_gbs": step_bytes / (ms * 1e-3) / 1e9,
+        "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * 2, "clocks": clk}), flush=True)
 
 
 def main():
@@ -695,7 +771,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5}[args.config]
+        runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6}[args.config]
         runner(args, rank, world, local)
     finally:
         if world > 1:

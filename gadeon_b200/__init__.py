@@ -18,6 +18,8 @@ from .kv import (  # noqa: F401
     BlockPool,
     GkvError,
     PagePool,
+    conv_rollback,
     host_flash_decode,
     load_library,
+    mtp_rollback,
 )

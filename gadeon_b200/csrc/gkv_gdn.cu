@@ -1,0 +1,290 @@
+// gkv_gdn.cu -- rollback of the Gated-DeltaNet layers' state after an
+// accepted speculative prefix: the step that runs beside the KV truncate in
+// every MTP cycle (leok7v/gadeon Engine.decodeSpecStep ->
+// rollbackGDN, LLM/src/CoreML/Engine.swift:2678-2716).
+//
+//   mtp_rollback_kernel  MtpRollback.stateAfter (LLM/src/CoreML/MtpRollback.swift
+//                        :20-60): S_m = exp(g[m-1]) S0 + sum_{t<m}
+//                        exp(g[m-1]-g[t]) outer(k_t, delta_t), per value head.
+//   conv_rollback_kernel Engine.convFromProj (Engine.swift:2719-2740): the
+//                        conv tail after m committed tokens.
+//
+// Both are HBM-bound streams (the recurrent state is read and written once);
+// items are (sequence, GDN layer) pairs of a batch, each with its own m.
+// The per-item m travels in the kernel parameters, so a call allocates
+// nothing and needs no upload.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+
+#include "gadeon_kv.h"
+#include "gkv_kernels.cuh"
+
+namespace gkv {
+namespace {
+
+constexpr int kMaxItemsPerLaunch = 2048;
+constexpr int kMaxChunk = 64;  // verify width C
+
+struct RollbackParams {
+    int32_t H, DK, DV, C;
+    const float *s0, *delta, *k, *gcum;
+    float *out;
+    int32_t m[kMaxItemsPerLaunch];
+};
+
+struct ConvParams {
+    int32_t CD, taps, C;
+    const float *proj, *pre;
+    float *out;
+    int32_t m[kMaxItemsPerLaunch];
+};
+
+// One CTA per (item, value head): the head's [DK, DV] state streams through
+// in float4s, kUnroll of them in flight per thread; the m gate weights are
+// computed once per CTA and the head's k / delta rows stay in L1.
+constexpr int kRollThreads = 256;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ float4 rollback_elem(const RollbackParams &p, const float *w, float eM, const float *kk,
+                                                const float *dd, int m, int e4, float4 s) {
+    const int i = e4 * 4 / p.DV, j = e4 * 4 % p.DV;
+    // reference order: out = eM * s0, then out += (w_t * k_t[i]) * delta_t[j]
+    // for t ascending, each multiply and add rounded on its own
+    float4 o = make_float4(__fmul_rn(eM, s.x), __fmul_rn(eM, s.y), __fmul_rn(eM, s.z), __fmul_rn(eM, s.w));
+    for (int t = 0; t < m; ++t) {
+        const float wk = __fmul_rn(w[t], __ldg(kk + t * p.DK + i));
+        const float4 d = __ldg(reinterpret_cast<const float4 *>(dd + t * p.DV + j));
+        o.x = __fadd_rn(o.x, __fmul_rn(wk, d.x));
+        o.y = __fadd_rn(o.y, __fmul_rn(wk, d.y));
+        o.z = __fadd_rn(o.z, __fmul_rn(wk, d.z));
+        o.w = __fadd_rn(o.w, __fmul_rn(wk, d.w));
+    }
+    return o;
+}
+
+// Any DV: one element per thread step, same operation order as the vector
+// path.
+__device__ __forceinline__ float rollback_scalar(const RollbackParams &p, const float *w, float eM, const float *kk,
+                                                 const float *dd, int m, int e, float s) {
+    const int i = e / p.DV, j = e % p.DV;
+    float o = __fmul_rn(eM, s);
+    for (int t = 0; t < m; ++t)
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(w[t], __ldg(kk + t * p.DK + i)), __ldg(dd + t * p.DV + j)));
+    return o;
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid_constant__ RollbackParams p) {
+    __shared__ float w[kMaxChunk];
+    __shared__ float eM;
+    const int hs = blockIdx.x;  // item * H + head
+    const int m = p.m[hs / p.H];
+    const float *g = p.gcum + (int64_t)hs * p.C;
+    if (threadIdx.x < m) w[threadIdx.x] = expf(g[m - 1] - g[threadIdx.x]);
+    if (threadIdx.x == 0) eM = expf(g[m - 1]);
+    __syncthreads();
+    const int64_t sbase = (int64_t)hs * p.DK * p.DV;
+    const float *kk = p.k + (int64_t)hs * p.C * p.DK;
+    const float *dd = p.delta + (int64_t)hs * p.C * p.DV;
+    const float e = eM;
+    if constexpr (VEC) {
+        const int nv4 = p.DK * p.DV / 4;
+        const float4 *s4 = reinterpret_cast<const float4 *>(p.s0 + sbase);
+        float4 *o4 = reinterpret_cast<float4 *>(p.out + sbase);
+        for (int base = threadIdx.x; base < nv4; base += kUnroll * kRollThreads) {
+            float4 s[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int e4 = base + u * kRollThreads;
+                if (e4 < nv4) s[u] = __ldcs(s4 + e4);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int e4 = base + u * kRollThreads;
+                if (e4 < nv4) __stcs(o4 + e4, rollback_elem(p, w, e, kk, dd, m, e4, s[u]));
+            }
+        }
+    } else {
+        const int n = p.DK * p.DV;
+        for (int x = threadIdx.x; x < n; x += kRollThreads)
+            p.out[sbase + x] = rollback_scalar(p, w, e, kk, dd, m, x, p.s0[sbase + x]);
+    }
+}
+
+// grid-stride over items * CD * taps outputs
+__global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constant__ ConvParams p, int items) {
+    const int64_t total = (int64_t)items * p.CD * p.taps;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(idx % p.taps);
+        const int64_t rest = idx / p.taps;
+        const int c = (int)(rest % p.CD);
+        const int item = (int)(rest / p.CD);
+        const int m = p.m[item];
+        const int pos = m - p.taps + t;
+        p.out[idx] = pos >= 0 ? p.proj[((int64_t)item * p.C + pos) * p.CD + c]
+                              : p.pre[((int64_t)item * p.CD + c) * p.taps + (m + t)];
+    }
+}
+
+// Fast path for the verify widths MTP uses (C <= kFastC) and DV % 4 == 0,
+// DV <= 4 * kRollThreads, DK <= kFastDK: thread = one float4 column group cg
+// of the state and rows r0, r0 + rstride, ...; its delta_t[cg] for t < m
+// live in registers, the m rows of w_t * k_t (the reference's wk) in shared
+// memory, read as warp-wide broadcasts when a warp covers one row.  The
+// state streams through kFastUnroll float4 loads in flight per thread; the
+// first batch is issued before the prologue so its latency overlaps it.
+constexpr int kFastC = 8;
+constexpr int kFastDK = 256;
+constexpr int kFastUnroll = 8;
+
+__global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams p) {
+    __shared__ float kw[kFastC][kFastDK];
+    __shared__ float eM_s;
+    const int hs = blockIdx.x;
+    const int m = p.m[hs / p.H];
+    const int ncg = p.DV >> 2;
+    const int rstride = kRollThreads / ncg;
+    const int cg = threadIdx.x % ncg, r0 = threadIdx.x / ncg;
+    const bool active = r0 < rstride;
+    const int64_t sbase = (int64_t)hs * p.DK * p.DV;
+    const float4 *s4 = reinterpret_cast<const float4 *>(p.s0 + sbase);
+    float4 *o4 = reinterpret_cast<float4 *>(p.out + sbase);
+    float4 s[kFastUnroll];
+#pragma unroll
+    for (int u = 0; u < kFastUnroll; ++u) {
+        const int i = r0 + u * rstride;
+        if (active && i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
+    }
+    // prologue: gate weights, wk rows, this thread's delta column
+    const float *g = p.gcum + (int64_t)hs * p.C;
+    const float gLast = g[m - 1];
+    const float *kk = p.k + (int64_t)hs * p.C * p.DK;
+    for (int x = threadIdx.x; x < m * p.DK; x += kRollThreads) {
+        const int t = x / p.DK, i = x - t * p.DK;
+        kw[t][i] = __fmul_rn(expf(gLast - g[t]), kk[x]);
+    }
+    if (threadIdx.x == 0) eM_s = expf(gLast);
+    float4 d[kFastC];
+    const float4 *d4 = reinterpret_cast<const float4 *>(p.delta + (int64_t)hs * p.C * p.DV);
+#pragma unroll
+    for (int t = 0; t < kFastC; ++t)
+        if (t < m) d[t] = __ldg(d4 + t * ncg + cg);
+    __syncthreads();
+    if (!active) return;
+    const float eM = eM_s;
+    for (int base = r0;; base += kFastUnroll * rstride) {
+#pragma unroll
+        for (int u = 0; u < kFastUnroll; ++u) {
+            const int i = base + u * rstride;
+            if (i < p.DK) {
+                float4 o = make_float4(__fmul_rn(eM, s[u].x), __fmul_rn(eM, s[u].y), __fmul_rn(eM, s[u].z),
+                                       __fmul_rn(eM, s[u].w));
+#pragma unroll
+                for (int t = 0; t < kFastC; ++t) {
+                    if (t < m) {
+                        const float wk = kw[t][i];
+                        o.x = __fadd_rn(o.x, __fmul_rn(wk, d[t].x));
+                        o.y = __fadd_rn(o.y, __fmul_rn(wk, d[t].y));
+                        o.z = __fadd_rn(o.z, __fmul_rn(wk, d[t].z));
+                        o.w = __fadd_rn(o.w, __fmul_rn(wk, d[t].w));
+                    }
+                }
+                __stcs(o4 + (int64_t)i * ncg + cg, o);
+            }
+        }
+        const int next = base + kFastUnroll * rstride;
+        if (next >= p.DK) break;
+#pragma unroll
+        for (int u = 0; u < kFastUnroll; ++u) {
+            const int i = next + u * rstride;
+            if (i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
+        }
+    }
+}
+
+bool misaligned(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
+
+}  // namespace
+}  // namespace gkv
+
+extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV,
+                                int32_t C, const float *s0, const float *delta, const float *k,
+                                const float *gcum, float *out, void *stream) {
+    using gkv::report_error;
+    if (n_items < 0 || H < 1 || DK < 1 || DV < 1 || C < 1)
+        return report_error(GKV_ERR_INVALID, "n_items=%d H=%d DK=%d DV=%d C=%d", n_items, H, DK, DV, C);
+    if (C > gkv::kMaxChunk) return report_error(GKV_ERR_UNSUPPORTED, "C=%d > %d", C, gkv::kMaxChunk);
+    if (H > (1 << 20)) return report_error(GKV_ERR_CAPACITY, "H=%d", H);
+    if ((int64_t)DK * DV > (1LL << 30)) return report_error(GKV_ERR_CAPACITY, "DK*DV=%lld", (long long)DK * DV);
+    if (n_items == 0) return GKV_OK;
+    if (!m || !s0 || !delta || !k || !gcum || !out) return report_error(GKV_ERR_INVALID, "null pointer");
+    if ((reinterpret_cast<uintptr_t>(s0) | reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(k) |
+         reinterpret_cast<uintptr_t>(gcum) | reinterpret_cast<uintptr_t>(out)) & 3)
+        return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
+    // float4 path: rows of DV a multiple of 4 floats on 16-byte boundaries
+    const bool vec = DV % 4 == 0 && !gkv::misaligned(s0) && !gkv::misaligned(delta) && !gkv::misaligned(out);
+    const bool fast = vec && C <= gkv::kFastC && DK <= gkv::kFastDK && DV <= 4 * gkv::kRollThreads;
+    for (int32_t i = 0; i < n_items; ++i)
+        if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // items per launch: what the parameter block's m[] holds
+    const int32_t per = gkv::kMaxItemsPerLaunch;
+    for (int32_t first = 0; first < n_items; first += per) {
+        const int32_t cnt = n_items - first < per ? n_items - first : per;
+        gkv::RollbackParams p{};
+        p.H = H;
+        p.DK = DK;
+        p.DV = DV;
+        p.C = C;
+        const int64_t hs0 = (int64_t)first * H;
+        p.s0 = s0 + hs0 * DK * DV;
+        p.delta = delta + hs0 * C * DV;
+        p.k = k + hs0 * C * DK;
+        p.gcum = gcum + hs0 * C;
+        p.out = out + hs0 * DK * DV;
+        for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+        const unsigned blocks = (unsigned)((int64_t)cnt * H);
+        if (fast)
+            gkv::mtp_rollback_fast_kernel<<<blocks, gkv::kRollThreads, 0, st>>>(p);
+        else if (vec)
+            gkv::mtp_rollback_kernel<true><<<blocks, gkv::kRollThreads, 0, st>>>(p);
+        else
+            gkv::mtp_rollback_kernel<false><<<blocks, gkv::kRollThreads, 0, st>>>(p);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "mtp_rollback launch: %s", cudaGetErrorString(e));
+    }
+    return GKV_OK;
+}
+
+extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
+                                 const float *proj, const float *pre, float *out, void *stream) {
+    using gkv::report_error;
+    if (n_items < 0 || conv_dim < 1 || taps < 1 || C < 1)
+        return report_error(GKV_ERR_INVALID, "n_items=%d conv_dim=%d taps=%d C=%d", n_items, conv_dim, taps, C);
+    if (n_items == 0) return GKV_OK;
+    if (!m || !proj || !pre || !out) return report_error(GKV_ERR_INVALID, "null pointer");
+    for (int32_t i = 0; i < n_items; ++i)
+        if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int32_t first = 0; first < n_items; first += gkv::kMaxItemsPerLaunch) {
+        const int32_t cnt = n_items - first < gkv::kMaxItemsPerLaunch ? n_items - first : gkv::kMaxItemsPerLaunch;
+        gkv::ConvParams p{};
+        p.CD = conv_dim;
+        p.taps = taps;
+        p.C = C;
+        p.proj = proj + (int64_t)first * C * conv_dim;
+        p.pre = pre + (int64_t)first * conv_dim * taps;
+        p.out = out + (int64_t)first * conv_dim * taps;
+        for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+        const int64_t total = (int64_t)cnt * conv_dim * taps;
+        const int64_t blocks = (total + 255) / 256;
+        gkv::conv_rollback_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(p, cnt);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "conv_rollback launch: %s", cudaGetErrorString(e));
+    }
+    return GKV_OK;
+}

@@ -45,7 +45,7 @@ EXPORTED = (
     "gkv_append", "gkv_seed", "gkv_attend", "gkv_append_attend", "gkv_truncate",
     "gkv_clone_seq", "gkv_compact_seq", "gkv_from_compact", "gkv_export_table",
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
-    "gkv_attend_noalloc",
+    "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback",
 )
 
 
@@ -102,6 +102,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_device_status": (C.c_int, [P, i32p]),
         "gkv_attend_noalloc": (C.c_int, [P, P, i32, i32, i32, i32, P, i32, i32, i32p, i32, i32, P, P,
                                          f32, P]),
+        "gkv_mtp_rollback": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
+        "gkv_conv_rollback": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -404,3 +406,45 @@ def host_flash_decode(q, pool: PagePool, G: int, stream=None):
     qq = q.reshape(1, 1, bp.kv_heads * G, bp.head_dim)
     out = bp.attend([pool.seq_id], 1, G, qq, scale=bp.head_dim ** -0.5, stream=stream)
     return out.reshape(-1)
+
+
+def mtp_rollback(m, s0, delta, k, gcum, out=None, stream=None):
+    """``MtpRollback.stateAfter`` (LLM/src/CoreML/MtpRollback.swift:47-60) on the
+    GPU for a batch of items (sequence x GDN layer): s0 [n, H, DK, DV],
+    delta [n, H, C, DV], k [n, H, C, DK], gcum [n, H, C] fp32 CUDA tensors,
+    m = accepted prefix per item (1..C).  Returns S_m [n, H, DK, DV] fp32."""
+    import torch
+    L = load_library()
+    n, H, DK, DV = (int(x) for x in s0.shape)
+    Cw = int(gcum.shape[-1])
+    _check_shape("delta", delta, (n, H, Cw, DV), ("float32",))
+    _check_shape("k", k, (n, H, Cw, DK), ("float32",))
+    _check_shape("gcum", gcum, (n, H, Cw), ("float32",))
+    if out is None:
+        out = torch.empty_like(s0)
+    _check_shape("out", out, (n, H, DK, DV), ("float32",))
+    mm = _i32(m)
+    if len(mm) != n:
+        raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
+    _check(L.gkv_mtp_rollback(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k),
+                              _dev_ptr(gcum), _dev_ptr(out), _stream_ptr(stream)))
+    return out
+
+
+def conv_rollback(m, proj, pre, out=None, stream=None):
+    """``Engine.convFromProj`` (LLM/src/CoreML/Engine.swift:2719-2740) on the GPU
+    for a batch: proj [n, C, CD], pre [n, CD, taps] fp32 -> [n, CD, taps]."""
+    import torch
+    L = load_library()
+    n, Cw, CD = (int(x) for x in proj.shape)
+    taps = int(pre.shape[-1])
+    _check_shape("pre", pre, (n, CD, taps), ("float32",))
+    if out is None:
+        out = torch.empty_like(pre)
+    _check_shape("out", out, (n, CD, taps), ("float32",))
+    mm = _i32(m)
+    if len(mm) != n:
+        raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
+    _check(L.gkv_conv_rollback(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out),
+                               _stream_ptr(stream)))
+    return out

@@ -45,6 +45,41 @@ CONFIGS = {
 }
 
 
+@dataclasses.dataclass(frozen=True)
+class GdnConfig:
+    """GDN rollback beside config 3's truncate: every sequence of the MTP
+    verify batch rolls back the recurrent state and conv tail of the GDN
+    layers that share its full-attention layer (3 GDN : 1 attention in the
+    hybrid).  Head geometry of the Qwen3.5 GDN layers: 16 key heads and 32
+    value heads of dim 128, conv kernel 4 (3 carried taps) over q|k|v
+    channels; verify width C = 1 + 4 drafts."""
+    seqs: int = 128
+    layers: int = 3
+    value_heads: int = 32
+    key_heads: int = 16
+    head_dim: int = 128
+    chunk: int = 5
+    taps: int = 3
+
+    @property
+    def conv_dim(self) -> int:
+        return (2 * self.key_heads + self.value_heads) * self.head_dim
+
+
+GDN = GdnConfig()
+
+
+def rollback_bytes(m: Sequence[int], g: GdnConfig) -> tuple:
+    """Algorithmic HBM bytes of one rollback call pair over items with
+    accepted lengths m: (state kernel, conv kernel).  The state is read and
+    written once; only the m accepted rows of k and delta and the gate row
+    are read; the conv tail is written once and each tap read once."""
+    H, D = g.value_heads, g.head_dim
+    state = sum(H * (2 * D * D + int(x) * 2 * D + g.chunk) * 4 for x in m)
+    conv = len(m) * g.conv_dim * g.taps * 2 * 4
+    return state, conv
+
+
 def contexts(cfg_id: int, seed: int, n: int) -> np.ndarray:
     """Context lengths of config cfg_id drawn from `seed`."""
     rng = np.random.default_rng(seed)

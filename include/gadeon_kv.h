@@ -143,6 +143,31 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V,
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V,
                      int64_t length, int32_t *seq_id, void *stream);
 
+/* ---- the GDN state rollback that runs beside gkv_truncate in an MTP cycle
+ * (Engine.rollbackGDN, LLM/src/CoreML/Engine.swift:2678-2716) ---- */
+
+/* MtpRollback.stateAfter (LLM/src/CoreML/MtpRollback.swift:47-60) for a batch
+ * of n_items (sequence x GDN layer) items, item i with accepted prefix m[i]
+ * in 1..C (HOST array):
+ *   S_m[h] = exp(g[h,m-1]) S0[h] + sum_{t<m} exp(g[h,m-1]-g[h,t]) k[h,t] x delta[h,t]
+ * Device fp32 buffers: s0/out [n_items, H, DK, DV], delta [n_items, H, C, DV],
+ * k [n_items, H, C, DK], gcum [n_items, H, C] (inclusive gate cumsum).
+ * C <= 64; every m[i] in 1..C; buffers 4-byte aligned (rows stream as
+ * float4 when DV is a multiple of 4 and s0/delta/out are 16-byte aligned). */
+int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK,
+                     int32_t DV, int32_t C, const float *s0,
+                     const float *delta, const float *k, const float *gcum,
+                     float *out, void *stream);
+
+/* Engine.convFromProj (Engine.swift:2719-2740) for a batch: conv state
+ * [conv_dim, taps] after m[i] committed tokens; tap t holds position
+ * m - taps + t, from this chunk's conv-projection rows proj [n_items, C,
+ * conv_dim] when >= 0, else from the pre-verify tail pre [n_items, conv_dim,
+ * taps] (oldest..newest).  out [n_items, conv_dim, taps]; all fp32 device. */
+int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim,
+                      int32_t taps, int32_t C, const float *proj,
+                      const float *pre, float *out, void *stream);
+
 /* Size of the library's static scratch array used by gkv_attend_noalloc
  * (held on every GPU that loads the library until the process exits), and
  * the largest batch that entry point takes. */

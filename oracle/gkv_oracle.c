@@ -37,6 +37,11 @@
  *   CPU route Engine.swift:1220-1224): append row s, then hostFlashDecode of
  *   query row s -- row s of a batch that starts at p0 sees keys [0, p0+s].
  *
+ *   GDN rollback after an accepted speculative prefix (MtpRollback.stateAfter,
+ *   LLM/src/CoreML/MtpRollback.swift:20-60; Engine.convFromProj,
+ *   Engine.swift:2719-2740), pinned by the reference's own known answers
+ *   (LLM/tests/MtpRollbackTests.swift).
+ *
  * The block pool, block tables and free list do NOT exist in the reference
  * (each PagePool is a private array of ARC'd pages).  The oracle defines the
  * one explicit model that the GPU library mirrors bit-for-bit:
@@ -633,4 +638,60 @@ int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
     for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
     free(th);
     return ORC_OK;
+}
+
+/* ------------------------------------------------------------------ */
+/* GDN rollback after an accepted speculative prefix (SURVEY "next")   */
+/* ------------------------------------------------------------------ */
+
+/* MtpRollback.stateAfter (LLM/src/CoreML/MtpRollback.swift:20-60) for a
+ * batch of n items (sequence x GDN layer), each with its own accepted
+ * prefix m[i] in 1..C:
+ *   S_m[h] = exp(gcum[h,m-1]) * S0[h]
+ *            + sum_{t<m} exp(gcum[h,m-1] - gcum[h,t]) * outer(k[h,t], delta[h,t])
+ * in the reference's order: out = eM * s0, then for t ascending
+ * out[i][j] += (w_t * k[t][i]) * delta[t][j].
+ * s0/out [n,H,DK,DV], delta [n,H,C,DV], k [n,H,C,DK], gcum [n,H,C]; fp32. */
+void orc_mtp_rollback(int n, const int32_t *m, int H, int DK, int DV, int C,
+                      const float *s0, const float *delta, const float *k,
+                      const float *gcum, float *out) {
+    for (int it = 0; it < n; it++)
+        for (int h = 0; h < H; h++) {
+            const int64_t hs = (int64_t)it * H + h;
+            const float *g = gcum + hs * C;
+            const float *kk = k + hs * C * DK;
+            const float *dd = delta + hs * C * DV;
+            const float *s = s0 + hs * DK * DV;
+            float *o = out + hs * DK * DV;
+            const int mm = m[it];
+            const float gLast = g[mm - 1];
+            const float eM = expf(gLast);
+            for (int i = 0; i < DK * DV; i++) o[i] = eM * s[i];
+            for (int t = 0; t < mm; t++) {
+                const float w = expf(gLast - g[t]);
+                for (int i = 0; i < DK; i++) {
+                    const float wk = w * kk[t * DK + i];
+                    for (int j = 0; j < DV; j++) o[i * DV + j] += wk * dd[t * DV + j];
+                }
+            }
+        }
+}
+
+/* Engine.convFromProj (LLM/src/CoreML/Engine.swift:2719-2740): conv state
+ * [CD, taps] after m committed tokens; tap t holds position m - taps + t,
+ * taken from this chunk's conv-projection rows proj [C, CD] when >= 0 and
+ * from the pre-verify tail pre [CD, taps] (oldest..newest) otherwise.
+ * Batched over n items; fp32 in and out (the engine then stores fp16). */
+void orc_conv_rollback(int n, const int32_t *m, int CD, int taps, int C,
+                       const float *proj, const float *pre, float *out) {
+    for (int it = 0; it < n; it++) {
+        const float *pr = proj + (int64_t)it * C * CD;
+        const float *pc = pre + (int64_t)it * CD * taps;
+        float *o = out + (int64_t)it * CD * taps;
+        for (int t = 0; t < taps; t++) {
+            const int pos = m[it] - taps + t;
+            for (int c = 0; c < CD; c++)
+                o[c * taps + t] = pos >= 0 ? pr[pos * CD + c] : pc[c * taps + (m[it] + t)];
+        }
+    }
 }

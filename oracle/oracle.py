@@ -73,6 +73,9 @@ def lib():
         "orc_flash_decode": (C.c_int, [P, C.c_int, u16p, C.c_int, C.c_float, f32p]),
         "orc_attend_causal": (
             C.c_int, [P, C.c_int, i32p, C.c_int, u16p, C.c_int, C.c_float, f32p, C.c_int]),
+        "orc_mtp_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p,
+                                    f32p, f32p]),
+        "orc_conv_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -222,3 +225,32 @@ class OraclePool:
         if rc:
             raise ValueError(f"orc_attend_causal rc={rc}")
         return out
+
+
+def mtp_rollback(m, s0, delta, k, gcum) -> np.ndarray:
+    """MtpRollback.stateAfter restated (gkv_oracle.c): s0 [n,H,DK,DV],
+    delta [n,H,C,DV], k [n,H,C,DK], gcum [n,H,C] fp32; m per item."""
+    s0 = np.ascontiguousarray(s0, dtype=np.float32)
+    delta = np.ascontiguousarray(delta, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    gcum = np.ascontiguousarray(gcum, dtype=np.float32)
+    n, H, DK, DV = s0.shape
+    Cw = gcum.shape[-1]
+    mm = np.ascontiguousarray(m, dtype=np.int32)
+    out = np.empty_like(s0)
+    lib().orc_mtp_rollback(n, _ptr(mm, C.c_int32), H, DK, DV, Cw, _ptr(s0, C.c_float), _ptr(delta, C.c_float),
+                           _ptr(k, C.c_float), _ptr(gcum, C.c_float), _ptr(out, C.c_float))
+    return out
+
+
+def conv_rollback(m, proj, pre) -> np.ndarray:
+    """Engine.convFromProj restated: proj [n,C,CD], pre [n,CD,taps] -> [n,CD,taps]."""
+    proj = np.ascontiguousarray(proj, dtype=np.float32)
+    pre = np.ascontiguousarray(pre, dtype=np.float32)
+    n, Cw, CD = proj.shape
+    taps = pre.shape[-1]
+    mm = np.ascontiguousarray(m, dtype=np.int32)
+    out = np.empty_like(pre)
+    lib().orc_conv_rollback(n, _ptr(mm, C.c_int32), CD, taps, Cw, _ptr(proj, C.c_float), _ptr(pre, C.c_float),
+                            _ptr(out, C.c_float))
+    return out

@@ -1,0 +1,199 @@
+"""GDN rollback after an accepted speculative prefix: the recurrent-state
+reconstruction (MtpRollback.stateAfter, LLM/src/CoreML/MtpRollback.swift:47-60)
+and the conv tail (Engine.convFromProj, LLM/src/CoreML/Engine.swift:2719-2740).
+
+The oracle restatement is pinned by the reference's own known answers
+(LLM/tests/MtpRollbackTests.swift, tolerance 1e-3) and by a numpy evaluation
+of the closed form; the CUDA path is checked against both.  The conv tail is
+a pure gather, so it must match bit for bit."""
+import math
+
+import numpy as np
+import pytest
+
+# MtpRollbackTests.swift:11-13 (one head, DK=DV=C=2) and :44-47 (C=5)
+S0 = np.array([1, 0, 0, 1], dtype=np.float32)
+K2 = np.array([1, 2, 5, 6], dtype=np.float32)
+D2 = np.array([3, 4, 7, 8], dtype=np.float32)
+K5 = np.array([1, 2, 5, 6, 1, 1, 2, 0, 1, 1], dtype=np.float32)
+D5 = np.array([3, 4, 7, 8, 1, 1, 0, 3, 2, 2], dtype=np.float32)
+KAT_TOL = 1e-3
+
+
+def kat_cases():
+    """(name, m, C, k, delta, gcum, want) -- the reference's six known answers."""
+    eM, w0 = math.exp(-1.5), math.exp(-0.5)
+    g4 = [-1, -1.5, -1.8, -2.0, -2.1]
+    o = [[3, 4, 6, 8], [35, 40, 42, 48], [1, 1, 1, 1], [0, 6, 0, 0]]
+    m4 = [math.exp(g4[3]) * S0[i] + sum(math.exp(g4[3] - g4[t]) * o[t][i] for t in range(4)) for i in range(4)]
+    return [
+        ("full_prefix_no_decay", 2, 2, K2, D2, [0, 0], [39, 44, 48, 57]),
+        ("partial_prefix_no_decay", 1, 2, K2, D2, [0, 0], [4, 4, 6, 9]),
+        ("decay_weighting", 2, 2, K2, D2, [-1, -1.5],
+         [eM + w0 * 3 + 35, w0 * 4 + 40, w0 * 6 + 42, eM + w0 * 8 + 48]),
+        ("m4_no_decay", 4, 5, K5, D5, [0] * 5, [40, 51, 49, 58]),
+        ("m5_no_decay", 5, 5, K5, D5, [0] * 5, [42, 53, 51, 60]),
+        ("m4_decay", 4, 5, K5, D5, g4, m4),
+    ]
+
+
+def kat_arrays(m, C, k, d, g):
+    return (np.array([m], dtype=np.int32), S0.reshape(1, 1, 2, 2), d.reshape(1, 1, C, 2),
+            k.reshape(1, 1, C, 2), np.array(g, dtype=np.float32).reshape(1, 1, C))
+
+
+def closed_form(m, s0, delta, k, gcum):
+    """S_m = exp(g[m-1]) S0 + sum_{t<m} exp(g[m-1]-g[t]) outer(k_t, delta_t), float64."""
+    n, H = s0.shape[:2]
+    out = np.empty(s0.shape, dtype=np.float64)
+    for it in range(n):
+        mm = int(m[it])
+        for h in range(H):
+            g = gcum[it, h].astype(np.float64)
+            w = np.exp(g[mm - 1] - g[:mm])
+            out[it, h] = math.exp(g[mm - 1]) * s0[it, h] + np.einsum(
+                "t,ti,tj->ij", w, k[it, h, :mm].astype(np.float64), delta[it, h, :mm].astype(np.float64))
+    return out
+
+
+def random_batch(seed, n, H, DK, DV, C, m=None):
+    """Shapes and value ranges of a Qwen3.5 GDN layer's verify ingredients:
+    state entries O(0.1), unit-norm-ish keys, gates = negative cumsums."""
+    rng = np.random.default_rng(seed)
+    s0 = (rng.standard_normal((n, H, DK, DV)) * 0.1).astype(np.float32)
+    k = (rng.standard_normal((n, H, C, DK)) / math.sqrt(DK)).astype(np.float32)
+    delta = (rng.standard_normal((n, H, C, DV)) * 0.5).astype(np.float32)
+    gcum = np.cumsum(-rng.uniform(0.0, 0.7, (n, H, C)), axis=-1).astype(np.float32)
+    if m is None:
+        m = rng.integers(1, C + 1, n).astype(np.int32)
+    return np.asarray(m, dtype=np.int32), s0, delta, k, gcum
+
+
+def conv_closed_form(m, proj, pre):
+    n, C, CD = proj.shape
+    taps = pre.shape[-1]
+    out = np.empty_like(pre)
+    for it in range(n):
+        for t in range(taps):
+            pos = int(m[it]) - taps + t
+            out[it, :, t] = proj[it, pos] if pos >= 0 else pre[it, :, int(m[it]) + t]
+    return out
+
+
+# ---------------------------------------------------------------- CPU: oracle
+
+@pytest.mark.parametrize("case", kat_cases(), ids=lambda c: c[0])
+def test_oracle_reference_known_answers(oracle, case):
+    _, m, C, k, d, g, want = case
+    got = oracle.mtp_rollback(*kat_arrays(m, C, k, d, g))
+    np.testing.assert_allclose(got.reshape(-1), np.array(want, dtype=np.float64), rtol=0, atol=KAT_TOL)
+
+
+def test_oracle_matches_closed_form(oracle):
+    m, s0, delta, k, gcum = random_batch(3, 6, 4, 16, 12, 5)
+    got = oracle.mtp_rollback(m, s0, delta, k, gcum)
+    want = closed_form(m, s0, delta, k, gcum)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
+def test_oracle_conv_tail(oracle):
+    rng = np.random.default_rng(4)
+    n, C, CD, taps = 7, 5, 24, 3
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float32)
+    m = np.array([1, 2, 3, 4, 5, 1, 5], dtype=np.int32)
+    assert np.array_equal(oracle.conv_rollback(m, proj, pre), conv_closed_form(m, proj, pre))
+    # a 1-token commit keeps the two newest carried taps and adds proj row 0
+    one = oracle.conv_rollback(m[:1], proj[:1], pre[:1])
+    assert np.array_equal(one[0, :, :2], pre[0, :, 1:]) and np.array_equal(one[0, :, 2], proj[0, 0])
+
+
+# ---------------------------------------------------------------- GPU
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", kat_cases(), ids=lambda c: c[0])
+def test_gpu_reference_known_answers(cuda, case):
+    import gadeon_b200 as gk
+    torch = cuda
+    _, m, C, k, d, g, want = case
+    mm, s0, delta, kk, gcum = kat_arrays(m, C, k, d, g)
+    out = gk.mtp_rollback(mm, _dev(torch, s0), _dev(torch, delta), _dev(torch, kk), _dev(torch, gcum))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy().reshape(-1), np.array(want, dtype=np.float64), rtol=0,
+                               atol=KAT_TOL)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,DK,DV,C", [
+    (16, 128, 128, 5), (32, 128, 128, 4), (2, 256, 96, 8),  # register-resident path (C <= 8)
+    (4, 64, 96, 17), (2, 8, 4, 64), (2, 300, 8, 3),          # float4 path
+    (3, 5, 6, 7),                                            # scalar path (DV % 4 != 0)
+])
+def test_gpu_matches_oracle(cuda, oracle, H, DK, DV, C):
+    """Batch of items with their own accepted lengths (every m in 1..C met)."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n = max(C, 6)
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(10 + C, n, H, DK, DV, C, m)
+    want = oracle.mtp_rollback(m, s0, delta, k, gcum)
+    got = gk.mtp_rollback(m, _dev(torch, s0), _dev(torch, delta), _dev(torch, k), _dev(torch, gcum))
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    # fp32 with the reference's operation order; only expf may differ by an ulp
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(got, closed_form(m, s0, delta, k, gcum), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_gpu_many_items_cross_launch_chunks(cuda, oracle):
+    """More items than one launch carries (2048 accepted lengths per parameter block)."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n, H, DK, DV, C = 2100, 40, 4, 8, 3
+    m, s0, delta, k, gcum = random_batch(21, n, H, DK, DV, C)
+    want = oracle.mtp_rollback(m, s0, delta, k, gcum)
+    got = gk.mtp_rollback(m, _dev(torch, s0), _dev(torch, delta), _dev(torch, k), _dev(torch, gcum))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_gpu_conv_tail_bit_exact(cuda, oracle):
+    import gadeon_b200 as gk
+    torch = cuda
+    rng = np.random.default_rng(5)
+    n, C, CD, taps = 2500, 5, 96, 3
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float32)
+    m = rng.integers(1, C + 1, n).astype(np.int32)
+    got = gk.conv_rollback(m, _dev(torch, proj), _dev(torch, pre))
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), oracle.conv_rollback(m, proj, pre))
+
+
+@pytest.mark.gpu
+def test_gpu_rollback_rejects_bad_arguments(cuda):
+    import gadeon_b200 as gk
+    torch = cuda
+    m, s0, delta, k, gcum = random_batch(1, 2, 2, 8, 8, 4)
+    args = [_dev(torch, x) for x in (s0, delta, k, gcum)]
+    for bad_m in ([0, 1], [1, 5]):
+        with pytest.raises(gk.GkvError) as e:
+            gk.mtp_rollback(bad_m, *args)
+        assert e.value.code == gk.GKV_ERR_INVALID
+    with pytest.raises(gk.GkvError):
+        gk.mtp_rollback([1], *args)  # m count != items
+    m2, s2, d2, k2, g2 = random_batch(2, 1, 1, 8, 8, 65)
+    with pytest.raises(gk.GkvError) as e:
+        gk.mtp_rollback(m2, *[_dev(torch, x) for x in (s2, d2, k2, g2)])
+    assert e.value.code == gk.GKV_ERR_UNSUPPORTED
+    proj = torch.zeros(2, 4, 8, device="cuda")
+    pre = torch.zeros(2, 8, 3, device="cuda")
+    with pytest.raises(gk.GkvError) as e:
+        gk.conv_rollback([0, 1], proj, pre)
+    assert e.value.code == gk.GKV_ERR_INVALID
