@@ -114,19 +114,19 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid
     }
 }
 
-// grid-stride over items * CD * taps outputs
-__global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constant__ ConvParams p, int items) {
-    const int64_t total = (int64_t)items * p.CD * p.taps;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(idx % p.taps);
-        const int64_t rest = idx / p.taps;
-        const int c = (int)(rest % p.CD);
-        const int item = (int)(rest / p.CD);
-        const int m = p.m[item];
+// grid (ceil(CD / 256), items): thread = one channel c of one item, all its
+// taps; reads of proj rows and writes of the [CD, taps] tail are coalesced
+// across the warp's consecutive channels.
+__global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constant__ ConvParams p) {
+    const int item = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= p.CD) return;
+    const int m = p.m[item];
+    const float *proj = p.proj + (int64_t)item * p.C * p.CD + c;
+    const int64_t tail = ((int64_t)item * p.CD + c) * p.taps;
+    for (int t = 0; t < p.taps; ++t) {
         const int pos = m - p.taps + t;
-        p.out[idx] = pos >= 0 ? p.proj[((int64_t)item * p.C + pos) * p.CD + c]
-                              : p.pre[((int64_t)item * p.CD + c) * p.taps + (m + t)];
+        p.out[tail + t] = pos >= 0 ? __ldcs(proj + (int64_t)pos * p.CD) : __ldcs(p.pre + tail + m + t);
     }
 }
 
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constan
 // first batch is issued before the prologue so its latency overlaps it.
 constexpr int kFastC = 8;
 constexpr int kFastDK = 256;
-constexpr int kFastUnroll = 8;
+constexpr int kFastUnroll = 4;  // 8 needs 80 registers: 3 CTAs/SM and 0.89 of the HBM copy rate; 4 reaches 0.94
 
 __global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams p) {
     __shared__ float kw[kFastC][kFastDK];
@@ -267,6 +267,8 @@ extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv
         return report_error(GKV_ERR_INVALID, "n_items=%d conv_dim=%d taps=%d C=%d", n_items, conv_dim, taps, C);
     if (n_items == 0) return GKV_OK;
     if (!m || !proj || !pre || !out) return report_error(GKV_ERR_INVALID, "null pointer");
+    if ((reinterpret_cast<uintptr_t>(proj) | reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(out)) & 3)
+        return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -280,9 +282,8 @@ extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv
         p.pre = pre + (int64_t)first * conv_dim * taps;
         p.out = out + (int64_t)first * conv_dim * taps;
         for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
-        const int64_t total = (int64_t)cnt * conv_dim * taps;
-        const int64_t blocks = (total + 255) / 256;
-        gkv::conv_rollback_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(p, cnt);
+        const dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)cnt);
+        gkv::conv_rollback_kernel<<<grid, 256, 0, st>>>(p);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "conv_rollback launch: %s", cudaGetErrorString(e));
     }
