@@ -20,10 +20,11 @@
 //              the P.V MMA.  The running max is raised only when it grows by
 //              more than 2^8; only then is that row of O rescaled in tensor
 //              memory.
-//   warp 4     TMA loads of K halves (one lane per page) into a 4-stage ring whose stages are
-//              stacked per 64-column block, so the two halves of a tile form
-//              one 128-row operand with a uniform stride.
-//   warp 5     TMA loads of V halves into a 2-stage ring.
+//   warps 4, 5 TMA loads of K tiles (warp 4) and V tiles (warp 5), one lane
+//              per page group, into ONE ring of 128-key stages that both share.
+//              The ring is filled in the order the tensor core consumes it --
+//              K0, K1, V0, K2, V1, K3, V2, ... -- so every load is issued two
+//              MMAs ahead of its use (with separate K and V rings, V got one).
 //   warp 6     owns tensor memory; one thread issues S = Q K^T
 //              (tcgen05.mma M=128, N=128) and O += P V (N = dh, V read
 //              MN-major, eight K=16 steps) into the fp32 O accumulator that
@@ -48,23 +49,25 @@ constexpr int kSoftmaxWarps = 4;
 constexpr int kChunkThreads = (kSoftmaxWarps + 3) * 32;
 constexpr int kKWarp = 4, kVWarp = 5, kMmaWarp = 6;
 constexpr int kChunkRows = 128;   // tcgen05 M
-constexpr int kHalf = 64;         // keys per TMA stage
+constexpr int kHalf = 64;         // keys per P atom; most rows in one TMA box
 constexpr int kTile = 2 * kHalf;  // keys per tile (tcgen05 N of Q K^T)
-constexpr int kKStages = 4;       // K ring: two tiles of two halves
-constexpr int kVStages = 2;       // V ring: the two halves of one tile
 constexpr uint32_t kTmemMaxCols = 512;  // tensor memory columns per SM
 
 template <int DH>
 struct ChunkCfg {
     static constexpr int NCB = DH / 64;
-    static constexpr int HALF_BYTES = kHalf * DH * 2;               // one 64-key stage
-    static constexpr int KCB_STRIDE = kKStages * kHalf * 128;       // K column-block stride
+    // A stage = one 128-key tile of K or V: NCB column blocks of 64 head-dim
+    // columns, each 128 keys x 128 bytes (128B-swizzled, 8-key groups 1024
+    // bytes apart).  Read K-major it is the B operand of Q K^T; read MN-major
+    // (column-block stride as LBO) it is the B operand of P V.
+    static constexpr int CB_BYTES = kTile * 128;
+    static constexpr int STAGE_BYTES = NCB * CB_BYTES;
+    static constexpr int NS = DH == 256 ? 3 : (DH == 128 ? 6 : 8);  // ring depth within 227 KB
     static constexpr int P_BYTES = kChunkRows * kTile * 2;          // two 64-key atoms
-    static constexpr int OFF_K = 0;
-    static constexpr int OFF_V = OFF_K + kKStages * HALF_BYTES;
-    static constexpr int OFF_P = OFF_V + kVStages * HALF_BYTES;
+    static constexpr int OFF_STAGE = 0;
+    static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int NBARS = 2 + 2 + 2 + 2 + 4;
+    static constexpr int NBARS = 2 * NS + 4;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
     // Tensor memory: S (128 fp32 columns), O (dh fp32 columns), Q (dh fp16 =
     // dh/2 columns, the A operand of Q K^T).
@@ -91,14 +94,12 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-    uint64_t *k_full = bars;        // [2] per tile slot: TMA -> MMA
-    uint64_t *k_empty = bars + 2;   // [2] MMA commit -> K loader
-    uint64_t *v_full = bars + 4;    // [2] per V stage
-    uint64_t *v_empty = bars + 6;   // [2]
-    uint64_t *s_full = bars + 8;    // MMA commit -> softmax
-    uint64_t *s_free = bars + 9;    // softmax warps -> MMA
-    uint64_t *p_full = bars + 10;   // softmax warps -> MMA
-    uint64_t *p_free = bars + 11;   // MMA commit (P.V done) -> softmax
+    uint64_t *full = bars;               // [NS] TMA -> MMA (and the V-tail zeroing)
+    uint64_t *empty = bars + C::NS;      // [NS] MMA commit -> loaders
+    uint64_t *s_full = bars + 2 * C::NS;      // MMA commit -> softmax
+    uint64_t *s_free = bars + 2 * C::NS + 1;  // softmax warps -> MMA
+    uint64_t *p_full = bars + 2 * C::NS + 2;  // softmax warps -> MMA
+    uint64_t *p_free = bars + 2 * C::NS + 3;  // MMA commit (P.V done) -> softmax
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -111,9 +112,13 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     const int t_lo = qb * p.qtok, t_hi = min(p.n_q, t_lo + p.qtok);
     const int kend = p0 + t_hi;  // keys [0, kend) feed this block
     const int nt = (kend + TT - 1) / TT;
+    // position of tile j's K and V in the ring's fill sequence K0 K1 V0 K2 V1 ...
+    auto kidx = [&](int j) { return j == 0 ? 0 : 2 * j - 1; };
+    auto vidx = [&](int j) { return min(2 * j + 2, 2 * nt - 1); };
+    auto stage = [&](int idx) { return smem + C::OFF_STAGE + (idx % C::NS) * C::STAGE_BYTES; };
 
     if (tid == 0) {
-        for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 2 * C::NS; ++i) mbar_init(&bars[i], 1);
         mbar_init(s_full, 1);
         mbar_init(s_free, kSoftmaxWarps);
         mbar_init(p_full, kSoftmaxWarps);
@@ -126,8 +131,8 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         tmem_relinquish();
     }
     // K/V stages start zeroed so never-loaded slots hold finite values.
-    for (int i = tid; i < (C::OFF_P - C::OFF_K) / 16; i += kChunkThreads)
-        reinterpret_cast<uint4 *>(smem + C::OFF_K)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < (C::OFF_P - C::OFF_STAGE) / 16; i += kChunkThreads)
+        reinterpret_cast<uint4 *>(smem + C::OFF_STAGE)[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
@@ -163,22 +168,21 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     if (warp == kKWarp || warp == kVWarp) {
         // ============================================ TMA producers
         // Lane i of the warp owns page group i of a 128-key tile (group =
-        // min(P, 64) keys of one page; half h = i / gph).  Every lane reads its
-        // block-table entry before the slot wait, in parallel, so the table
-        // latency is paid once per tile instead of once per page; then each
-        // lane issues its own group's boxes.
+        // min(P, 64) keys of one page).  Every lane reads its block-table
+        // entry before the stage wait, in parallel, so the table latency is
+        // paid once per tile instead of once per page; then each lane issues
+        // its own group's boxes (one per 64-column block).
         const bool is_k = warp == kKWarp;
         const CUtensorMap *map = is_k ? &tmk : &tmv;
         const int lP = __ffs(p.P) - 1;
         const int bh = min(p.P, H);
-        const int gph = H / bh;  // page groups per 64-key half (<= 8: P >= 8)
         const int32_t *trow = p.table + (int64_t)e.seq_id * p.table_stride;
-        auto half_bytes = [&](int t0) { return ((max(0, min(H, kend - t0)) + bh - 1) / bh) * bh * DH * 2; };
-        const int h_lane = lane / gph, g_lane = lane % gph;
         for (int j = 0; j < nt; ++j) {
+            const int idx = is_k ? kidx(j) : vidx(j);
+            const int st = idx % C::NS;
             const int t0 = j * TT;
-            const int tg = t0 + h_lane * H + g_lane * bh;
-            const bool mine = lane < 2 * gph && tg < kend;
+            const int tg = t0 + lane * bh;
+            const bool mine = lane < TT / bh && tg < kend;
             int row0 = 0;
             if (mine) {
                 int pid = __ldg(trow + (tg >> lP));
@@ -190,35 +194,16 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             }
             bool ok = true;
             if (lane == 0) {
-                if (is_k) {
-                    const int slot = j & 1;
-                    if (j >= 2) ok = mbar_wait(&k_empty[slot], ((j >> 1) - 1) & 1, abort_flag, p.status);
-                    if (ok) mbar_expect_tx(&k_full[slot], (uint32_t)(half_bytes(t0) + half_bytes(t0 + H)));
-                } else {
-                    for (int h = 0; h < 2 && ok; ++h) {
-                        if (j >= 1) ok = mbar_wait(&v_empty[h], (j - 1) & 1, abort_flag, p.status);
-                        if (ok) mbar_expect_tx(&v_full[h], (uint32_t)half_bytes(t0 + h * H));
-                    }
-                }
+                if (idx >= C::NS) ok = mbar_wait(&empty[st], ((idx / C::NS) - 1) & 1, abort_flag, p.status);
+                const int groups = (min(TT, kend - t0) + bh - 1) / bh;
+                if (ok) mbar_expect_tx(&full[st], (uint32_t)(groups * bh * DH * 2));
             }
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
             if (mine) {
-                uint8_t *dst;
-                int cb_stride;
-                uint64_t *bar;
-                if (is_k) {
-                    dst = smem + C::OFF_K + ((j & 1) * 2 + h_lane) * H * 128;
-                    cb_stride = C::KCB_STRIDE;
-                    bar = &k_full[j & 1];
-                } else {
-                    dst = smem + C::OFF_V + h_lane * C::HALF_BYTES;
-                    cb_stride = H * 128;
-                    bar = &v_full[h_lane];
-                }
+                const uint32_t dst = smem_u32(stage(idx)) + (uint32_t)(lane * bh * 128);
 #pragma unroll
                 for (int cb = 0; cb < C::NCB; ++cb)
-                    tma_load_2d(smem_u32(dst) + (uint32_t)(cb * cb_stride + g_lane * bh * 128), map, cb * 64,
-                                row0, bar);
+                    tma_load_2d(dst + (uint32_t)(cb * C::CB_BYTES), map, cb * 64, row0, &full[st]);
             }
             __syncwarp();
         }
@@ -228,42 +213,41 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             constexpr uint32_t IDESC_QK = umma_idesc_f16(M, TT, 0);
             constexpr uint32_t IDESC_PV = umma_idesc_f16(M, DH, 1);
             auto issue_pv = [&](int i) -> bool {
-                if (!mbar_wait(p_full, i & 1, abort_flag, p.status)) return false;
-                const int halves = min(2, (kend - i * TT + H - 1) / H);
-                for (int h = 0; h < halves; ++h) {
-                    if (!mbar_wait(&v_full[h], i & 1, abort_flag, p.status)) return false;
-                    tc_fence_after();
-                    const uint32_t sV = smem_u32(smem + C::OFF_V + h * C::HALF_BYTES);
-                    const uint32_t sP = smem_u32(smem + C::OFF_P + h * M * 128);
+                const int vi = vidx(i);
+                if (!mbar_wait(p_full, i & 1, abort_flag, p.status) ||
+                    !mbar_wait(&full[vi % C::NS], (vi / C::NS) & 1, abort_flag, p.status))
+                    return false;
+                tc_fence_after();
+                const uint32_t sV = smem_u32(stage(vi));
+                const uint32_t sP = smem_u32(smem + C::OFF_P);
 #pragma unroll
-                    for (int kk = 0; kk < H / 16; ++kk) {
-                        const uint64_t a = umma_desc_sw128(sP + kk * 32, 16, 1024);
-                        // V is MN-major: 64-column blocks H*128 bytes apart
-                        // (LBO), 8-key groups 1024 bytes apart (SBO).
-                        const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, H * 128, 1024);
-                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || h > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    umma_commit(&v_empty[h]);
+                for (int kk = 0; kk < TT / 16; ++kk) {
+                    // P atom kk/4 holds keys 64*(kk/4) .. +63; V is MN-major:
+                    // 64-column blocks CB_BYTES apart (LBO), 8-key groups 1024
+                    // bytes apart (SBO), 16 keys = 2048 bytes per K step.
+                    const uint64_t a = umma_desc_sw128(sP + (kk >> 2) * M * 128 + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, C::CB_BYTES, 1024);
+                    umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
                 }
-                if (halves < 2) umma_commit(&v_empty[1]);  // the unloaded half's stage is free too
+                umma_commit(&empty[vi % C::NS]);
                 umma_commit(p_free);
                 return true;
             };
             bool ok = true;
             for (int j = 0; j < nt && ok; ++j) {
-                ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, abort_flag, p.status) &&
+                const int ki = kidx(j);
+                ok = mbar_wait(&full[ki % C::NS], (ki / C::NS) & 1, abort_flag, p.status) &&
                      (j < 1 || mbar_wait(s_free, (j - 1) & 1, abort_flag, p.status));
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t sK = smem_u32(smem + C::OFF_K + (j & 1) * 2 * H * 128);
+                const uint32_t sK = smem_u32(stage(ki));
 #pragma unroll
                 for (int ks = 0; ks < DH / 16; ++ks) {  // A = Q from tensor memory, 8 columns per K=16
-                    const uint64_t bd =
-                        umma_desc_sw128(sK + (ks >> 2) * C::KCB_STRIDE + (ks & 3) * 32, 16, 1024);
+                    const uint64_t bd = umma_desc_sw128(sK + (ks >> 2) * C::CB_BYTES + (ks & 3) * 32, 16, 1024);
                     umma_f16_ts(tmem, tmem + C::Q_COL + ks * 8, bd, IDESC_QK, ks > 0);
                 }
                 umma_commit(s_full);
-                umma_commit(&k_empty[j & 1]);
+                umma_commit(&empty[ki % C::NS]);
                 if (j >= 1) ok = issue_pv(j - 1);
             }
             if (ok) issue_pv(nt - 1);
@@ -362,23 +346,19 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             l = l * factor + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
             const int nkeys = min(TT, kend - t0);
             if (nkeys < TT) {
-                // last tile: rows past the block's end may hold stale data;
-                // P is 0 there, zero V too so 0 * V stays 0.
-                for (int h = 0; h < 2; ++h) {
-                    const int valid_h = nkeys - h * H;
-                    if (valid_h <= 0 || valid_h >= H) continue;
-                    if (!mbar_wait(&v_full[h], j & 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sV = smem + C::OFF_V + h * C::HALF_BYTES;
-                    for (int i = tid; i < (H - valid_h) * (DH / 8); i += kSoftmaxWarps * 32) {
-                        const int key = valid_h + i / (DH / 8), c16 = i % (DH / 8);
-                        *reinterpret_cast<uint4 *>(sV + ((c16 >> 3) * H + key) * 128 +
-                                                   (((c16 & 7) ^ (key & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-                    }
+                // last tile: V rows past the block's end hold stale data; P is
+                // 0 there, zero V too so 0 * V stays 0 (once the tile landed).
+                const int vi = vidx(j);
+                if (!mbar_wait(&full[vi % C::NS], (vi / C::NS) & 1, abort_flag, p.status)) {
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
+                uint8_t *sV = stage(vi);
+                for (int i = tid; i < (TT - nkeys) * (DH / 8); i += kSoftmaxWarps * 32) {
+                    const int key = nkeys + i / (DH / 8), c16 = i % (DH / 8);
+                    *reinterpret_cast<uint4 *>(sV + (c16 >> 3) * C::CB_BYTES + key * 128 +
+                                               (((c16 & 7) ^ (key & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+                }
             }
             fence_proxy_async();  // P (and V zeroing) written by threads -> tensor core
             tc_fence_before();
