@@ -35,6 +35,16 @@
 // Completion flows through mbarriers: tcgen05.commit for tensor-core work,
 // TMA transaction counts for loads.  Every wait is bounded; a timeout raises
 // the device status word.
+//
+// CTA pairs (PAIR = true, dh 128/256, two or more query blocks): a cluster of
+// two CTAs on neighbouring SMs runs one M = 256 tile with tcgen05.mma
+// cta_group::2 -- each CTA holds its own 128 rows (Q, S, O in its tensor
+// memory, P in its shared memory) and loads HALF of every K tile (64 of the
+// 128 keys) and HALF of every V tile (dh/2 of the head-dim columns); the
+// tensor cores of the pair exchange the halves.  Each SM then streams half
+// the K/V bytes per FLOP.  The even CTA issues every MMA; its commits arrive
+// on both CTAs' barriers, the odd CTA's loads complete on the even CTA's
+// barriers, and the odd CTA's softmax warps arrive remotely on them.
 #include <cuda_fp16.h>
 
 #include "gkv_kernels.cuh"
@@ -48,26 +58,36 @@ using namespace ptx;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kChunkThreads = (kSoftmaxWarps + 3) * 32;
 constexpr int kKWarp = 4, kVWarp = 5, kMmaWarp = 6;
-constexpr int kChunkRows = 128;   // tcgen05 M
+constexpr int kChunkRows = 128;   // tensor-memory lanes = rows per CTA
 constexpr int kHalf = 64;         // keys per P atom; most rows in one TMA box
 constexpr int kTile = 2 * kHalf;  // keys per tile (tcgen05 N of Q K^T)
 constexpr uint32_t kTmemMaxCols = 512;  // tensor memory columns per SM
+constexpr int kSmemLimit = 227 * 1024;
 
-template <int DH>
+template <int DH, bool PAIR>
 struct ChunkCfg {
     static constexpr int NCB = DH / 64;
-    // A stage = one 128-key tile of K or V: NCB column blocks of 64 head-dim
-    // columns, each 128 keys x 128 bytes (128B-swizzled, 8-key groups 1024
-    // bytes apart).  Read K-major it is the B operand of Q K^T; read MN-major
-    // (column-block stride as LBO) it is the B operand of P V.
-    static constexpr int CB_BYTES = kTile * 128;
-    static constexpr int STAGE_BYTES = NCB * CB_BYTES;
-    static constexpr int NS = DH == 256 ? 3 : (DH == 128 ? 6 : 8);  // ring depth within 227 KB
-    static constexpr int P_BYTES = kChunkRows * kTile * 2;          // two 64-key atoms
+    static_assert(!PAIR || NCB >= 2, "a CTA pair splits V by 64-column blocks");
+    // A stage holds this CTA's part of one 128-key tile of K or V, 64-column
+    // blocks of 128-byte rows (128B swizzle, 8-row groups 1024 bytes apart).
+    // K (read K-major, the B operand of Q K^T): NCB blocks of K_ROWS keys --
+    // all 128 keys, or this CTA's 64 in a pair.  V (read MN-major, the B
+    // operand of P V, block stride as LBO): V_NCB blocks of 128 keys -- all
+    // head-dim blocks, or this CTA's half in a pair.  Both fill a stage.
+    static constexpr int K_ROWS = PAIR ? kHalf : kTile;
+    static constexpr int CB_K = K_ROWS * 128;
+    static constexpr int V_NCB = PAIR ? NCB / 2 : NCB;
+    static constexpr int CB_V = kTile * 128;
+    static constexpr int STAGE_BYTES = NCB * CB_K;
+    static_assert(STAGE_BYTES == V_NCB * CB_V, "K and V parts fill the same stage");
+    static constexpr int P_BYTES = kChunkRows * kTile * 2;  // two 64-key atoms
+    static constexpr int NS_FIT = (kSmemLimit - 2048 - P_BYTES) / STAGE_BYTES;
+    static constexpr int NS = NS_FIT < 8 ? NS_FIT : 8;      // ring depth
+    static_assert(NS >= 3, "the ring needs three stages");
     static constexpr int OFF_STAGE = 0;
     static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int NBARS = 2 * NS + 4;
+    static constexpr int NBARS = 2 * NS + 5;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
     // Tensor memory: S (128 fp32 columns), O (dh fp32 columns), Q (dh fp16 =
     // dh/2 columns, the A operand of Q K^T).
@@ -81,54 +101,80 @@ struct ChunkCfg {
     // shared-memory request so at most 512 / TMEM_COLS CTAs fit on an SM.
     static constexpr int MIN_SMEM = (228 * 1024) / (int)(kTmemMaxCols / TMEM_COLS + 1) + 1024;
     static constexpr int SMEM_ALLOC = SMEM + 1024 > MIN_SMEM ? SMEM + 1024 : MIN_SMEM;
-    static_assert(SMEM_ALLOC <= 227 * 1024, "fits the per-CTA shared memory limit");
+    static_assert(SMEM_ALLOC <= kSmemLimit, "fits the per-CTA shared memory limit");
 };
 
-template <int DH>
+template <int DH, bool PAIR>
 __global__ void __launch_bounds__(kChunkThreads, 1)
     chunk_kernel(const __grid_constant__ ChunkParams p, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv) {
-    using C = ChunkCfg<DH>;
+    using C = ChunkCfg<DH, PAIR>;
     constexpr int M = kChunkRows, TT = kTile, H = kHalf;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-    uint64_t *full = bars;               // [NS] TMA -> MMA (and the V-tail zeroing)
-    uint64_t *empty = bars + C::NS;      // [NS] MMA commit -> loaders
+    uint64_t *full = bars;                    // [NS] TMA -> MMA (the even CTA's count both halves)
+    uint64_t *empty = bars + C::NS;           // [NS] MMA commit -> loaders
     uint64_t *s_full = bars + 2 * C::NS;      // MMA commit -> softmax
-    uint64_t *s_free = bars + 2 * C::NS + 1;  // softmax warps -> MMA
-    uint64_t *p_full = bars + 2 * C::NS + 2;  // softmax warps -> MMA
+    uint64_t *s_free = bars + 2 * C::NS + 1;  // softmax warps (of both CTAs) -> MMA
+    uint64_t *p_full = bars + 2 * C::NS + 2;  // softmax warps (of both CTAs) -> MMA
     uint64_t *p_free = bars + 2 * C::NS + 3;  // MMA commit (P.V done) -> softmax
+    uint64_t *vtail = bars + 2 * C::NS + 4;   // pair: this CTA's part of the last V tile landed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int qb = p.n_qblocks - 1 - (int)blockIdx.x;  // longest key ranges first
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    // longest key ranges first; a pair takes two consecutive query blocks
+    const int qb = PAIR ? 2 * ((p.n_qblocks + 1) / 2 - 1 - (int)(blockIdx.x >> 1)) + (int)rank
+                        : p.n_qblocks - 1 - (int)blockIdx.x;
     const int kvh = blockIdx.y, b = blockIdx.z;
     const AttendEntry e = p.entries[b];
     const int G = p.G, KVH = p.kvh, nH = KVH * G;
     const int p0 = e.len - p.n_q;
+    // t_hi < t_lo (no valid rows) for a pair's odd block past the chunk's end
     const int t_lo = qb * p.qtok, t_hi = min(p.n_q, t_lo + p.qtok);
-    const int kend = p0 + t_hi;  // keys [0, kend) feed this block
+    const int kend = p0 + (PAIR ? min(p.n_q, (qb - (int)rank + 2) * p.qtok) : t_hi);  // keys [0, kend)
     const int nt = (kend + TT - 1) / TT;
     // position of tile j's K and V in the ring's fill sequence K0 K1 V0 K2 V1 ...
     auto kidx = [&](int j) { return j == 0 ? 0 : 2 * j - 1; };
     auto vidx = [&](int j) { return min(2 * j + 2, 2 * nt - 1); };
     auto stage = [&](int idx) { return smem + C::OFF_STAGE + (idx % C::NS) * C::STAGE_BYTES; };
+    // waits on barriers that the other CTA of a pair also arrives on acquire at cluster scope
+    auto wait = [&](uint64_t *bar, uint32_t parity) {
+        if constexpr (PAIR)
+            return mbar_wait_cluster(bar, parity, abort_flag, p.status);
+        else
+            return mbar_wait(bar, parity, abort_flag, p.status);
+    };
+    // softmax -> MMA arrivals land on the even CTA's barrier
+    auto arrive_leader = [&](uint64_t *bar) {
+        if (PAIR && !leader)
+            mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
+        else
+            mbar_arrive(bar);
+    };
 
     if (tid == 0) {
         for (int i = 0; i < 2 * C::NS; ++i) mbar_init(&bars[i], 1);
         mbar_init(s_full, 1);
-        mbar_init(s_free, kSoftmaxWarps);
-        mbar_init(p_full, kSoftmaxWarps);
+        mbar_init(s_free, (PAIR ? 2 : 1) * kSoftmaxWarps);
+        mbar_init(p_full, (PAIR ? 2 : 1) * kSoftmaxWarps);
         mbar_init(p_free, 1);
+        mbar_init(vtail, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     // K/V stages start zeroed so never-loaded slots hold finite values.
     for (int i = tid; i < (C::OFF_P - C::OFF_STAGE) / 16; i += kChunkThreads)
@@ -161,28 +207,46 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         }
         tmem_wait_st();
     }
+    // Both CTAs' Q rows and barriers are in place before the first MMA or
+    // remote arrival.
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    if constexpr (PAIR)
+        cluster_sync();
+    else
+        __syncthreads();
     tc_fence_after();
 
     if (warp == kKWarp || warp == kVWarp) {
         // ============================================ TMA producers
-        // Lane i of the warp owns page group i of a 128-key tile (group =
-        // min(P, 64) keys of one page).  Every lane reads its block-table
-        // entry before the stage wait, in parallel, so the table latency is
-        // paid once per tile instead of once per page; then each lane issues
-        // its own group's boxes (one per 64-column block).
+        // Lane i of the warp owns page group i of this CTA's part of a tile
+        // (group = min(P, 64) keys of one page).  Every lane reads its
+        // block-table entry before the stage wait, in parallel, so the table
+        // latency is paid once per tile instead of once per page; then each
+        // lane issues its own group's boxes (one per 64-column block).
         const bool is_k = warp == kKWarp;
         const CUtensorMap *map = is_k ? &tmk : &tmv;
         const int lP = __ffs(p.P) - 1;
         const int bh = min(p.P, H);
         const int32_t *trow = p.table + (int64_t)e.seq_id * p.table_stride;
+        const int key_cnt = (PAIR && is_k) ? H : TT;            // keys of a tile this CTA loads
+        const int key_off = (PAIR && is_k) ? (int)rank * H : 0;
+        const int ncb = is_k ? C::NCB : C::V_NCB;               // 64-column blocks it loads
+        const int cb_lo = (PAIR && !is_k) ? (int)rank * C::V_NCB : 0;
+        const int cb_bytes = is_k ? C::CB_K : C::CB_V;
+        auto part_bytes = [&](int t0, int r) {  // bytes CTA r loads of the tile at t0
+            const int n = max(0, min(key_cnt, kend - t0 - ((PAIR && is_k) ? r * H : 0)));
+            return (uint32_t)(((n + bh - 1) / bh) * bh * ncb * 128);
+        };
         for (int j = 0; j < nt; ++j) {
             const int idx = is_k ? kidx(j) : vidx(j);
             const int st = idx % C::NS;
             const int t0 = j * TT;
-            const int tg = t0 + lane * bh;
-            const bool mine = lane < TT / bh && tg < kend;
+            const int tg = t0 + key_off + lane * bh;
+            const bool mine = lane < key_cnt / bh && tg < kend;
+            // pair: each CTA counts its part of the last V tile on its own
+            // barrier, so its softmax warps can zero the rows past the end
+            const bool tail = PAIR && !is_k && j == nt - 1;
             int row0 = 0;
             if (mine) {
                 int pid = __ldg(trow + (tg >> lP));
@@ -195,59 +259,87 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             bool ok = true;
             if (lane == 0) {
                 if (idx >= C::NS) ok = mbar_wait(&empty[st], ((idx / C::NS) - 1) & 1, abort_flag, p.status);
-                const int groups = (min(TT, kend - t0) + bh - 1) / bh;
-                if (ok) mbar_expect_tx(&full[st], (uint32_t)(groups * bh * DH * 2));
+                if (ok) {
+                    if (tail)
+                        mbar_expect_tx(vtail, part_bytes(t0, (int)rank));
+                    else if (leader)
+                        mbar_expect_tx(&full[st], PAIR ? part_bytes(t0, 0) + part_bytes(t0, 1) : part_bytes(t0, 0));
+                }
             }
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
             if (mine) {
                 const uint32_t dst = smem_u32(stage(idx)) + (uint32_t)(lane * bh * 128);
-#pragma unroll
-                for (int cb = 0; cb < C::NCB; ++cb)
-                    tma_load_2d(dst + (uint32_t)(cb * C::CB_BYTES), map, cb * 64, row0, &full[st]);
+                const uint32_t lead_bar = PAIR && !leader && !tail ? mapa_shared(smem_u32(&full[st]), 0) : 0u;
+                for (int c = 0; c < ncb; ++c) {
+                    const uint32_t d = dst + (uint32_t)(c * cb_bytes);
+                    const int x = (cb_lo + c) * 64;
+                    if (tail)
+                        tma_load_2d(d, map, x, row0, vtail);
+                    else if (!PAIR || leader)
+                        tma_load_2d(d, map, x, row0, &full[st]);
+                    else
+                        tma_load_2d_pair(d, map, x, row0, lead_bar);
+                }
             }
             __syncwarp();
         }
     } else if (warp == kMmaWarp) {
-        // ============================================ MMA issue (lane 0)
-        if (lane == 0) {
-            constexpr uint32_t IDESC_QK = umma_idesc_f16(M, TT, 0);
-            constexpr uint32_t IDESC_PV = umma_idesc_f16(M, DH, 1);
+        // ============================================ MMA issue (lane 0 of the even CTA)
+        if (lane == 0 && leader) {
+            constexpr int MM = PAIR ? 2 * M : M;
+            constexpr uint32_t IDESC_QK = umma_idesc_f16(MM, TT, 0);
+            constexpr uint32_t IDESC_PV = umma_idesc_f16(MM, DH, 1);
+            auto commit = [&](uint64_t *bar) {  // this CTA's barrier and the peer's
+                if constexpr (PAIR) {
+                    umma_pair_commit(smem_u32(bar));
+                    umma_pair_commit(mapa_shared(smem_u32(bar), 1));
+                } else {
+                    umma_commit(bar);
+                }
+            };
             auto issue_pv = [&](int i) -> bool {
                 const int vi = vidx(i);
-                if (!mbar_wait(p_full, i & 1, abort_flag, p.status) ||
-                    !mbar_wait(&full[vi % C::NS], (vi / C::NS) & 1, abort_flag, p.status))
-                    return false;
+                if (!wait(p_full, i & 1)) return false;
+                // a pair's last V tile is covered by p_full: each softmax
+                // group waited for its CTA's part before arriving
+                if (!(PAIR && i == nt - 1) && !wait(&full[vi % C::NS], (vi / C::NS) & 1)) return false;
                 tc_fence_after();
                 const uint32_t sV = smem_u32(stage(vi));
                 const uint32_t sP = smem_u32(smem + C::OFF_P);
 #pragma unroll
                 for (int kk = 0; kk < TT / 16; ++kk) {
                     // P atom kk/4 holds keys 64*(kk/4) .. +63; V is MN-major:
-                    // 64-column blocks CB_BYTES apart (LBO), 8-key groups 1024
+                    // 64-column blocks CB_V apart (LBO), 8-key groups 1024
                     // bytes apart (SBO), 16 keys = 2048 bytes per K step.
                     const uint64_t a = umma_desc_sw128(sP + (kk >> 2) * M * 128 + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, C::CB_BYTES, 1024);
-                    umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, C::CB_V, 1024);
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    if constexpr (PAIR)
+                        umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
+                    else
+                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
                 }
-                umma_commit(&empty[vi % C::NS]);
-                umma_commit(p_free);
+                commit(&empty[vi % C::NS]);
+                commit(p_free);
                 return true;
             };
             bool ok = true;
             for (int j = 0; j < nt && ok; ++j) {
                 const int ki = kidx(j);
-                ok = mbar_wait(&full[ki % C::NS], (ki / C::NS) & 1, abort_flag, p.status) &&
-                     (j < 1 || mbar_wait(s_free, (j - 1) & 1, abort_flag, p.status));
+                ok = wait(&full[ki % C::NS], (ki / C::NS) & 1) && (j < 1 || wait(s_free, (j - 1) & 1));
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t sK = smem_u32(stage(ki));
 #pragma unroll
                 for (int ks = 0; ks < DH / 16; ++ks) {  // A = Q from tensor memory, 8 columns per K=16
-                    const uint64_t bd = umma_desc_sw128(sK + (ks >> 2) * C::CB_BYTES + (ks & 3) * 32, 16, 1024);
-                    umma_f16_ts(tmem, tmem + C::Q_COL + ks * 8, bd, IDESC_QK, ks > 0);
+                    const uint64_t bd = umma_desc_sw128(sK + (ks >> 2) * C::CB_K + (ks & 3) * 32, 16, 1024);
+                    if constexpr (PAIR)
+                        umma_pair_f16_ts(tmem, tmem + C::Q_COL + ks * 8, bd, IDESC_QK, ks > 0);
+                    else
+                        umma_f16_ts(tmem, tmem + C::Q_COL + ks * 8, bd, IDESC_QK, ks > 0);
                 }
-                umma_commit(s_full);
-                umma_commit(&empty[ki % C::NS]);
+                commit(s_full);
+                commit(&empty[ki % C::NS]);
                 if (j >= 1) ok = issue_pv(j - 1);
             }
             if (ok) issue_pv(nt - 1);
@@ -265,7 +357,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
-            if (!mbar_wait(s_full, j & 1, abort_flag, p.status)) {
+            if (!wait(s_full, j & 1)) {
                 ok = false;
                 break;
             }
@@ -279,7 +371,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
+            if (lane == 0) arrive_leader(s_free);
 
             const int t0 = j * TT;
             if (t0 + TT - 1 > all_visible) {
@@ -308,7 +400,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             const float nmu = m_ref == -INFINITY ? 0.f : -m_ref;
             if (j >= 1) {
                 // P.V of tile j-1 must be done before P is rewritten or O rescaled.
-                if (!mbar_wait(p_free, (j - 1) & 1, abort_flag, p.status)) {
+                if (!wait(p_free, (j - 1) & 1)) {
                     ok = false;
                     break;
                 }
@@ -345,28 +437,30 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             }
             l = l * factor + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
             const int nkeys = min(TT, kend - t0);
-            if (nkeys < TT) {
-                // last tile: V rows past the block's end hold stale data; P is
-                // 0 there, zero V too so 0 * V stays 0 (once the tile landed).
+            if (j == nt - 1 && (PAIR || nkeys < TT)) {
+                // last tile: once this CTA's part of V landed, zero its rows
+                // past the block's end (stale data; P is 0 there, and 0 * V
+                // must stay 0)
                 const int vi = vidx(j);
-                if (!mbar_wait(&full[vi % C::NS], (vi / C::NS) & 1, abort_flag, p.status)) {
+                const bool landed = PAIR ? wait(vtail, 0) : wait(&full[vi % C::NS], (vi / C::NS) & 1);
+                if (!landed) {
                     ok = false;
                     break;
                 }
                 uint8_t *sV = stage(vi);
-                for (int i = tid; i < (TT - nkeys) * (DH / 8); i += kSoftmaxWarps * 32) {
-                    const int key = nkeys + i / (DH / 8), c16 = i % (DH / 8);
-                    *reinterpret_cast<uint4 *>(sV + (c16 >> 3) * C::CB_BYTES + key * 128 +
+                for (int i = tid; i < (TT - nkeys) * (C::V_NCB * 8); i += kSoftmaxWarps * 32) {
+                    const int key = nkeys + i / (C::V_NCB * 8), c16 = i % (C::V_NCB * 8);
+                    *reinterpret_cast<uint4 *>(sV + (c16 >> 3) * C::CB_V + key * 128 +
                                                (((c16 & 7) ^ (key & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
             fence_proxy_async();  // P (and V zeroing) written by threads -> tensor core
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) arrive_leader(p_full);
         }
         // ---- epilogue: O / l for valid rows once the last P.V is done
-        if (ok && mbar_wait(p_free, (nt - 1) & 1, abort_flag, p.status)) {
+        if (ok && wait(p_free, (nt - 1) & 1)) {
             tc_fence_after();
             const float inv = 1.f / l;
             float *dst =
@@ -385,30 +479,55 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
             }
         }
     }
+    // No CTA of a pair frees tensor memory or leaves while the other may
+    // still use it or its shared memory.
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    if constexpr (PAIR)
+        cluster_sync();
+    else
+        __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem, C::TMEM_COLS);
+        else
+            tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
-template <int DH>
+template <int DH, bool PAIR>
 cudaError_t launch_chunk_t(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                            cudaStream_t s) {
-    auto kern = chunk_kernel<DH>;
+    auto kern = chunk_kernel<DH, PAIR>;
+    constexpr int smem = ChunkCfg<DH, PAIR>::SMEM_ALLOC;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             ChunkCfg<DH>::SMEM_ALLOC);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    dim3 grid(p.n_qblocks, p.kvh, p.n_seqs);
-    kern<<<grid, kChunkThreads, ChunkCfg<DH>::SMEM_ALLOC, s>>>(p, *tk, *tv);
-    return cudaGetLastError();
+    if constexpr (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * ((p.n_qblocks + 1) / 2), p.kvh, p.n_seqs);
+        cfg.blockDim = dim3(kChunkThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, p, *tk, *tv);
+    } else {
+        dim3 grid(p.n_qblocks, p.kvh, p.n_seqs);
+        kern<<<grid, kChunkThreads, smem, s>>>(p, *tk, *tv);
+        return cudaGetLastError();
+    }
 }
 
 }  // namespace
@@ -417,12 +536,15 @@ bool chunk_supported(int dh, int P, int G) {
     return (dh == 64 || dh == 128 || dh == 256) && P >= 8 && G >= 1 && G <= kChunkRows;
 }
 
+// CTA pairs when the chunk has two or more query blocks and dh splits into
+// two halves of whole 64-column blocks; one CTA per block otherwise.
 cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int dh,
                          cudaStream_t s) {
+    const bool pair = p.n_qblocks >= 2;
     switch (dh) {
-        case 64: return launch_chunk_t<64>(p, tk, tv, s);
-        case 128: return launch_chunk_t<128>(p, tk, tv, s);
-        case 256: return launch_chunk_t<256>(p, tk, tv, s);
+        case 64: return launch_chunk_t<64, false>(p, tk, tv, s);
+        case 128: return pair ? launch_chunk_t<128, true>(p, tk, tv, s) : launch_chunk_t<128, false>(p, tk, tv, s);
+        case 256: return pair ? launch_chunk_t<256, true>(p, tk, tv, s) : launch_chunk_t<256, false>(p, tk, tv, s);
         default: return cudaErrorInvalidValue;
     }
 }
