@@ -64,6 +64,9 @@ def parse_args():
     # a line measured with them is not the config-2 number
     ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: config 2's 6)")
+    ap.add_argument("--producer", action="store_true",
+                    help="config 2 through gkv_attn_step: raw fp32 q|gate, k, v projections, RMSNorm + RoPE "
+                         "+ output gate fused into the decode step (Qwen3.5 attention layer)")
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6],
                     help="BASELINE config: 2 decode (default, the headline), 3 MTP verify+rollback, "
                          "4 prefill chunk, 5 long-context sharded decode; 6 = the GDN state rollback "
@@ -675,6 +678,76 @@ def run_config5(args, rank, world, local):
         "clocks": clk}), flush=True)
 
 
+def run_config2_producer(args, rank, world, local):
+    """Config 2 geometry through gkv_attn_step: per layer, one call takes
+    each sequence's raw fp32 q|gate [nH, 2*dh], k and v [KVH, dh]
+    projections, RMSNorm's q and k, applies the partial NEOX rope (64 of 256
+    dims, base 1e7, per-position tables), appends, attends and gates the
+    output.  Same contexts, pools and timing as the default line."""
+    import torch
+    import torch.distributed as dist
+    import gadeon_b200 as gk
+    cfg = CONFIGS[2]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L, S = args.layers or cfg.layers, args.seqs or cfg.seqs
+    KVH, dh, G, nH = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads
+    n_rot, base = 64, 1e7
+    W, K = max(args.warmup, 3), args.steps
+    ctx = contexts(2, args.seed + 1000 * rank, S)
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, W + K + 2, local)
+    NS = W + K
+    qg = torch.randn((L, S, nH, 2 * dh), generator=gen, device=dev)
+    kr = torch.randn((L, S, KVH, dh), generator=gen, device=dev)
+    vr = torch.randn((L, S, KVH, dh), generator=gen, device=dev)
+    q_norm = 1 + 0.1 * torch.randn((L, dh), generator=gen, device=dev)
+    k_norm = 1 + 0.1 * torch.randn((L, dh), generator=gen, device=dev)
+    # rope tables of every step's positions (host helper), resident on the device
+    cos_np = np.empty((NS, S, n_rot // 2), dtype=np.float32)
+    sin_np = np.empty_like(cos_np)
+    for i in range(NS):
+        cos_np[i], sin_np[i] = gk.rope_table(n_rot, base, ctx + i)
+    cos_t, sin_t = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    outs = [torch.empty((S, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+
+    def step(i, ti):
+        for layer in range(L):
+            if ti is not None:
+                ev[ti * L + layer][0].record()
+            pools[layer].attn_step(ids[layer], G, qg[layer], kr[layer], vr[layer], q_norm[layer], k_norm[layer],
+                                   cos_t[i], sin_t[i], eps=1e-6, out=outs[layer])
+            if ti is not None:
+                ev[ti * L + layer][1].record()
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
+    # algorithmic bytes: the decode bytes (K/V once, q as fp16, fp32 out,
+    # table) with the fp16 q replaced by the fp32 q|gate row, plus the raw
+    # k/v read, the fp16 rows written, the rope rows and norm weights
+    prod_bytes = S * (nH * (2 * dh * 4 - dh * 2) + KVH * dh * (4 * 2 + 2 * 2) + n_rot * 4) + 2 * dh * 4
+    bpl = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K)) + prod_bytes
+    hbm, kind = peaks()
+    for p_ in pools:
+        assert p_.device_status() == 0
+    if rank != 0:
+        return
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "KV append+attend tok/s through gkv_attn_step (config 2, producer fused)",
+        "value": S * world / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 projections in, fp16 K/V/Q storage, f32 accumulate",
+        "data": "synthetic (seeded N(0,1): fp16 contexts, fp32 projections)",
+        "config": {"workload": f"config2 + producer: {S} seqs/GPU x {L} layers, ctx ~U[1024,32768], "
+                               f"q/k RMSNorm, rope {n_rot}/{dh} base {base:g}, sigmoid output gate",
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append,producer>",
+                     "bytes_per_launch": bpl, "launch_ms": launch_ms},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * L, "clocks": clk}), flush=True)
+
+
 def run_config6(args, rank, world, local):
     """GDN rollback beside config 3: per step, every one of 128 sequences
     (per GPU) rolls back the recurrent state and conv tail of its 3 GDN
@@ -772,6 +845,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6}[args.config]
+        if args.config == 2 and args.producer:
+            runner = run_config2_producer
         runner(args, rank, world, local)
     finally:
         if world > 1:

@@ -22,4 +22,5 @@ from .kv import (  # noqa: F401
     host_flash_decode,
     load_library,
     mtp_rollback,
+    rope_table,
 )

@@ -156,6 +156,86 @@ __device__ __forceinline__ uint32_t q_off(int row, int c16) {
     return (uint32_t)(((c16 >> 3) * kRows + row) * 128 + (((c16 & 7) ^ (row & 7)) << 4));
 }
 
+// ---- producer fusion helpers (SIMD/Attention.swift:72-139)
+// One head row of a projection, held by a warp: lane owns elements
+// [lane*E, lane*E + E), E = DH/32.  RMSNorm with weight w (Kernels.swift
+// :26-37: x * (1 / sqrt(mean(x^2) + eps)) * w), then NEOX RoPE of the first
+// n_rot elements with the token's cos/sin row (Kernels.swift:66-84: pair
+// (i, i + n_rot/2) -> (a c - b s, a s + b c)).  Products and sums are rounded
+// one at a time, as the reference writes them (no fused multiply-add).
+template <int DH>
+__device__ __forceinline__ void produce_row(const float *x, const float *w, float eps, const float *cs,
+                                            const float *sn, int n_rot, int lane, float (&v)[DH / 32]) {
+    constexpr int E = DH / 32;
+    const int half = n_rot >> 1, d0 = lane * E;  // half % E == 0 (host check)
+    const bool lo = d0 < half, hi = !lo && d0 < n_rot;
+    const int src = lo ? lane + half / E : (hi ? lane - half / E : lane);
+    const int ti = lo ? d0 : (hi ? d0 - half : 0);
+    // every global load first: one memory latency per row, not three
+    float wv[E], cv[E], sv[E];
+#pragma unroll
+    for (int i = 0; i < E; i += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(x + d0 + i));
+        v[i] = t.x;
+        v[i + 1] = t.y;
+        v[i + 2] = t.z;
+        v[i + 3] = t.w;
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        wv[i] = __ldg(w + d0 + i);
+        cv[i] = (lo || hi) ? __ldg(cs + ti + i) : 1.f;
+        sv[i] = (lo || hi) ? __ldg(sn + ti + i) : 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float inv = 1.f / sqrtf(ss / (float)DH + eps);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const float pv = __shfl_sync(0xffffffffu, v[i], src);
+        if (lo)
+            v[i] = __fsub_rn(__fmul_rn(v[i], cv[i]), __fmul_rn(pv, sv[i]));
+        else if (hi)
+            v[i] = __fadd_rn(__fmul_rn(pv, sv[i]), __fmul_rn(v[i], cv[i]));
+    }
+}
+
+// This lane's E elements as fp16 (round to nearest even) at dst + lane*E.
+template <int DH>
+__device__ __forceinline__ void store_row_f16(uint16_t *dst, int lane, const float (&v)[DH / 32]) {
+    constexpr int E = DH / 32;
+    if constexpr (E == 8) {
+        *reinterpret_cast<uint4 *>(dst + lane * E) = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                                                                pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
+    } else {
+        static_assert(E == 4, "producer rows of 128 or 256 elements");
+        *reinterpret_cast<uint2 *>(dst + lane * E) = make_uint2(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]));
+    }
+}
+
+// A raw fp32 row rounded to fp16 (V of a producer step).
+template <int DH>
+__device__ __forceinline__ void copy_row_f16(uint16_t *dst, const float *x, int lane) {
+    float v[DH / 32];
+#pragma unroll
+    for (int i = 0; i < DH / 32; i += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(x + lane * (DH / 32) + i));
+        v[i] = t.x;
+        v[i + 1] = t.y;
+        v[i + 2] = t.z;
+        v[i + 3] = t.w;
+    }
+    store_row_f16<DH>(dst, lane, v);
+}
+
+// sigmoid(x) = 1 / (1 + exp(-x)) (Kernels.swift:6), the output gate.
+__device__ __forceinline__ float sigmoid_gate(float x) { return 1.f / (1.f + expf(-x)); }
+
 // Walks work units in order: unit -> (sequence b, kv head, tile j).
 struct UnitWalker {
     const AttendEntry *entries;
@@ -189,7 +269,7 @@ __device__ __forceinline__ int cta_of_unit(int64_t u, int64_t units, int64_t cta
     return (int)(((u + 1) * ctas - 1) / units);
 }
 
-template <int DH, bool TMA, bool FUSED>
+template <int DH, bool TMA, bool FUSED, bool PROD>
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ AttendParams p, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv) {
@@ -238,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the page is fresh (PagePool.zeroPage) -- then fence the stores
         // against the TMA reads that follow.
         UnitWalker a = w;
-        int u = u_begin;
+        int u = u_begin, n_own = 0;
         while (u < u_end) {
             const int item_last = a.e.unit_base + a.kvh * a.e.ntiles + a.e.ntiles - 1;
             if (item_last < u_end) {
@@ -247,14 +327,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t slab = ((int64_t)ft.pid * KVH + a.kvh) * p.P * DH;
                 uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
                 uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
-                const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
-                const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
                 const int rows = ft.fresh ? p.P : 1;
-                for (int i = threadIdx.x; i < rows * C::CH; i += kThreads) {
-                    const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
-                    const bool mine = row == slot;
-                    kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
-                    vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (PROD) {
+                    // every other row of a fresh page is zeroed by all
+                    // threads; one warp builds the new K/V row from the raw
+                    // projections (items round-robin over the warps)
+                    if (ft.fresh)
+                        for (int i = threadIdx.x; i < rows * C::CH; i += kThreads)
+                            if (i / C::CH != slot) {
+                                kd[i] = make_uint4(0u, 0u, 0u, 0u);
+                                vd[i] = make_uint4(0u, 0u, 0u, 0u);
+                            }
+                    if (warp == n_own % (kThreads / 32)) {
+                        const int64_t row = (int64_t)a.b * KVH + a.kvh;
+                        const int64_t tok = (int64_t)a.b * p.n_q + p.n_q - 1;  // the new row's token
+                        const int hr = p.prod.n_rot >> 1;
+                        float kv[DH / 32];
+                        produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps,
+                                        p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr, p.prod.n_rot, lane,
+                                        kv);
+                        store_row_f16<DH>(p.k_pool_w + slab + (int64_t)slot * DH, lane, kv);
+                        copy_row_f16<DH>(p.v_pool_w + slab + (int64_t)slot * DH, p.prod.v_raw + row * DH, lane);
+                    }
+                    ++n_own;
+                } else {
+                    const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                    const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                    for (int i = threadIdx.x; i < rows * C::CH; i += kThreads) {
+                        const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
+                        const bool mine = row == slot;
+                        kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
+                        vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
+                    }
                 }
                 if (ft.fresh && a.kvh == 0 && threadIdx.x == 0)
                     p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx] = ft.pid;
@@ -367,16 +471,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = w.b, kvh = w.kvh, j = w.j, len = w.e.len;
         if (item_start) {
             consumer_sync();  // earlier readers of sQ are done
-            for (int i = tid; i < kRows * C::CH; i += 128) {
-                const int row = i / C::CH, c16 = i - row * C::CH;
-                uint4 val = make_uint4(0u, 0u, 0u, 0u);
-                if (row < R) {
-                    const int s = row / G, g = row - s * G;
-                    const uint16_t *src =
-                        p.q + (((int64_t)b * p.n_q + s) * nH + kvh * G + g) * DH + c16 * 8;
-                    val = *reinterpret_cast<const uint4 *>(src);
+            if constexpr (PROD) {
+                // q rows from the raw q|gate projection: warp w builds rows
+                // w, w+4, ... (RMSNorm + RoPE), lane l its DH/32 elements
+                constexpr int E = DH / 32;
+                const int hr = p.prod.n_rot >> 1;
+                for (int row = warp; row < kRows; row += kConsumerWarps) {
+                    float qv[E];
+                    if (row < R) {
+                        const int s = row / G, g = row - s * G;
+                        const int64_t tok = (int64_t)b * p.n_q + s;
+                        produce_row<DH>(p.prod.q_gate + (tok * nH + kvh * G + g) * (2 * DH), p.prod.q_norm,
+                                        p.prod.eps, p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr,
+                                        p.prod.n_rot, lane, qv);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < E; ++i) qv[i] = 0.f;
+                    }
+                    uint8_t *dst = sQ + q_off(row, lane * E / 8) + (lane * E % 8) * 2;
+                    if constexpr (E == 8)
+                        *reinterpret_cast<uint4 *>(dst) = make_uint4(pack_half2(qv[0], qv[1]), pack_half2(qv[2], qv[3]),
+                                                                     pack_half2(qv[4], qv[5]), pack_half2(qv[6], qv[7]));
+                    else
+                        *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_half2(qv[0], qv[1]), pack_half2(qv[2], qv[3]));
                 }
-                *reinterpret_cast<uint4 *>(sQ + q_off(row, c16)) = val;
+            } else {
+                for (int i = tid; i < kRows * C::CH; i += 128) {
+                    const int row = i / C::CH, c16 = i - row * C::CH;
+                    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+                    if (row < R) {
+                        const int s = row / G, g = row - s * G;
+                        const uint16_t *src =
+                            p.q + (((int64_t)b * p.n_q + s) * nH + kvh * G + g) * DH + c16 * 8;
+                        val = *reinterpret_cast<const uint4 *>(src);
+                    }
+                    *reinterpret_cast<uint4 *>(sQ + q_off(row, c16)) = val;
+                }
             }
             consumer_sync();
             if constexpr (C::Q_REGS) {
@@ -566,9 +696,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float *dst = p.out + (((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * DH;
                         const float inv = half ? i1 : i0;
 #pragma unroll
-                        for (int n = 0; n < C::NT_PV; ++n)
-                            *reinterpret_cast<float2 *>(dst + col0 + n * 8) =
-                                make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+                        for (int n = 0; n < C::NT_PV; ++n) {
+                            float2 r2 = make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+                            if constexpr (PROD) {  // attnOut *= sigmoid(gate) (Attention.swift:133-135)
+                                const float *gt = p.prod.q_gate +
+                                                  (((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * (2 * DH) + DH;
+                                r2.x *= sigmoid_gate(__ldg(gt + col0 + n * 8));
+                                r2.y *= sigmoid_gate(__ldg(gt + col0 + n * 8 + 1));
+                            }
+                            *reinterpret_cast<float2 *>(dst + col0 + n * 8) = r2;
+                        }
                     }
                 }
             } else {
@@ -618,7 +755,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             Os += __ldcg(pk + 32 + (int64_t)row * DH + d) * wk;
                         }
                         const int s_ = row / G, g = row - s_ * G;
-                        p.out[(((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * DH + d] = Os / Ls;
+                        const int64_t orow = ((int64_t)b * p.n_q + s_) * nH + kvh * G + g;
+                        float res = Os / Ls;
+                        if constexpr (PROD) res *= sigmoid_gate(__ldg(p.prod.q_gate + orow * (2 * DH) + DH + d));
+                        p.out[orow * DH + d] = res;
                     }
                 }
             }
@@ -628,10 +768,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int DH, bool TMA, bool FUSED = false>
+template <int DH, bool TMA, bool FUSED = false, bool PROD = false>
 cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                             int grid, cudaStream_t s) {
-    auto kern = attend_kernel<DH, TMA, FUSED>;
+    auto kern = attend_kernel<DH, TMA, FUSED, PROD>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -677,9 +817,54 @@ int attend_grid(int dh, int P, int units, int sm_count) {
     return units < sm_count ? units : sm_count;
 }
 
+// dh 128 / 256 with the producer fusion: TMA (fused append or not) or the
+// cp.async loader (P < 8, append done beforehand).
+template <int DH>
+cudaError_t launch_attend_prod(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int grid,
+                               cudaStream_t s) {
+    if (p.P < 8) return launch_attend_t<DH, false, false, true>(p, tk, tv, grid, s);
+    return p.tails ? launch_attend_t<DH, true, true, true>(p, tk, tv, grid, s)
+                   : launch_attend_t<DH, true, false, true>(p, tk, tv, grid, s);
+}
+
+// grid: n_seqs * KVH rows, 4 warps per block, one warp per row.
+template <int DH>
+__global__ void __launch_bounds__(128) produce_kv_kernel(const __grid_constant__ ProduceParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (row >= (int64_t)p.n_seqs * p.kvh) return;
+    const int64_t b = row / p.kvh;
+    const int hr = p.prod.n_rot >> 1;
+    float kv[DH / 32];
+    produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps, p.prod.rope_cos + b * hr,
+                    p.prod.rope_sin + b * hr, p.prod.n_rot, lane, kv);
+    store_row_f16<DH>(p.k_out + row * DH, lane, kv);
+    copy_row_f16<DH>(p.v_out + row * DH, p.prod.v_raw + row * DH, lane);
+}
+
+bool producer_supported(int dh) { return dh == 128 || dh == 256; }
+
+cudaError_t launch_produce_kv(const ProduceParams &p, int dh, cudaStream_t s) {
+    const int64_t rows = (int64_t)p.n_seqs * p.kvh;
+    if (rows <= 0) return cudaSuccess;
+    const unsigned blocks = (unsigned)((rows + 3) / 4);
+    if (dh == 256)
+        produce_kv_kernel<256><<<blocks, 128, 0, s>>>(p);
+    else if (dh == 128)
+        produce_kv_kernel<128><<<blocks, 128, 0, s>>>(p);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
 cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                           int dh, int grid, cudaStream_t s) {
     const bool tma = p.P >= 8;
+    if (p.prod.q_gate) {
+        if (dh == 128) return launch_attend_prod<128>(p, tk, tv, grid, s);
+        if (dh == 256) return launch_attend_prod<256>(p, tk, tv, grid, s);
+        return cudaErrorInvalidValue;
+    }
     switch (dh) {
         case 64: return tma ? launch_attend_t<64, true>(p, tk, tv, grid, s)
                             : launch_attend_t<64, false>(p, tk, tv, grid, s);

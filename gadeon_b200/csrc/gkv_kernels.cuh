@@ -67,6 +67,21 @@ struct FusedTail {
     int32_t pad;
 };
 
+// Producer fusion (gkv_attn_step; q_gate == nullptr turns it off): the
+// attend kernel builds its fp16 q rows from the raw q|gate projections --
+// RMSNorm with q_norm, then partial NEOX RoPE of the first n_rot elements
+// with the token's cos/sin row -- and multiplies every output by sigmoid of
+// the gate half; the fused append builds the new K row the same way from
+// k_raw (k_norm) and rounds v_raw to fp16 (SIMD/Attention.swift:72-139).
+struct ProducerArgs {
+    const float *q_gate;               // [n_seqs, n_q, KVH*G, 2*dh]: q | gate per head
+    const float *k_raw, *v_raw;        // [n_seqs, KVH, dh]
+    const float *q_norm, *k_norm;      // [dh]
+    const float *rope_cos, *rope_sin;  // [n_seqs, n_q, n_rot/2]
+    int32_t n_rot;
+    float eps;
+};
+
 struct AttendParams {
     const AttendEntry *entries;
     int32_t n_seqs;
@@ -89,6 +104,15 @@ struct AttendParams {
     int32_t *status;         // device status word
     int32_t n_q, G, kvh, P, num_pages;
     float scale_log2;        // scale * log2(e)
+    ProducerArgs prod;
+};
+
+// K/V rows of a producer step built outside the attend kernel (when the
+// append cannot be fused): k_out/v_out [n_seqs, KVH, dh] fp16.
+struct ProduceParams {
+    ProducerArgs prod;
+    uint16_t *k_out, *v_out;
+    int32_t n_seqs, kvh;
 };
 
 // Host-side launchers (gkv_kernels.cu).
@@ -102,6 +126,9 @@ cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tmap_k,
                           cudaStream_t s);
 // Key tile length used by the attend kernel for head_dim dh.
 int attend_tile_keys(int dh);
+// True when the attend kernel can run the producer fusion for head_dim dh.
+bool producer_supported(int dh);
+cudaError_t launch_produce_kv(const ProduceParams &p, int dh, cudaStream_t s);
 
 // ---------------------------------------------------------------- chunk
 // Causal attention for many query rows per (sequence, kv head): prefill

@@ -168,6 +168,7 @@ struct gkv_pool {
     int32_t *d_status = nullptr;
     float *d_partials = nullptr;
     int32_t *d_counters = nullptr;
+    uint16_t *d_prod = nullptr;  // [2][max_seqs * KVH * dh] fp16 K/V rows of gkv_attn_step's unfused route
     CUtensorMap tmk{}, tmv{};
     std::vector<int32_t> stack;  // free list; back() is the head
     std::vector<int32_t> ref;
@@ -328,7 +329,7 @@ int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_
 int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
                    const void *q, float *out, float scale, cudaStream_t st,
                    const gkv::FusedTail *tails = nullptr, const void *k_new = nullptr,
-                   const void *v_new = nullptr) {
+                   const void *v_new = nullptr, const gkv::ProducerArgs *prod = nullptr) {
     if (n == 0) return GKV_OK;
     const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
     cudaError_t err;
@@ -397,6 +398,7 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
     p.P = pool->cfg.page_tokens;
     p.num_pages = pool->cfg.num_pages;
     p.scale_log2 = scale * 1.4426950408889634f;
+    if (prod) p.prod = *prod;
     const int grid = gkv::attend_grid(pool->cfg.head_dim, p.P, (int)units, pool->sm_count);
     GKV_CUDA(gkv::launch_attend(p, &pool->tmk, &pool->tmv, pool->cfg.head_dim, grid, st),
              "attend kernel launch");
@@ -412,6 +414,8 @@ void free_device(gkv_pool *p) {
     cudaFree(p->d_status);
     cudaFree(p->d_partials);
     cudaFree(p->d_counters);
+    cudaFree(p->d_prod);
+    p->d_prod = nullptr;
     p->d_k = p->d_v = nullptr;
     p->d_table = p->d_status = p->d_counters = nullptr;
     p->d_partials = nullptr;
@@ -505,6 +509,7 @@ int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out) {
     GKV_ALLOC(p->d_partials,
               sizeof(float) * (items + p->sm_count) * gkv::attend_partial_floats(c.head_dim));
     GKV_ALLOC(p->d_counters, sizeof(int32_t) * items);
+    if (gkv::producer_supported(c.head_dim)) GKV_ALLOC(p->d_prod, sizeof(uint16_t) * 2 * items * c.head_dim);
 #undef GKV_ALLOC
     if ((e = cudaMemset(p->d_table, 0xff, sizeof(int32_t) * (size_t)c.max_seqs *
                                               c.max_pages_per_seq)) != cudaSuccess ||
@@ -697,6 +702,72 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
     rc = enqueue_append(pool, entries, pages, k, v, 0, st);
     if (rc) return rc;
     return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st);
+}
+
+int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t group, const float *q_gate,
+                  const float *k_raw, const float *v_raw, const float *q_norm, const float *k_norm, float eps,
+                  const float *rope_cos, const float *rope_sin, int32_t n_rot, float scale, float *out,
+                  void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    const int dh = pool->cfg.head_dim;
+    if (!gkv::producer_supported(dh)) return fail(GKV_ERR_UNSUPPORTED, "gkv_attn_step needs head_dim 128 or 256");
+    if (group < 1 || group > 16) return fail(GKV_ERR_INVALID, "group=%d (1..16 query heads per kv head)", group);
+    if (n_rot < 16 || n_rot > dh || n_rot % 16)
+        return fail(GKV_ERR_INVALID, "n_rot=%d (a multiple of 16 in 16..%d)", n_rot, dh);
+    if (!(std::isfinite(eps) && eps >= 0.f)) return fail(GKV_ERR_INVALID, "eps must be finite and >= 0");
+    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
+    if (n_seqs > 0 && (!q_gate || !k_raw || !v_raw || !q_norm || !k_norm || !rope_cos || !rope_sin || !out))
+        return fail(GKV_ERR_INVALID, "null argument");
+    if (!aligned16(q_gate) || !aligned16(k_raw) || !aligned16(v_raw) || !aligned16(out) ||
+        ((reinterpret_cast<uintptr_t>(q_norm) | reinterpret_cast<uintptr_t>(k_norm) |
+          reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 3))
+        return fail(GKV_ERR_INVALID, "q_gate/k_raw/v_raw/out must be 16-byte aligned, the rest 4-byte");
+    DeviceGuard guard(pool->cfg.device);
+    std::vector<int32_t> n_new(n_seqs, 1);
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
+    if (rc) return rc;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    gkv::ProducerArgs prod{q_gate, k_raw, v_raw, q_norm, k_norm, rope_cos, rope_sin, n_rot, eps};
+    // Same fusion rule as gkv_append_attend: TMA-staged pages and no shared
+    // tail page -> the attend kernel's prologue builds and writes the rows.
+    bool fuse = pool->cfg.page_tokens >= 8 && (int32_t)pages.size() == n_seqs;
+    for (size_t i = 0; fuse && i < pages.size(); ++i) fuse = pages[i].entry == (int32_t)i && pages[i].src_pid < 0;
+    if (fuse) {
+        std::vector<gkv::FusedTail> tails(n_seqs);
+        for (int32_t i = 0; i < n_seqs; ++i)
+            tails[i] = {pages[i].pid, pages[i].pidx, pages[i].src_pid == gkv::PAGE_NEW ? 1 : 0, 0};
+        return enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, st, tails.data(), nullptr,
+                              nullptr, &prod);
+    }
+    // Otherwise the rows are built by a small kernel, appended (copy-on-write
+    // of a shared tail included), then attended.
+    const size_t rows = (size_t)n_seqs * pool->cfg.kv_heads;
+    gkv::ProduceParams pp{prod, pool->d_prod, pool->d_prod + rows * dh, n_seqs, pool->cfg.kv_heads};
+    GKV_CUDA(gkv::launch_produce_kv(pp, dh, st), "producer kernel launch");
+    rc = enqueue_append(pool, entries, pages, pp.k_out, pp.v_out, 0, st);
+    if (rc) return rc;
+    return enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, st, nullptr, nullptr, nullptr, &prod);
+}
+
+int gkv_rope_table(int32_t n_rot, float base, int32_t n, const int64_t *positions, float *cos_out,
+                   float *sin_out) {
+    if (n_rot < 2 || n_rot % 2 || !(std::isfinite(base) && base > 0.f) || n < 0)
+        return fail(GKV_ERR_INVALID, "n_rot=%d base=%g n=%d", n_rot, (double)base, n);
+    if (n > 0 && (!positions || !cos_out || !sin_out)) return fail(GKV_ERR_INVALID, "null argument");
+    const int half = n_rot / 2;
+    for (int32_t t = 0; t < n; ++t)
+        for (int i = 0; i < half; ++i) {
+            // Kernels.swift:74-76: freq = base^(-2i/nRot), angle = pos * freq (fp32)
+            const float freq = powf(base, -2.0f * (float)i / (float)n_rot);
+            const float ang = (float)positions[t] * freq;
+            cos_out[(size_t)t * half + i] = cosf(ang);
+            sin_out[(size_t)t * half + i] = sinf(ang);
+        }
+    return GKV_OK;
 }
 
 int gkv_truncate(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int64_t *new_len) {

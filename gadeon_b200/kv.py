@@ -45,7 +45,8 @@ EXPORTED = (
     "gkv_append", "gkv_seed", "gkv_attend", "gkv_append_attend", "gkv_truncate",
     "gkv_clone_seq", "gkv_compact_seq", "gkv_from_compact", "gkv_export_table",
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
-    "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback",
+    "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
+    "gkv_rope_table",
 )
 
 
@@ -103,6 +104,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_attend_noalloc": (C.c_int, [P, P, i32, i32, i32, i32, P, i32, i32, i32p, i32, i32, P, P,
                                          f32, P]),
         "gkv_mtp_rollback": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
+        "gkv_attn_step": (C.c_int, [P, i32, i32p, i32, P, P, P, P, P, f32, P, P, i32, f32, P, P]),
+        "gkv_rope_table": (C.c_int, [i32, f32, i32, i64p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
         "gkv_conv_rollback": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
@@ -273,6 +276,35 @@ class BlockPool:
         _check(_lib.gkv_append_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(k),
                                       _dev_ptr(v), _dev_ptr(q), _dev_ptr(out), float(scale),
                                       _stream_ptr(stream)))
+        return out
+
+    def attn_step(self, seq_ids: Sequence[int], group: int, q_gate, k_raw, v_raw, q_norm, k_norm,
+                  rope_cos, rope_sin, eps: float = 1e-6, out=None, scale: Optional[float] = None,
+                  stream=None):
+        """One decode token from raw fp32 projections (``gkv_attn_step``,
+        the reference's ``Attn.step``): q|gate split, q/k RMSNorm, partial
+        NEOX RoPE (n_rot = 2 * rope_cos.shape[-1]), append, attend, sigmoid
+        output gate.  Returns out [n_seqs, kv_heads*group, head_dim] fp32."""
+        import torch
+        ids = _i32(seq_ids)
+        n, KVH, dh = len(ids), self.kv_heads, self.head_dim
+        half = int(rope_cos.shape[-1])
+        _check_shape("q_gate", q_gate, (n, KVH * group, 2 * dh), ("float32",))
+        _check_shape("k_raw", k_raw, (n, KVH, dh), ("float32",))
+        _check_shape("v_raw", v_raw, (n, KVH, dh), ("float32",))
+        _check_shape("q_norm", q_norm, (dh,), ("float32",))
+        _check_shape("k_norm", k_norm, (dh,), ("float32",))
+        _check_shape("rope_cos", rope_cos, (n, half), ("float32",))
+        _check_shape("rope_sin", rope_sin, (n, half), ("float32",))
+        if out is None:
+            out = torch.empty((n, KVH * group, dh), dtype=torch.float32, device=q_gate.device)
+        _check_shape("out", out, (n, KVH * group, dh), ("float32",))
+        if scale is None:
+            scale = dh ** -0.5
+        _check(_lib.gkv_attn_step(self._h, n, _p32(ids), group, _dev_ptr(q_gate), _dev_ptr(k_raw),
+                                  _dev_ptr(v_raw), _dev_ptr(q_norm), _dev_ptr(k_norm), float(eps),
+                                  _dev_ptr(rope_cos), _dev_ptr(rope_sin), 2 * half, float(scale),
+                                  _dev_ptr(out), _stream_ptr(stream)))
         return out
 
     def truncate(self, seq_ids: Sequence[int], new_len: Sequence[int]):
@@ -448,3 +480,15 @@ def conv_rollback(m, proj, pre, out=None, stream=None):
     _check(L.gkv_conv_rollback(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out),
                                _stream_ptr(stream)))
     return out
+
+
+def rope_table(n_rot: int, base: float, positions) -> tuple:
+    """``gkv_rope_table``: cos and sin tables [n, n_rot/2] (numpy fp32) for
+    the given token positions, angle = pos * base^(-2i/n_rot) in fp32."""
+    L = load_library()
+    pos = _i64(positions)
+    cos = np.empty((len(pos), n_rot // 2), dtype=np.float32)
+    sin = np.empty_like(cos)
+    _check(L.gkv_rope_table(n_rot, float(base), len(pos), _p64(pos),
+                            cos.ctypes.data_as(C.POINTER(C.c_float)), sin.ctypes.data_as(C.POINTER(C.c_float))))
+    return cos, sin

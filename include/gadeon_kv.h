@@ -120,6 +120,33 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                       const void *v, const void *q, float *out, float scale,
                       void *stream);
 
+/* One decode token of a Qwen3.5 full-attention layer from its raw
+ * projections, with the producer and the output gate fused into the append
+ * and attention (Attn.step, LLM/src/SIMD/Attention.swift:72-139; Metal
+ * split_qgate / rope_neox / gated attn_head, LLM/metal/Kernels.metal
+ * :1100-1117, :1250-1262, :1330-1332):
+ *   q, gate = split of q_gate [n_seqs, kv_heads*group, 2*head_dim] per head
+ *   q = rope(rmsnorm(q, q_norm)), k = rope(rmsnorm(k_raw, k_norm))
+ *   append (k, v_raw) as fp16 rows; out = attend(q) * sigmoid(gate)
+ * rmsnorm: x / sqrt(mean(x^2) + eps) * w (Kernels.swift:26-37); rope: NEOX
+ * on the first n_rot elements, pair (i, i + n_rot/2) rotated by this token's
+ * rope_cos / rope_sin row [n_seqs, n_rot/2] (Kernels.swift:66-84; the
+ * CoreML engine feeds such tables to its programs, Engine.swift:2168-2181).
+ * k_raw, v_raw [n_seqs, kv_heads, head_dim]; q_norm, k_norm [head_dim];
+ * out [n_seqs, kv_heads*group, head_dim]; every buffer fp32 on the device.
+ * head_dim 128 or 256, group <= 16, n_rot a multiple of 16 <= head_dim. */
+int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                  int32_t group, const float *q_gate, const float *k_raw,
+                  const float *v_raw, const float *q_norm, const float *k_norm,
+                  float eps, const float *rope_cos, const float *rope_sin,
+                  int32_t n_rot, float scale, float *out, void *stream);
+
+/* Host helper: rope tables for gkv_attn_step, row t for position
+ * positions[t]: angle = pos * base^(-2i/n_rot) in fp32, cos/sin (the
+ * formula of Kernels.swift:74-76).  cos_out, sin_out: HOST [n, n_rot/2]. */
+int gkv_rope_table(int32_t n_rot, float base, int32_t n,
+                   const int64_t *positions, float *cos_out, float *sin_out);
+
 /* PagePool.truncate(to:) for a batch (PagedAttention.swift:181-189; the
  * rollback of Engine.decodeSpecStep :2787, :2792): lengths drop to
  * new_len[i]; whole pages past ceil(new_len/P) leave the table last-first and

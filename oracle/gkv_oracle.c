@@ -695,3 +695,60 @@ void orc_conv_rollback(int n, const int32_t *m, int CD, int taps, int C,
         }
     }
 }
+
+/* ------------------------------------------------------------------------
+ * Producer of a Qwen3.5 full-attention step (SIMD/Attention.swift:72-139),
+ * restated for gkv_attn_step's parity tests.  Every product and sum is
+ * rounded on its own, as the Swift source writes them (no contraction into
+ * fused multiply-adds).
+ */
+#pragma GCC push_options
+#pragma GCC optimize("fp-contract=off")
+
+/* Kern.rmsnormRows (SIMD/Kernels.swift:26-37): each row of d floats becomes
+ * x * (1 / sqrt(sum(x^2) / d + eps)) * w, in place. */
+void orc_rmsnorm_rows(float *x, int d, int rows, const float *w, float eps) {
+    for (int r = 0; r < rows; ++r) {
+        float *p = x + (size_t)r * d;
+        float ss = 0.f;
+        for (int i = 0; i < d; ++i) ss += p[i] * p[i];
+        const float s = 1.f / sqrtf(ss / (float)d + eps);
+        for (int i = 0; i < d; ++i) p[i] = p[i] * s * w[i];
+    }
+}
+
+/* Kern.ropeNeox (SIMD/Kernels.swift:66-84) with the angle's cos / sin given
+ * per pair: for every head, pair (i, i + n_rot/2), i < n_rot/2, becomes
+ * (a c - b s, a s + b c); elements past n_rot are untouched. */
+void orc_rope_neox(float *x, int head_dim, int n_head, int n_rot, const float *cs, const float *sn) {
+    const int half = n_rot / 2;
+    for (int h = 0; h < n_head; ++h) {
+        float *p = x + (size_t)h * head_dim;
+        for (int i = 0; i < half; ++i) {
+            const float a = p[i], b = p[i + half];
+            p[i] = a * cs[i] - b * sn[i];
+            p[i + half] = a * sn[i] + b * cs[i];
+        }
+    }
+}
+
+/* The angle of ropeNeox (Kernels.swift:74-76): freq = base^(-2i/n_rot),
+ * angle = pos * freq, in fp32; tables [n, n_rot/2]. */
+void orc_rope_table(int n_rot, float base, int n, const int64_t *pos, float *cs, float *sn) {
+    const int half = n_rot / 2;
+    for (int t = 0; t < n; ++t)
+        for (int i = 0; i < half; ++i) {
+            const float freq = powf(base, -2.f * (float)i / (float)n_rot);
+            const float ang = (float)pos[t] * freq;
+            cs[(size_t)t * half + i] = cosf(ang);
+            sn[(size_t)t * half + i] = sinf(ang);
+        }
+}
+
+/* attnOut[i] *= sigmoidf(gate[i]) (Attention.swift:133-135, sigmoidf =
+ * 1 / (1 + expf(-x)), Kernels.swift:6). */
+void orc_gate(float *x, const float *gate, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) x[i] *= 1.f / (1.f + expf(-gate[i]));
+}
+
+#pragma GCC pop_options

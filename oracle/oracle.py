@@ -76,6 +76,10 @@ def lib():
         "orc_mtp_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p,
                                     f32p, f32p]),
         "orc_conv_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p]),
+        "orc_rmsnorm_rows": (None, [f32p, C.c_int, C.c_int, f32p, C.c_float]),
+        "orc_rope_neox": (None, [f32p, C.c_int, C.c_int, C.c_int, f32p, f32p]),
+        "orc_rope_table": (None, [C.c_int, C.c_float, C.c_int, i64p, f32p, f32p]),
+        "orc_gate": (None, [f32p, f32p, C.c_int64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -254,3 +258,38 @@ def conv_rollback(m, proj, pre) -> np.ndarray:
     lib().orc_conv_rollback(n, _ptr(mm, C.c_int32), CD, taps, Cw, _ptr(proj, C.c_float), _ptr(pre, C.c_float),
                             _ptr(out, C.c_float))
     return out
+
+
+def rmsnorm_rows(x, w, eps) -> np.ndarray:
+    """Kern.rmsnormRows restated: every row of the last axis normalised."""
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    d = x.shape[-1]
+    lib().orc_rmsnorm_rows(_ptr(x, C.c_float), d, x.size // d, _ptr(w, C.c_float), float(eps))
+    return x
+
+
+def rope_neox(x, n_rot, cos_row, sin_row) -> np.ndarray:
+    """Kern.ropeNeox restated with one token's cos / sin row; x [n_head, head_dim]."""
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    cs = np.ascontiguousarray(cos_row, dtype=np.float32)
+    sn = np.ascontiguousarray(sin_row, dtype=np.float32)
+    lib().orc_rope_neox(_ptr(x, C.c_float), x.shape[-1], x.size // x.shape[-1], int(n_rot), _ptr(cs, C.c_float),
+                        _ptr(sn, C.c_float))
+    return x
+
+
+def rope_table(n_rot, base, positions):
+    pos = np.ascontiguousarray(positions, dtype=np.int64)
+    cs = np.empty((len(pos), n_rot // 2), dtype=np.float32)
+    sn = np.empty_like(cs)
+    lib().orc_rope_table(int(n_rot), float(base), len(pos), _ptr(pos, C.c_int64), _ptr(cs, C.c_float),
+                         _ptr(sn, C.c_float))
+    return cs, sn
+
+
+def gate(x, g) -> np.ndarray:
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    lib().orc_gate(_ptr(x, C.c_float), _ptr(g, C.c_float), x.size)
+    return x
