@@ -21,6 +21,10 @@ from .kv import (  # noqa: F401
     conv_rollback,
     host_flash_decode,
     load_library,
+    deserialize,
     mtp_rollback,
+    read_state_header,
     rope_table,
+    serialize,
+    state_header,
 )

@@ -455,6 +455,39 @@ int encode_page_tensor_map(CUtensorMap *map, const void *pages, int num_pages, i
 
 }  // namespace gkv
 
+// ------------------------------------------------------------ wire format
+// The pool section of Engine.serialize / deserialize (Engine.swift:1078-1087,
+// :1106-1116): little-endian Int64 framing, layers in ascending order, each
+// `layer, length, count, K[count] fp16, count, V[count] fp16` with K/V the
+// head-major compact [kv_heads, length, head_dim] (PagePool.compact).  And
+// the StateBytes header, "GDNS" + Int64 version 1 (Shared/StateBytes.swift
+// :12-40).
+
+namespace {
+
+void put_i64(uint8_t *&p, int64_t v) {
+    for (int i = 0; i < 8; ++i) p[i] = (uint8_t)((uint64_t)v >> (8 * i));
+    p += 8;
+}
+
+bool get_i64(const uint8_t *base, int64_t size, int64_t &off, int64_t *v) {
+    if (off < 0 || size - off < 8) return false;
+    uint64_t x = 0;
+    for (int i = 0; i < 8; ++i) x |= (uint64_t)base[off + i] << (8 * i);
+    *v = (int64_t)x;
+    off += 8;
+    return true;
+}
+
+int64_t compact_elems(const gkv_pool *pool, int64_t len) {
+    return (int64_t)pool->cfg.kv_heads * len * pool->cfg.head_dim;
+}
+
+constexpr uint8_t kStateMagic[4] = {'G', 'D', 'N', 'S'};
+constexpr int64_t kStateVersion = 1;
+
+}  // namespace
+
 extern "C" {
 
 const char *gkv_last_error(void) { return g_last_error.c_str(); }
@@ -927,6 +960,152 @@ int gkv_device_status(gkv_pool *pool, int32_t *status) {
     GKV_CUDA(cudaDeviceSynchronize(), "synchronize");
     GKV_CUDA(cudaMemcpy(status, pool->d_status, sizeof(int32_t), cudaMemcpyDeviceToHost),
              "status copy");
+    return GKV_OK;
+}
+
+
+int gkv_serialize(int32_t n_layers, gkv_pool *const *pools, const int32_t *layer_ids, const int32_t *seq_ids,
+                  void *buf, int64_t cap, int64_t *size, void *stream) {
+    if (n_layers < 0 || !size || (n_layers > 0 && (!pools || !layer_ids || !seq_ids)))
+        return fail(GKV_ERR_INVALID, "null argument");
+    int64_t total = 8;
+    std::vector<int32_t> order(n_layers);
+    for (int32_t i = 0; i < n_layers; ++i) {
+        if (!pools[i]) return fail(GKV_ERR_INVALID, "null pool %d", i);
+        const Seq *s = pools[i]->seq(seq_ids[i]);
+        if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d in pool %d", seq_ids[i], i);
+        total += 8 * 4 + 4 * compact_elems(pools[i], s->len);  // layer, length, n, n + K, V
+        order[i] = i;
+    }
+    // Engine.serialize walks b.pools.keys.sorted()
+    std::sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return layer_ids[a] < layer_ids[b]; });
+    for (int32_t i = 1; i < n_layers; ++i)
+        if (layer_ids[order[i]] == layer_ids[order[i - 1]])
+            return fail(GKV_ERR_INVALID, "layer id %d given twice", layer_ids[order[i]]);
+    *size = total;
+    if (!buf) return GKV_OK;
+    if (cap < total) return fail(GKV_ERR_CAPACITY, "buffer of %lld bytes < %lld", (long long)cap, (long long)total);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t *p = static_cast<uint8_t *>(buf);
+    put_i64(p, n_layers);
+    for (int32_t oi = 0; oi < n_layers; ++oi) {
+        gkv_pool *pool = pools[order[oi]];
+        const int32_t sid = seq_ids[order[oi]];
+        const int64_t len = pool->seq(sid)->len, n = compact_elems(pool, len);
+        put_i64(p, layer_ids[order[oi]]);
+        put_i64(p, len);
+        uint16_t *dk = nullptr;
+        if (n > 0) {
+            DeviceGuard guard(pool->cfg.device);
+            GKV_CUDA(cudaMalloc(&dk, sizeof(uint16_t) * 2 * n), "serialize scratch");
+            int rc = gkv_compact_seq(pool, sid, dk, dk + n, stream);
+            cudaError_t e = cudaSuccess;
+            if (rc == GKV_OK) {
+                put_i64(p, n);
+                e = cudaMemcpyAsync(p, dk, sizeof(uint16_t) * n, cudaMemcpyDeviceToHost, st);
+                p += 2 * n;
+                put_i64(p, n);
+                if (e == cudaSuccess) e = cudaMemcpyAsync(p, dk + n, sizeof(uint16_t) * n, cudaMemcpyDeviceToHost, st);
+                p += 2 * n;
+                if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            }
+            cudaFree(dk);
+            if (rc) return rc;
+            if (e != cudaSuccess) return cuda_fail(e, "serialize copy");
+        } else {
+            put_i64(p, 0);
+            put_i64(p, 0);
+        }
+    }
+    return GKV_OK;
+}
+
+int gkv_deserialize(int32_t n_layers, gkv_pool *const *pools, const void *buf, int64_t size, int32_t *layer_ids_out,
+                    int32_t *seq_ids_out, int64_t *consumed, void *stream) {
+    if (n_layers < 0 || !buf || size < 0 || (n_layers > 0 && (!pools || !layer_ids_out || !seq_ids_out)))
+        return fail(GKV_ERR_INVALID, "null argument");
+    const uint8_t *b = static_cast<const uint8_t *>(buf);
+    // parse and check everything before any sequence is created
+    struct Sec { int64_t layer, len, n, k_off, v_off; };
+    std::vector<Sec> secs(n_layers);
+    int64_t off = 0, count = 0;
+    if (!get_i64(b, size, off, &count)) return fail(GKV_ERR_INVALID, "truncated: no layer count");
+    if (count != n_layers) return fail(GKV_ERR_INVALID, "%lld layers in the data, %d pools", (long long)count, n_layers);
+    for (int32_t i = 0; i < n_layers; ++i) {
+        if (!pools[i]) return fail(GKV_ERR_INVALID, "null pool %d", i);
+        Sec &s = secs[i];
+        int64_t kn = 0, vn = 0;
+        if (!get_i64(b, size, off, &s.layer) || !get_i64(b, size, off, &s.len) || !get_i64(b, size, off, &kn))
+            return fail(GKV_ERR_INVALID, "truncated section %d", i);
+        if (s.len < 0 || s.layer < INT32_MIN || s.layer > INT32_MAX)
+            return fail(GKV_ERR_INVALID, "section %d: layer %lld length %lld", i, (long long)s.layer, (long long)s.len);
+        s.n = compact_elems(pools[i], s.len);
+        if (kn != s.n) return fail(GKV_ERR_INVALID, "section %d: %lld K values, pool geometry needs %lld", i,
+                                   (long long)kn, (long long)s.n);
+        s.k_off = off;
+        if (size - off < 2 * kn) return fail(GKV_ERR_INVALID, "truncated K of section %d", i);
+        off += 2 * kn;
+        if (!get_i64(b, size, off, &vn) || vn != s.n) return fail(GKV_ERR_INVALID, "section %d: V count", i);
+        s.v_off = off;
+        if (size - off < 2 * vn) return fail(GKV_ERR_INVALID, "truncated V of section %d", i);
+        off += 2 * vn;
+        if (pools[i]->pages_for(s.len) > (int64_t)pools[i]->stack.size())
+            return fail(GKV_ERR_NO_PAGES, "section %d needs %lld pages", i, (long long)pools[i]->pages_for(s.len));
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t made = 0;
+    int rc = GKV_OK;
+    for (; made < n_layers && rc == GKV_OK; ++made) {
+        gkv_pool *pool = pools[made];
+        const Sec &s = secs[made];
+        DeviceGuard guard(pool->cfg.device);
+        uint16_t *dk = nullptr;
+        cudaError_t e = cudaSuccess;
+        if (s.n > 0) {
+            e = cudaMalloc(&dk, sizeof(uint16_t) * 2 * s.n);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(dk, b + s.k_off, sizeof(uint16_t) * s.n, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(dk + s.n, b + s.v_off, sizeof(uint16_t) * s.n, cudaMemcpyHostToDevice, st);
+        }
+        if (e != cudaSuccess) {
+            rc = cuda_fail(e, "deserialize copy");
+        } else {
+            rc = gkv_from_compact(pool, dk, dk + s.n, s.len, &seq_ids_out[made], stream);
+            const cudaError_t e2 = cudaStreamSynchronize(st);
+            if (rc == GKV_OK && e2 != cudaSuccess) rc = cuda_fail(e2, "deserialize synchronize");
+        }
+        if (dk) cudaFree(dk);
+        if (rc != GKV_OK) break;
+        layer_ids_out[made] = (int32_t)s.layer;
+    }
+    if (rc != GKV_OK) {  // a failing call changes nothing: release what was made
+        for (int32_t i = 0; i < made; ++i) gkv_seq_release(pools[i], seq_ids_out[i]);
+        return rc;
+    }
+    if (consumed) *consumed = off;
+    return GKV_OK;
+}
+
+int gkv_state_header(void *buf, int64_t cap, int64_t *size) {
+    if (!size) return fail(GKV_ERR_INVALID, "null size");
+    *size = 12;
+    if (!buf) return GKV_OK;
+    if (cap < 12) return fail(GKV_ERR_CAPACITY, "buffer of %lld bytes < 12", (long long)cap);
+    uint8_t *p = static_cast<uint8_t *>(buf);
+    memcpy(p, kStateMagic, 4);
+    p += 4;
+    put_i64(p, kStateVersion);
+    return GKV_OK;
+}
+
+int gkv_state_read_header(const void *buf, int64_t size, int64_t *offset) {
+    if (!buf || !offset) return fail(GKV_ERR_INVALID, "null argument");
+    const uint8_t *b = static_cast<const uint8_t *>(buf);
+    int64_t off = 4, version = 0;
+    if (size < 12 || memcmp(b, kStateMagic, 4) != 0) return fail(GKV_ERR_INVALID, "not a GDNS state file");
+    get_i64(b, size, off, &version);
+    if (version != kStateVersion) return fail(GKV_ERR_INVALID, "GDNS version %lld", (long long)version);
+    *offset = off;
     return GKV_OK;
 }
 

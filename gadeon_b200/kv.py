@@ -46,7 +46,7 @@ EXPORTED = (
     "gkv_clone_seq", "gkv_compact_seq", "gkv_from_compact", "gkv_export_table",
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
-    "gkv_rope_table",
+    "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
 )
 
 
@@ -106,6 +106,10 @@ def load_library(path: str = LIB_PATH):
         "gkv_mtp_rollback": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
         "gkv_attn_step": (C.c_int, [P, i32, i32p, i32, P, P, P, P, P, f32, P, P, i32, f32, P, P]),
         "gkv_rope_table": (C.c_int, [i32, f32, i32, i64p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
+        "gkv_serialize": (C.c_int, [i32, C.POINTER(P), i32p, i32p, P, i64, i64p, P]),
+        "gkv_deserialize": (C.c_int, [i32, C.POINTER(P), P, i64, i32p, i32p, i64p, P]),
+        "gkv_state_header": (C.c_int, [P, i64, i64p]),
+        "gkv_state_read_header": (C.c_int, [P, i64, i64p]),
         "gkv_conv_rollback": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
@@ -492,3 +496,50 @@ def rope_table(n_rot: int, base: float, positions) -> tuple:
     _check(L.gkv_rope_table(n_rot, float(base), len(pos), _p64(pos),
                             cos.ctypes.data_as(C.POINTER(C.c_float)), sin.ctypes.data_as(C.POINTER(C.c_float))))
     return cos, sin
+
+
+def serialize(pools: Sequence["BlockPool"], layer_ids: Sequence[int], seq_ids: Sequence[int], stream=None) -> bytes:
+    """``gkv_serialize``: Engine.serialize's pool section for sequence
+    seq_ids[i] of pools[i] under layer id layer_ids[i] (layers ascending)."""
+    L = load_library()
+    n = len(pools)
+    hs = (C.c_void_p * n)(*[p._h.value for p in pools])
+    lids, sids = _i32(layer_ids), _i32(seq_ids)
+    size = C.c_int64()
+    _check(L.gkv_serialize(n, hs, _p32(lids), _p32(sids), None, 0, C.byref(size), _stream_ptr(stream)))
+    buf = (C.c_uint8 * size.value)()
+    _check(L.gkv_serialize(n, hs, _p32(lids), _p32(sids), buf, size.value, C.byref(size), _stream_ptr(stream)))
+    return bytes(buf)
+
+
+def deserialize(pools: Sequence["BlockPool"], data: bytes, stream=None):
+    """``gkv_deserialize``: rebuild each layer's sequence; returns
+    (layer_ids, seq_ids, bytes consumed)."""
+    L = load_library()
+    n = len(pools)
+    hs = (C.c_void_p * n)(*[p._h.value for p in pools])
+    lids = np.zeros(n, dtype=np.int32)
+    sids = np.zeros(n, dtype=np.int32)
+    used = C.c_int64()
+    raw = (C.c_uint8 * len(data)).from_buffer_copy(data) if data else (C.c_uint8 * 1)()
+    _check(L.gkv_deserialize(n, hs, raw, len(data), _p32(lids), _p32(sids), C.byref(used), _stream_ptr(stream)))
+    return lids.tolist(), sids.tolist(), used.value
+
+
+def state_header() -> bytes:
+    """``gkv_state_header``: the StateBytes "GDNS" v1 header (12 bytes)."""
+    L = load_library()
+    size = C.c_int64()
+    buf = (C.c_uint8 * 12)()
+    _check(L.gkv_state_header(buf, 12, C.byref(size)))
+    return bytes(buf[: size.value])
+
+
+def read_state_header(data: bytes) -> Optional[int]:
+    """``gkv_state_read_header``: payload offset when data starts with the
+    GDNS v1 header, else None."""
+    L = load_library()
+    off = C.c_int64()
+    raw = (C.c_uint8 * max(1, len(data))).from_buffer_copy(data.ljust(1, b"\0"))
+    rc = L.gkv_state_read_header(raw, len(data), C.byref(off))
+    return off.value if rc == GKV_OK else None

@@ -170,6 +170,34 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V,
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V,
                      int64_t length, int32_t *seq_id, void *stream);
 
+/* The pool section of Engine.serialize (Engine.swift:1078-1087): into the
+ * HOST buffer buf, little-endian Int64 framing --
+ *   count, then per layer in ascending layer id:
+ *   layer, length, n, K[n] fp16, n, V[n] fp16   (n = kv_heads*length*head_dim,
+ *   K/V head-major as PagePool.compact)
+ * -- for sequence seq_ids[i] of pools[i] under layer id layer_ids[i].
+ * buf == NULL: only *size is set (the bytes needed).  Synchronizes stream. */
+int gkv_serialize(int32_t n_layers, gkv_pool *const *pools,
+                  const int32_t *layer_ids, const int32_t *seq_ids, void *buf,
+                  int64_t cap, int64_t *size, void *stream);
+
+/* Engine.deserialize's pool half (Engine.swift:1106-1116): reads that
+ * section from the HOST buffer into pools[i] (given in the data's layer
+ * order) through gkv_from_compact; returns the new sequence ids, the layer
+ * ids read and the bytes consumed.  The whole section is checked against
+ * the pools' geometry before any sequence is made; a failing call changes
+ * nothing.  Synchronizes stream. */
+int gkv_deserialize(int32_t n_layers, gkv_pool *const *pools, const void *buf,
+                    int64_t size, int32_t *layer_ids_out,
+                    int32_t *seq_ids_out, int64_t *consumed, void *stream);
+
+/* StateBytes header (Shared/StateBytes.swift:12-40): "GDNS" then Int64
+ * version 1, 12 bytes.  gkv_state_header writes it (buf == NULL: *size
+ * only); gkv_state_read_header accepts it and sets *offset to the payload,
+ * else returns GKV_ERR_INVALID.  Host only. */
+int gkv_state_header(void *buf, int64_t cap, int64_t *size);
+int gkv_state_read_header(const void *buf, int64_t size, int64_t *offset);
+
 /* ---- the GDN state rollback that runs beside gkv_truncate in an MTP cycle
  * (Engine.rollbackGDN, LLM/src/CoreML/Engine.swift:2678-2716) ---- */
 
