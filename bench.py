@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import argparse
 import csv
+import dataclasses
 import datetime
 import io
 import json
@@ -67,10 +68,11 @@ def parse_args():
     ap.add_argument("--producer", action="store_true",
                     help="config 2 through gkv_attn_step: raw fp32 q|gate, k, v projections, RMSNorm + RoPE "
                          "+ output gate fused into the decode step (Qwen3.5 attention layer)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6],
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6, 7],
                     help="BASELINE config: 2 decode (default, the headline), 3 MTP verify+rollback, "
                          "4 prefill chunk, 5 long-context sharded decode; 6 = the GDN state rollback "
-                         "that runs beside config 3's truncate")
+                         "that runs beside config 3's truncate; 7 = a whole MTP cycle (drafts on the drafter "
+                         "pool, verify, truncate, GDN rollback, drafter rewind)")
     return ap.parse_args()
 
 
@@ -825,6 +827,107 @@ def run_config6(args, rank, world, local):
         "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * 2, "clocks": clk}), flush=True)
 
 
+def run_config7(args, rank, world, local):
+    """A whole MTP speculative cycle's cache work (Engine.decodeSpecStep,
+    LLM/src/CoreML/Engine.swift:2742-2812) on config 3's geometry: 128
+    sequences (per GPU) at context 8192, nH=16, KVH=4, dh=256, P=16; one
+    full-attention layer, its 3 GDN layers, and the MTP drafter's own pool
+    (same geometry, the committed history).  Per cycle: 3 draft steps on the
+    drafter pool (append 1 + decode, each depending on the last), the verify
+    of 4 rows on the main pool (append + causal attend), accepted length
+    m ~ U{1..4} (seeded), main truncate to p0 + m, GDN state + conv-tail
+    rollback, drafter rewind to its base + m rows re-appended."""
+    import torch
+    import torch.distributed as dist
+    import gadeon_b200 as gk
+    from gadeon_b200.workload import GDN, rollback_bytes
+    cfg, g = CONFIGS[3], GDN
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    S = args.seqs or cfg.seqs
+    KVH, dh, G, nH, nq = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads, cfg.n_q
+    n_draft = nq - 1
+    cfg1 = dataclasses.replace(cfg, n_q=1)  # a drafter step: one query row per sequence
+    W, K = max(args.warmup, 3), min(max(args.steps, 20), 200)
+    ctx = contexts(3, args.seed + 1000 * rank, S)
+    growth = (W + K) * (nq + n_draft) + 8
+    (main,), (mids,), gen = make_pools(torch, cfg, ctx, 1, rank, args.seed, growth, local)
+    (drafter,), (dids,), _ = make_pools(torch, cfg, ctx, 1, rank, args.seed + 1, growth, local)
+    q1 = torch.randn((S, 1, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    k1 = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    q4 = torch.randn((S, nq, nH, dh), generator=gen, device=dev, dtype=torch.float16)
+    k4 = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
+    out1 = torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev)
+    out4 = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
+    n_items = S * g.layers
+    H, D, Cw = g.value_heads, g.head_dim, nq
+    s0 = torch.randn((n_items, H, D, D), generator=gen, device=dev) * 0.1
+    s_out = torch.empty_like(s0)
+    gk_ = torch.randn((n_items, H, Cw, D), generator=gen, device=dev) / math.sqrt(D)
+    gd = torch.randn((n_items, H, Cw, D), generator=gen, device=dev) * 0.5
+    gc = torch.cumsum(-torch.rand((n_items, H, Cw), generator=gen, device=dev) * 0.7, dim=-1)
+    proj = torch.randn((n_items, Cw, g.conv_dim), generator=gen, device=dev)
+    pre = torch.randn((n_items, g.conv_dim, g.taps), generator=gen, device=dev)
+    conv = torch.empty_like(pre)
+    rng = np.random.default_rng(args.seed + 17 * rank)
+    acc = rng.integers(1, nq + 1, size=(W + K, S))  # m = accepted drafts + 1
+    lens = ctx.copy()
+    dlens = ctx.copy()
+    att_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * nq)]
+    att_bytes = []
+
+    def step(i, ti):
+        nonlocal lens, dlens
+        base = dlens.copy()
+        for d in range(n_draft):  # each draft depends on the previous one
+            if ti is not None:
+                att_ev[ti * nq + d][0].record()
+                att_bytes.append(decode_bytes(base + d + 1, cfg1) + append_bytes(S, cfg))
+            drafter.append_attend(dids, 1, G, k1, k1, q1, out=out1)
+            if ti is not None:
+                att_ev[ti * nq + d][1].record()
+        if ti is not None:
+            att_ev[ti * nq + n_draft][0].record()
+            att_bytes.append(decode_bytes(lens + nq, cfg))
+        main.append_attend(mids, nq, G, k4, k4, q4, out=out4)
+        if ti is not None:
+            att_ev[ti * nq + n_draft][1].record()
+        m = acc[i]
+        lens = lens + m
+        main.truncate(mids, lens)
+        mm = np.repeat(m, g.layers).astype(np.int32)
+        gk.mtp_rollback(mm, s0, gd, gk_, gc, out=s_out)
+        gk.conv_rollback(mm, proj, pre, out=conv)
+        drafter.rewind_append(dids, base, m, k4[: int(m.sum())], k4[: int(m.sum())])
+        dlens = base + m
+
+    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    att_ms = sum(a.elapsed_time(b) for a, b in att_ev)
+    committed = float(acc[W:].sum())
+    hbm, kind = peaks()
+    achieved = max_over_ranks(torch, dist, world, local, sum(att_bytes) / (att_ms * 1e-3) / 1e9)
+    for p_ in (main, drafter):
+        assert p_.device_status() == 0
+    if rank != 0:
+        return
+    rb = statistics.mean(sum(rollback_bytes(np.repeat(acc[W + i], g.layers), g)) for i in range(K))
+    cycle_bytes = sum(att_bytes) / K + append_bytes(S * nq, cfg) + append_bytes(int(acc[W:].sum() / K), cfg) + rb
+    print(json.dumps({
+        "metric": "MTP cycle: committed tokens/s (drafts + verify + rollback + drafter rewind, config 3 geometry)",
+        "value": committed * world / (K * ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 accumulate, fp16 K/V/Q storage, f32 GDN state", "data": "synthetic (seeded)",
+        "config": {"workload": f"config7: {S} seqs/GPU at ctx 8192, 1 attention layer + its drafter pool + "
+                               f"{g.layers} GDN layers; {n_draft} drafts, verify {nq} rows, m ~ U{{1..{nq}}}",
+                   "mean_committed_per_seq_cycle": committed / (K * S), "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None,
+                     "kernel": "attend_kernel<256,TMA> (3 drafter decodes + 1 verify per cycle, fused appends)",
+                     "bytes_per_cycle": sum(att_bytes) / K, "attend_ms_per_cycle": att_ms / K},
+        "cycle_gbs": cycle_bytes / (ms * 1e-3) / 1e9,
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 2 + 2 + 1), "clocks": clk}), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -844,7 +947,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6}[args.config]
+        runner = {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6,
+                  7: run_config7}[args.config]
         if args.config == 2 and args.producer:
             runner = run_config2_producer
         runner(args, rank, world, local)

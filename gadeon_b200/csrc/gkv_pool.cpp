@@ -826,6 +826,66 @@ int gkv_truncate(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const i
     return GKV_OK;
 }
 
+int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int64_t *base_len,
+                      const int32_t *n_new, const void *k, const void *v, void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    int rc = check_batch(pool, n_seqs, seq_ids);
+    if (rc) return rc;
+    if (n_seqs > 0 && (!base_len || !n_new)) return fail(GKV_ERR_INVALID, "null base_len/n_new");
+    int64_t rows = 0;
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        const Seq &s = *pool->seq(seq_ids[i]);
+        if (base_len[i] < 0 || base_len[i] > s.len)
+            return fail(GKV_ERR_BAD_SEQ, "rewind sequence %d to %lld (length %lld)", seq_ids[i],
+                        (long long)base_len[i], (long long)s.len);
+        if (n_new[i] < 0) return fail(GKV_ERR_INVALID, "n_new[%d] = %d", i, n_new[i]);
+        rows += n_new[i];
+    }
+    if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
+    if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
+    DeviceGuard guard(pool->cfg.device);
+    // truncate (PagePool.truncate: pages pushed last-first), keeping an undo
+    // log so that an append refused for lack of pages leaves no trace
+    struct Undo {
+        int32_t seq;
+        int64_t len;
+        std::vector<int32_t> pages;  // removed, in removal order
+        std::vector<char> freed;     // pushed onto the free list
+    };
+    std::vector<Undo> undo(n_seqs);
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        Seq &s = *pool->seq(seq_ids[i]);
+        undo[i].seq = seq_ids[i];
+        undo[i].len = s.len;
+        s.len = base_len[i];
+        const int64_t need = pool->pages_for(s.len);
+        while ((int64_t)s.pages.size() > need) {
+            const int32_t pid = s.pages.back();
+            s.pages.pop_back();
+            undo[i].pages.push_back(pid);
+            undo[i].freed.push_back(pool->ref[pid] == 1);
+            pool->unref(pid);
+        }
+    }
+    std::vector<gkv::AppendEntry> entries;
+    std::vector<gkv::TouchedPage> pages;
+    rc = plan_append(pool, n_seqs, seq_ids, n_new, entries, pages);
+    if (rc) {
+        for (int32_t i = n_seqs - 1; i >= 0; --i) {
+            Seq &s = *pool->seq(undo[i].seq);
+            for (size_t j = undo[i].pages.size(); j-- > 0;) {
+                const int32_t pid = undo[i].pages[j];
+                if (undo[i].freed[j]) pool->stack.pop_back();  // the push of this page, undone
+                pool->ref[pid]++;
+                s.pages.push_back(pid);
+            }
+            s.len = undo[i].len;
+        }
+        return rc;
+    }
+    return enqueue_append(pool, entries, pages, k, v, 0, static_cast<cudaStream_t>(stream));
+}
+
 int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream) {
     if (!pool || !dst) return fail(GKV_ERR_INVALID, "null argument");
     if (!pool->seq(src)) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", src);

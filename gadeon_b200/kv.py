@@ -47,6 +47,7 @@ EXPORTED = (
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
+    "gkv_rewind_append",
 )
 
 
@@ -93,6 +94,7 @@ def load_library(path: str = LIB_PATH):
         "gkv_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, P]),
         "gkv_append_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, P]),
         "gkv_truncate": (C.c_int, [P, i32, i32p, i64p]),
+        "gkv_rewind_append": (C.c_int, [P, i32, i32p, i64p, i32p, P, P, P]),
         "gkv_clone_seq": (C.c_int, [P, i32, i32p, P]),
         "gkv_compact_seq": (C.c_int, [P, i32, P, P, P]),
         "gkv_from_compact": (C.c_int, [P, P, P, i64, i32p, P]),
@@ -314,6 +316,17 @@ class BlockPool:
     def truncate(self, seq_ids: Sequence[int], new_len: Sequence[int]):
         ids, nl = _i32(seq_ids), _i64(new_len)
         _check(_lib.gkv_truncate(self._h, len(ids), _p32(ids), _p64(nl)))
+
+    def rewind_append(self, seq_ids: Sequence[int], base_len: Sequence[int], n_new: Sequence[int], k, v,
+                      stream=None):
+        """Truncate each sequence to base_len[i], then append n_new[i] rows
+        (the drafter pool's per-cycle maintenance) in one call."""
+        ids, bl, nn = _i32(seq_ids), _i64(base_len), _i32(n_new)
+        rows = int(nn.sum()) if len(nn) else 0
+        for name, t in (("k", k), ("v", v)):
+            _check_shape(name, t, (rows, self.kv_heads, self.head_dim), _F16)
+        _check(_lib.gkv_rewind_append(self._h, len(ids), _p32(ids), _p64(bl), _p32(nn), _dev_ptr(k), _dev_ptr(v),
+                                      _stream_ptr(stream)))
 
     def clone(self, seq: int, stream=None) -> int:
         out = C.c_int32()

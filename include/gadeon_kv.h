@@ -155,6 +155,17 @@ int gkv_rope_table(int32_t n_rot, float base, int32_t n,
 int gkv_truncate(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                  const int64_t *new_len);
 
+/* The drafter-pool maintenance of an MTP cycle (Engine.decodeSpecStep,
+ * LLM/src/CoreML/Engine.swift:2788-2797: mtpPool.truncate(to: mtpBase),
+ * then the m committed positions re-appended) in one call: sequence i is
+ * truncated to base_len[i] and then n_new[i] rows of k / v (layout of
+ * gkv_append) are appended.  Page-for-page the same as gkv_truncate
+ * followed by gkv_append; if the append cannot be placed the truncate is
+ * undone too. */
+int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                      const int64_t *base_len, const int32_t *n_new,
+                      const void *k, const void *v, void *stream);
+
 /* PagePool.clone() (PagedAttention.swift:199-210; MetalKVPool.snapshot,
  * MetalKVPool.swift:102-109): a new sequence sharing every page of `src`,
  * with a private copy of a partially filled tail page. */
