@@ -135,7 +135,7 @@ struct Cfg {
     static constexpr int OFF_P = OFF_Q + kRows * DH * 2;
     static constexpr int OFF_RED = OFF_P + kRows * TKP * 2;
     static constexpr int OFF_BAR = OFF_RED + 2 * kConsumerWarps * kRows * 4;
-    static constexpr int OFF_FLAG = OFF_BAR + 2 * NSTAGE * 8;
+    static constexpr int OFF_FLAG = OFF_BAR + (2 * NSTAGE + 1) * 8;  // full, empty, rows_done
     static constexpr int SMEM = OFF_FLAG + 16;
     static constexpr int SMEM_ALLOC = SMEM + 1024;
     static_assert(TILE_BYTES % 1024 == 0, "tiles keep 1024-byte alignment");
@@ -272,7 +272,7 @@ __device__ __forceinline__ int cta_of_unit(int64_t u, int64_t units, int64_t cta
 template <int DH, bool TMA, bool FUSED, bool PROD>
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ AttendParams p, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmv) {
+                  const __grid_constant__ CUtensorMap tmv, const __grid_constant__ InlineDesc d) {
     using C = Cfg<DH>;
     constexpr int TK = C::TK, NSTAGE = C::NSTAGE;
     extern __shared__ uint8_t smem_raw[];
@@ -280,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
     uint64_t *empty = full + NSTAGE;
+    uint64_t *rows_done = empty + NSTAGE;  // fused append rows stored (consumers -> producer)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_FLAG);
     volatile int *merge_flag = abort_flag + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -288,89 +289,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int u_begin = (int)(U * blockIdx.x / NC);
     const int u_end = (int)(U * (blockIdx.x + 1) / NC);
 
+    // The next launch in the stream may place its CTAs on SMs this grid
+    // leaves; it waits for this grid's memory before touching any of it.
+    grid_dep_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(rows_done, kConsumerWarps * 32);
         *abort_flag = 0;
         *merge_flag = 0;
         fence_mbar_init();
     }
-    // Stage buffers start zeroed so a tile slot that is never loaded holds
-    // finite values.
-    for (int i = threadIdx.x; i < NSTAGE * 2 * C::TILE_BYTES / 16; i += kThreads)
-        reinterpret_cast<uint4 *>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
-    fence_proxy_async();
     __syncthreads();
+    // From here on the kernel reads and writes memory that earlier work in
+    // the stream produced (descriptor, block table, pages, q, scratch).
+    grid_dep_wait();
     if (u_begin >= u_end) return;
+    // Stage buffers are not cleared: a key row the producer did not load
+    // (past the sequence end) is masked to -inf in S, and its V row is
+    // zeroed before P.V, so stale or uninitialised shared memory never
+    // reaches the output.
 
+    const AttendEntry *entries = p.entries ? p.entries : d.entries;
+    const FusedTail *tails = p.tails ? p.tails : d.tails;
     const int lP = __ffs(p.P) - 1;
     const int lbh = TMA ? min(lP, __ffs(TK) - 1) : (__ffs(TK) - 1);  // log2 rows per tile group
     const int KVH = p.kvh;
-    UnitWalker w{p.entries, p.n_seqs, KVH, 0, 0, 0, {}};
+    UnitWalker w{entries, p.n_seqs, KVH, 0, 0, 0, {}};
     w.seek(u_begin, p.n_seqs);
-
-    if constexpr (FUSED) {
-        // Fused decode append, before any TMA is in flight: for every item
-        // whose last key tile (it holds the new row, position len-1) this CTA
-        // owns, write that kv head's row -- and zero the rest of its slab when
-        // the page is fresh (PagePool.zeroPage) -- then fence the stores
-        // against the TMA reads that follow.
-        UnitWalker a = w;
-        int u = u_begin, n_own = 0;
-        while (u < u_end) {
-            const int item_last = a.e.unit_base + a.kvh * a.e.ntiles + a.e.ntiles - 1;
-            if (item_last < u_end) {
-                const FusedTail ft = p.tails[a.b];
-                const int slot = (a.e.len - 1) & (p.P - 1);
-                const int64_t slab = ((int64_t)ft.pid * KVH + a.kvh) * p.P * DH;
-                uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
-                uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
-                const int rows = ft.fresh ? p.P : 1;
-                if constexpr (PROD) {
-                    // every other row of a fresh page is zeroed by all
-                    // threads; one warp builds the new K/V row from the raw
-                    // projections (items round-robin over the warps)
-                    if (ft.fresh)
-                        for (int i = threadIdx.x; i < rows * C::CH; i += kThreads)
-                            if (i / C::CH != slot) {
-                                kd[i] = make_uint4(0u, 0u, 0u, 0u);
-                                vd[i] = make_uint4(0u, 0u, 0u, 0u);
-                            }
-                    if (warp == n_own % (kThreads / 32)) {
-                        const int64_t row = (int64_t)a.b * KVH + a.kvh;
-                        const int64_t tok = (int64_t)a.b * p.n_q + p.n_q - 1;  // the new row's token
-                        const int hr = p.prod.n_rot >> 1;
-                        float kv[DH / 32];
-                        produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps,
-                                        p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr, p.prod.n_rot, lane,
-                                        kv);
-                        store_row_f16<DH>(p.k_pool_w + slab + (int64_t)slot * DH, lane, kv);
-                        copy_row_f16<DH>(p.v_pool_w + slab + (int64_t)slot * DH, p.prod.v_raw + row * DH, lane);
-                    }
-                    ++n_own;
-                } else {
-                    const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
-                    const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
-                    for (int i = threadIdx.x; i < rows * C::CH; i += kThreads) {
-                        const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
-                        const bool mine = row == slot;
-                        kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
-                        vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
-                    }
-                }
-                if (ft.fresh && a.kvh == 0 && threadIdx.x == 0)
-                    p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx] = ft.pid;
-            }
-            // next item
-            u = item_last + 1;
-            a.j = a.e.ntiles - 1;
-            a.next();
-        }
-        fence_proxy_async_global();
-        __syncthreads();
-    }
 
     if (warp == kConsumerWarps) {
         // ================================================= producer warp
@@ -391,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool fuse_here = FUSED && w.j == w.e.ntiles - 1;
                 FusedTail ft{};
                 if constexpr (FUSED) {
-                    if (fuse_here) ft = p.tails[w.b];
+                    if (fuse_here) ft = tails[w.b];
                 }
                 int row0 = 0;
                 if (lane < ngroups) {  // table read before the wait hides its latency
@@ -406,6 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     row0 = (pid * KVH + w.kvh) * p.P + (tg & (p.P - 1));
                 }
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) break;
+                // the consumers store this CTA's new rows (and zero fresh
+                // pages) while the ring fills; only the tile holding a new
+                // row waits for those stores
+                if (fuse_here && !mbar_wait(rows_done, 0, abort_flag, p.status)) break;
                 if (lane == 0)
                     mbar_expect_tx(&full[stage], (uint32_t)(ngroups << lbh) * DH * 2 * 2);
                 __syncwarp();
@@ -466,6 +418,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Causal limits of this thread's two fragment rows: key t is visible to
     // row r iff t <= len - n_q + r / G (padding rows use the last real row).
     const int rq0 = min(lr, R - 1) / G, rq1 = min(lr + 8, R - 1) / G;
+
+    if constexpr (FUSED) {
+        // Fused decode append, while the producer's first loads are in
+        // flight: for every item whose last key tile (it holds the new row,
+        // position len-1) this CTA owns, write that kv head's row -- and zero
+        // the rest of its slab when the page is fresh (PagePool.zeroPage) --
+        // then fence the stores against the TMA read of that tile.
+        UnitWalker a = w;
+        int u = u_begin, n_own = 0;
+        while (u < u_end) {
+            const int item_last = a.e.unit_base + a.kvh * a.e.ntiles + a.e.ntiles - 1;
+            if (item_last < u_end) {
+                const FusedTail ft = tails[a.b];
+                const int slot = (a.e.len - 1) & (p.P - 1);
+                const int64_t slab = ((int64_t)ft.pid * KVH + a.kvh) * p.P * DH;
+                uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
+                uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
+                const int rows = ft.fresh ? p.P : 1;
+                if constexpr (PROD) {
+                    // every other row of a fresh page is zeroed by all
+                    // threads; one warp builds the new K/V row from the raw
+                    // projections (items round-robin over the warps)
+                    if (ft.fresh)
+                        for (int i = tid; i < rows * C::CH; i += 128)
+                            if (i / C::CH != slot) {
+                                kd[i] = make_uint4(0u, 0u, 0u, 0u);
+                                vd[i] = make_uint4(0u, 0u, 0u, 0u);
+                            }
+                    if (warp == n_own % kConsumerWarps) {
+                        const int64_t row = (int64_t)a.b * KVH + a.kvh;
+                        const int64_t tok = (int64_t)a.b * p.n_q + p.n_q - 1;  // the new row's token
+                        const int hr = p.prod.n_rot >> 1;
+                        float kv[DH / 32];
+                        produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps,
+                                        p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr, p.prod.n_rot, lane,
+                                        kv);
+                        store_row_f16<DH>(p.k_pool_w + slab + (int64_t)slot * DH, lane, kv);
+                        copy_row_f16<DH>(p.v_pool_w + slab + (int64_t)slot * DH, p.prod.v_raw + row * DH, lane);
+                    }
+                    ++n_own;
+                } else {
+                    const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                    const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
+                    for (int i = tid; i < rows * C::CH; i += 128) {
+                        const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
+                        const bool mine = row == slot;
+                        kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
+                        vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+                if (ft.fresh && a.kvh == 0 && tid == 0)
+                    p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx] = ft.pid;
+            }
+            // next item
+            u = item_last + 1;
+            a.j = a.e.ntiles - 1;
+            a.next();
+        }
+        fence_proxy_async_global();
+        mbar_arrive(rows_done);
+    }
 
     for (int u = u_begin; u < u_end; ++u) {
         const int b = w.b, kvh = w.kvh, j = w.j, len = w.e.len;
@@ -719,6 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
+                    if (lr + half * 8 >= R) continue;  // padding rows are never merged
                     float *dst = part + 32 + (int64_t)(lr + half * 8) * DH;
 #pragma unroll
                     for (int n = 0; n < C::NT_PV; ++n)
@@ -770,9 +784,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int DH, bool TMA, bool FUSED = false, bool PROD = false>
 cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
-                            int grid, cudaStream_t s) {
+                            int grid, cudaStream_t s, const InlineDesc *desc) {
     auto kern = attend_kernel<DH, TMA, FUSED, PROD>;
     static bool configured[64] = {};
+    static const InlineDesc empty_desc{};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
@@ -781,8 +796,20 @@ cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const 
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    kern<<<grid, kThreads, Cfg<DH>::SMEM_ALLOC, s>>>(p, *tk, *tv);
-    return cudaGetLastError();
+    // Programmatic stream serialization: the launch may begin while the
+    // previous kernel of the stream drains; the kernel's grid_dep_wait()
+    // precedes every access to memory that kernel could have written.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg<DH>::SMEM_ALLOC;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p, *tk, *tv, desc ? *desc : empty_desc);
 }
 
 }  // namespace
@@ -821,10 +848,10 @@ int attend_grid(int dh, int P, int units, int sm_count) {
 // cp.async loader (P < 8, append done beforehand).
 template <int DH>
 cudaError_t launch_attend_prod(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int grid,
-                               cudaStream_t s) {
-    if (p.P < 8) return launch_attend_t<DH, false, false, true>(p, tk, tv, grid, s);
-    return p.tails ? launch_attend_t<DH, true, true, true>(p, tk, tv, grid, s)
-                   : launch_attend_t<DH, true, false, true>(p, tk, tv, grid, s);
+                               cudaStream_t s, const InlineDesc *d) {
+    if (p.P < 8) return launch_attend_t<DH, false, false, true>(p, tk, tv, grid, s, d);
+    return p.fused ? launch_attend_t<DH, true, true, true>(p, tk, tv, grid, s, d)
+                   : launch_attend_t<DH, true, false, true>(p, tk, tv, grid, s, d);
 }
 
 // grid: n_seqs * KVH rows, 4 warps per block, one warp per row.
@@ -858,24 +885,24 @@ cudaError_t launch_produce_kv(const ProduceParams &p, int dh, cudaStream_t s) {
 }
 
 cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
-                          int dh, int grid, cudaStream_t s) {
+                          int dh, int grid, cudaStream_t s, const InlineDesc *d) {
     const bool tma = p.P >= 8;
     if (p.prod.q_gate) {
-        if (dh == 128) return launch_attend_prod<128>(p, tk, tv, grid, s);
-        if (dh == 256) return launch_attend_prod<256>(p, tk, tv, grid, s);
+        if (dh == 128) return launch_attend_prod<128>(p, tk, tv, grid, s, d);
+        if (dh == 256) return launch_attend_prod<256>(p, tk, tv, grid, s, d);
         return cudaErrorInvalidValue;
     }
     switch (dh) {
-        case 64: return tma ? launch_attend_t<64, true>(p, tk, tv, grid, s)
-                            : launch_attend_t<64, false>(p, tk, tv, grid, s);
-        case 128: return tma ? (p.tails ? launch_attend_t<128, true, true>(p, tk, tv, grid, s)
-                                        : launch_attend_t<128, true>(p, tk, tv, grid, s))
-                             : launch_attend_t<128, false>(p, tk, tv, grid, s);
-        case 256: return tma ? (p.tails ? launch_attend_t<256, true, true>(p, tk, tv, grid, s)
-                                        : launch_attend_t<256, true>(p, tk, tv, grid, s))
-                             : launch_attend_t<256, false>(p, tk, tv, grid, s);
-        case 512: return tma ? launch_attend_t<512, true>(p, tk, tv, grid, s)
-                             : launch_attend_t<512, false>(p, tk, tv, grid, s);
+        case 64: return tma ? launch_attend_t<64, true>(p, tk, tv, grid, s, d)
+                            : launch_attend_t<64, false>(p, tk, tv, grid, s, d);
+        case 128: return tma ? (p.fused ? launch_attend_t<128, true, true>(p, tk, tv, grid, s, d)
+                                        : launch_attend_t<128, true>(p, tk, tv, grid, s, d))
+                             : launch_attend_t<128, false>(p, tk, tv, grid, s, d);
+        case 256: return tma ? (p.fused ? launch_attend_t<256, true, true>(p, tk, tv, grid, s, d)
+                                        : launch_attend_t<256, true>(p, tk, tv, grid, s, d))
+                             : launch_attend_t<256, false>(p, tk, tv, grid, s, d);
+        case 512: return tma ? launch_attend_t<512, true>(p, tk, tv, grid, s, d)
+                             : launch_attend_t<512, false>(p, tk, tv, grid, s, d);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -82,13 +82,24 @@ struct ProducerArgs {
     float eps;
 };
 
+// The descriptor of a call with at most kInlineSeqs sequences travels in the
+// attend kernel's parameter block instead of a device buffer: no upload sits
+// between two launches, so a launch follows the previous kernel directly and
+// its start-up overlaps that kernel's tail (programmatic dependent launch).
+constexpr int kInlineSeqs = 128;
+struct InlineDesc {
+    AttendEntry entries[kInlineSeqs];
+    FusedTail tails[kInlineSeqs];
+};
+
 struct AttendParams {
-    const AttendEntry *entries;
+    const AttendEntry *entries;  // null: InlineDesc::entries
     int32_t n_seqs;
     int32_t total_units;
-    // fused decode append (null when the rows were appended beforehand):
-    // k_new/v_new [n_seqs, KVH, dh] fp16, written into the pool before the
-    // last key tile of each (sequence, kv head) is loaded
+    // fused decode append (fused = 1): k_new/v_new [n_seqs, KVH, dh] fp16,
+    // written into the pool before the last key tile of each (sequence, kv
+    // head) is loaded; tails (null: InlineDesc::tails) say where
+    int32_t fused;
     const FusedTail *tails;
     const uint16_t *k_new, *v_new;
     uint16_t *k_pool_w, *v_pool_w;
@@ -121,9 +132,10 @@ cudaError_t launch_append(const AppendParams &p, cudaStream_t s);
 int attend_grid(int dh, int P, int units, int sm_count);
 // Floats of partial-result scratch per slot.
 __host__ __device__ inline int64_t attend_partial_floats(int dh) { return 32 + 16 * (int64_t)dh; }
+// desc: the inline descriptor when p.entries is null (else may be null).
 cudaError_t launch_attend(const AttendParams &p, const CUtensorMap *tmap_k,
                           const CUtensorMap *tmap_v, int dh, int grid,
-                          cudaStream_t s);
+                          cudaStream_t s, const InlineDesc *desc = nullptr);
 // Key tile length used by the attend kernel for head_dim dh.
 int attend_tile_keys(int dh);
 // True when the attend kernel can run the producer fusion for head_dim dh.

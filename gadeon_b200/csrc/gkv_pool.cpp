@@ -332,12 +332,26 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
                    const void *v_new = nullptr, const gkv::ProducerArgs *prod = nullptr) {
     if (n == 0) return GKV_OK;
     const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
-    cudaError_t err;
-    const size_t ebytes = ((size_t)n * sizeof(gkv::AttendEntry) + 255) & ~size_t(255);
-    const size_t bytes = tails ? ebytes + (size_t)n * sizeof(gkv::FusedTail) : (size_t)n * sizeof(gkv::AttendEntry);
-    const int slot = pool->staging.acquire(bytes, &err);
-    if (slot < 0) return cuda_fail(err, "descriptor staging");
-    auto *ent = reinterpret_cast<gkv::AttendEntry *>(pool->staging.host(slot));
+    const bool chunk = (int64_t)n_q * group > 16;  // many rows per kv head: tcgen05 chunk kernel
+    // Up to kInlineSeqs sequences: the descriptor rides in the kernel's
+    // parameter block (no upload between launches).
+    const bool inl = !chunk && n <= gkv::kInlineSeqs;
+    gkv::InlineDesc desc;
+    int slot = -1;
+    size_t ebytes = 0;
+    size_t bytes = 0;
+    gkv::AttendEntry *ent = desc.entries;
+    if (!inl) {
+        cudaError_t err;
+        ebytes = ((size_t)n * sizeof(gkv::AttendEntry) + 255) & ~size_t(255);
+        bytes = tails ? ebytes + (size_t)n * sizeof(gkv::FusedTail) : (size_t)n * sizeof(gkv::AttendEntry);
+        slot = pool->staging.acquire(bytes, &err);
+        if (slot < 0) return cuda_fail(err, "descriptor staging");
+        ent = reinterpret_cast<gkv::AttendEntry *>(pool->staging.host(slot));
+        if (tails) memcpy(pool->staging.host(slot) + ebytes, tails, (size_t)n * sizeof(gkv::FusedTail));
+    } else if (tails) {
+        memcpy(desc.tails, tails, (size_t)n * sizeof(gkv::FusedTail));
+    }
     int64_t units = 0;
     for (int32_t i = 0; i < n; ++i) {
         const Seq &s = *pool->seq(ids[i]);
@@ -345,8 +359,10 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         ent[i] = {ids[i], (int32_t)s.len, (int32_t)units, ntiles};
         units += (int64_t)KVH * ntiles;
     }
-    if ((int64_t)n_q * group > 16) {  // many rows per kv head: tcgen05 chunk kernel
-        GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
+    if (!chunk && units > INT32_MAX) return fail(GKV_ERR_CAPACITY, "too many key tiles in one call");
+    // the pinned slot is complete: the copy reads it when the stream gets there
+    if (!inl) GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
+    if (chunk) {
         gkv::ChunkParams c{};
         c.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
         c.n_seqs = n;
@@ -368,13 +384,13 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
         return GKV_OK;
     }
-    if (units > INT32_MAX) return fail(GKV_ERR_CAPACITY, "too many key tiles in one call");
-    if (tails) memcpy(pool->staging.host(slot) + ebytes, tails, (size_t)n * sizeof(gkv::FusedTail));
-    GKV_CUDA(pool->staging.upload(slot, bytes, st), "descriptor upload");
     gkv::AttendParams p{};
-    p.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
+    if (!inl) {
+        p.entries = reinterpret_cast<const gkv::AttendEntry *>(pool->staging.dev(slot));
+        if (tails) p.tails = reinterpret_cast<const gkv::FusedTail *>(pool->staging.dev(slot) + ebytes);
+    }
     if (tails) {
-        p.tails = reinterpret_cast<const gkv::FusedTail *>(pool->staging.dev(slot) + ebytes);
+        p.fused = 1;
         p.k_new = static_cast<const uint16_t *>(k_new);
         p.v_new = static_cast<const uint16_t *>(v_new);
         p.k_pool_w = pool->d_k;
@@ -400,9 +416,9 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
     p.scale_log2 = scale * 1.4426950408889634f;
     if (prod) p.prod = *prod;
     const int grid = gkv::attend_grid(pool->cfg.head_dim, p.P, (int)units, pool->sm_count);
-    GKV_CUDA(gkv::launch_attend(p, &pool->tmk, &pool->tmv, pool->cfg.head_dim, grid, st),
+    GKV_CUDA(gkv::launch_attend(p, &pool->tmk, &pool->tmv, pool->cfg.head_dim, grid, st, inl ? &desc : nullptr),
              "attend kernel launch");
-    GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
+    if (!inl) GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
     return GKV_OK;
 }
 

@@ -29,6 +29,16 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel in
+// the stream (launched with programmatic stream serialization) start its
+// CTAs once every CTA of this grid has issued it; grid_dep_wait blocks until
+// the preceding kernel has completed and its memory is visible (a no-op for
+// a launch without the attribute).
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
