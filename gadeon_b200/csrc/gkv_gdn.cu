@@ -14,6 +14,7 @@
 // The per-item m travels in the kernel parameters, so a call allocates
 // nothing and needs no upload.
 #include <cuda_runtime.h>
+#include <utility>
 
 #include <cmath>
 #include <cstdarg>
@@ -222,6 +223,10 @@ extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, in
     if ((int64_t)DK * DV > (1LL << 30)) return report_error(GKV_ERR_CAPACITY, "DK*DV=%lld", (long long)DK * DV);
     if (n_items == 0) return GKV_OK;
     if (!m || !s0 || !delta || !k || !gcum || !out) return report_error(GKV_ERR_INVALID, "null pointer");
+    for (const auto &b : {std::make_pair((const void *)s0, "s0"), std::make_pair((const void *)delta, "delta"),
+                          std::make_pair((const void *)k, "k"), std::make_pair((const void *)gcum, "gcum"),
+                          std::make_pair((const void *)out, "out")})
+        if (const int rc = gkv::check_reachable(b.first, -1, false, b.second)) return rc;
     if ((reinterpret_cast<uintptr_t>(s0) | reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(k) |
          reinterpret_cast<uintptr_t>(gcum) | reinterpret_cast<uintptr_t>(out)) & 3)
         return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
@@ -267,6 +272,9 @@ extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv
         return report_error(GKV_ERR_INVALID, "n_items=%d conv_dim=%d taps=%d C=%d", n_items, conv_dim, taps, C);
     if (n_items == 0) return GKV_OK;
     if (!m || !proj || !pre || !out) return report_error(GKV_ERR_INVALID, "null pointer");
+    for (const auto &b : {std::make_pair((const void *)proj, "proj"), std::make_pair((const void *)pre, "pre"),
+                          std::make_pair((const void *)out, "out")})
+        if (const int rc = gkv::check_reachable(b.first, -1, false, b.second)) return rc;
     if ((reinterpret_cast<uintptr_t>(proj) | reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(out)) & 3)
         return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
     for (int32_t i = 0; i < n_items; ++i)

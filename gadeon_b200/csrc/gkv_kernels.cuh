@@ -177,6 +177,11 @@ cudaError_t launch_compact(const CompactParams &p, cudaStream_t s);
 // thread's gkv_last_error() message and return `code`; encode the attend
 // kernel's TMA view of a caller-owned K or V page array.
 int report_error(int code, const char *fmt, ...);
+// GKV_OK when a kernel may read or write ptr from GPU `device` (-1: the
+// current one): device memory of that GPU, managed memory, or -- host_ok --
+// page-locked host memory mapped at the same address.  Pageable host memory
+// would fault the kernel; it is refused with GKV_ERR_INVALID.  Null passes.
+int check_reachable(const void *ptr, int device, bool host_ok, const char *what);
 int encode_page_tensor_map(CUtensorMap *map, const void *pages, int num_pages, int kv_heads,
                            int page_tokens, int head_dim);
 

@@ -99,6 +99,12 @@ extern "C" int gkv_attend_noalloc(const void *k_pages, const void *v_pages, int3
     for (const void *ptr : {k_pages, v_pages, q, static_cast<const void *>(out)})
         if (reinterpret_cast<uintptr_t>(ptr) & 15)
             return report_error(GKV_ERR_INVALID, "k_pages/v_pages/q/out must be 16-byte aligned");
+    {  // every buffer must be device (or managed) memory of the current GPU
+        const void *bufs[5] = {k_pages, v_pages, block_table, q, out};
+        const char *names[5] = {"k_pages", "v_pages", "block_table", "q", "out"};
+        for (int i = 0; i < 5; ++i)
+            if (const int rc = gkv::check_reachable(bufs[i], -1, false, names[i])) return rc;
+    }
 
     // Work descriptor on the host stack: no heap, no device allocation.
     gkv::AttendEntry entries[GKV_NOALLOC_MAX_SEQS];

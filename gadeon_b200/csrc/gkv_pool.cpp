@@ -23,6 +23,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 #include <vector>
 
@@ -222,6 +223,18 @@ int check_batch(const gkv_pool *pool, int32_t n, const int32_t *ids) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Caller buffers a kernel reads or writes with plain loads and stores: device
+// memory of the pool's GPU, managed memory, or page-locked host memory mapped
+// at the same address (zero-copy: the kernel moves those bytes over the host
+// link itself).  Pageable host memory would fault the kernel: refused.
+int check_buffers(const gkv_pool *pool, std::initializer_list<std::pair<const void *, const char *>> bufs) {
+    for (const auto &b : bufs) {
+        const int rc = gkv::check_reachable(b.first, pool->cfg.device, true, b.second);
+        if (rc) return rc;
+    }
+    return GKV_OK;
+}
 
 // Host half of an append/seed: validates, mutates the bookkeeping, and fills
 // the descriptor (entries + touched pages).  Nothing is mutated on failure.
@@ -451,6 +464,40 @@ int report_error(int code, const char *fmt, ...) {
     return code;
 }
 
+int check_reachable(const void *ptr, int device, bool host_ok, const char *what) {
+    if (!ptr) return GKV_OK;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();  // clear the sticky-free error of the query
+        return report_error(GKV_ERR_INVALID, "%s: not an address the CUDA runtime knows", what);
+    }
+    if (device < 0 && cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return report_error(GKV_ERR_CUDA, "%s: no current device", what);
+    }
+    switch (a.type) {
+        case cudaMemoryTypeDevice:
+            if (a.device != device)
+                return report_error(GKV_ERR_INVALID, "%s is memory of GPU %d; the call runs on GPU %d", what,
+                                    a.device, device);
+            return GKV_OK;
+        case cudaMemoryTypeManaged:
+            return GKV_OK;
+        case cudaMemoryTypeHost:
+            if (!host_ok)
+                return report_error(GKV_ERR_INVALID, "%s is host memory; this argument must be device memory",
+                                    what);
+            if (a.devicePointer != ptr)
+                return report_error(GKV_ERR_INVALID,
+                                    "%s: page-locked host memory not mapped at the same address on the GPU", what);
+            return GKV_OK;
+        default:
+            return report_error(GKV_ERR_INVALID,
+                                "%s is pageable host memory: pass device memory%s", what,
+                                host_ok ? " or page-locked host memory (cudaHostAlloc / cudaHostRegister)" : "");
+    }
+}
+
 int encode_page_tensor_map(CUtensorMap *map, const void *pages, int num_pages, int kv_heads,
                            int page_tokens, int head_dim) {
     EncodeTiledFn enc = encode_fn();
@@ -671,6 +718,7 @@ int gkv_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int
     for (int32_t i = 0; i < n_seqs; ++i) rows += std::max(n_new[i], 0);
     if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
     if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
+    if (rows > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}}))) return rc;
     DeviceGuard guard(pool->cfg.device);
     std::vector<gkv::AppendEntry> entries;
     std::vector<gkv::TouchedPage> pages;
@@ -689,6 +737,10 @@ int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64
     if (count < 0 || count > INT32_MAX) return fail(GKV_ERR_INVALID, "count=%lld", (long long)count);
     if (count > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
     if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    if (count > 0) {
+        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
+        if (rc) return rc;
+    }
     DeviceGuard guard(pool->cfg.device);
     const int32_t n = (int32_t)count;
     std::vector<gkv::AppendEntry> entries;
@@ -706,6 +758,7 @@ int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n
     rc = check_attend(pool, n_seqs, seq_ids, n_q, group, q, out);
     if (rc) return rc;
     if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
+    if (n_seqs > 0 && (rc = check_buffers(pool, {{q, "q"}, {out, "out"}}))) return rc;
     DeviceGuard guard(pool->cfg.device);
     return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale,
                           static_cast<cudaStream_t>(stream));
@@ -728,6 +781,7 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
     if (!aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(out))
         return fail(GKV_ERR_INVALID, "k/v/q/out not 16-byte aligned");
     if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
+    if (n_seqs > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}, {q, "q"}, {out, "out"}}))) return rc;
     DeviceGuard guard(pool->cfg.device);
     std::vector<int32_t> n_new(n_seqs, n_q);
     std::vector<gkv::AppendEntry> entries;
@@ -773,6 +827,10 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
         ((reinterpret_cast<uintptr_t>(q_norm) | reinterpret_cast<uintptr_t>(k_norm) |
           reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 3))
         return fail(GKV_ERR_INVALID, "q_gate/k_raw/v_raw/out must be 16-byte aligned, the rest 4-byte");
+    if (n_seqs > 0 && (rc = check_buffers(pool, {{q_gate, "q_gate"}, {k_raw, "k_raw"}, {v_raw, "v_raw"},
+                                                 {q_norm, "q_norm"}, {k_norm, "k_norm"}, {rope_cos, "rope_cos"},
+                                                 {rope_sin, "rope_sin"}, {out, "out"}})))
+        return rc;
     DeviceGuard guard(pool->cfg.device);
     std::vector<int32_t> n_new(n_seqs, 1);
     std::vector<gkv::AppendEntry> entries;
@@ -859,6 +917,7 @@ int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, co
     }
     if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
     if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
+    if (rows > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}}))) return rc;
     DeviceGuard guard(pool->cfg.device);
     // truncate (PagePool.truncate: pages pushed last-first), keeping an undo
     // log so that an append refused for lack of pages leaves no trace
@@ -945,6 +1004,10 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stre
     if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
     if (s->len > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
     if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    if (s->len > 0) {
+        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
+        if (rc) return rc;
+    }
     DeviceGuard guard(pool->cfg.device);
     gkv::CompactParams p{};
     p.table = pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq;
@@ -964,6 +1027,11 @@ int gkv_from_compact(gkv_pool *pool, const void *K, const void *V, int64_t lengt
                      int32_t *seq_id, void *stream) {
     if (!pool || !seq_id) return fail(GKV_ERR_INVALID, "null argument");
     if (length < 0) return fail(GKV_ERR_INVALID, "length=%lld", (long long)length);
+    if (length > 0) {  // before a sequence is made, so a refused buffer leaves nothing behind
+        if (!K || !V) return fail(GKV_ERR_INVALID, "null K/V");
+        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
+        if (rc) return rc;
+    }
     if (pool->pages_for(length) > (int64_t)pool->stack.size())
         return fail(GKV_ERR_NO_PAGES, "fromCompact needs %lld pages",
                     (long long)pool->pages_for(length));

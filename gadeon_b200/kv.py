@@ -144,14 +144,28 @@ def _p64(a: np.ndarray):
 
 
 def _dev_ptr(t) -> Optional[int]:
-    """Device address of a contiguous torch CUDA tensor (or None)."""
+    """Address of a contiguous torch tensor a kernel can reach (or None): a
+    CUDA tensor, or a page-locked CPU tensor (``pin_memory()``), which the
+    kernels read and write in place over the host link.  The library checks
+    each address again and refuses host memory where an argument must be
+    device memory.  A host buffer must stay referenced and unchanged until
+    the stream has finished with it: torch's pinned-memory cache can hand a
+    freed block to the next pin_memory() at once."""
     if t is None:
         return None
-    if not t.is_cuda:
-        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU")
+    if not t.is_cuda and not (t.device.type == "cpu" and t.is_pinned()):
+        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU or in page-locked host memory")
     if not t.is_contiguous():
         raise GkvError(GKV_ERR_INVALID, "tensor must be contiguous")
     return t.data_ptr()
+
+
+def _empty_f32(shape, like):
+    """fp32 output beside `like`: on its GPU, or page-locked host memory."""
+    import torch
+    if like.is_cuda:
+        return torch.empty(shape, dtype=torch.float32, device=like.device)
+    return torch.empty(shape, dtype=torch.float32).pin_memory()
 
 
 def _check_shape(name, t, shape, dtypes):
@@ -257,7 +271,7 @@ class BlockPool:
         qshape = (len(ids), n_q, self.kv_heads * group, self.head_dim)
         _check_shape("q", q, qshape, _F16)
         if out is None:
-            out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+            out = _empty_f32(qshape, q)
         _check_shape("out", out, qshape, ("float32",))
         if scale is None:
             scale = self.head_dim ** -0.5
@@ -275,7 +289,7 @@ class BlockPool:
         for name, t in (("k", k), ("v", v)):
             _check_shape(name, t, (len(ids) * n_q, self.kv_heads, self.head_dim), _F16)
         if out is None:
-            out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+            out = _empty_f32(qshape, q)
         _check_shape("out", out, qshape, ("float32",))
         if scale is None:
             scale = self.head_dim ** -0.5
@@ -303,7 +317,7 @@ class BlockPool:
         _check_shape("rope_cos", rope_cos, (n, half), ("float32",))
         _check_shape("rope_sin", rope_sin, (n, half), ("float32",))
         if out is None:
-            out = torch.empty((n, KVH * group, dh), dtype=torch.float32, device=q_gate.device)
+            out = _empty_f32((n, KVH * group, dh), q_gate)
         _check_shape("out", out, (n, KVH * group, dh), ("float32",))
         if scale is None:
             scale = dh ** -0.5

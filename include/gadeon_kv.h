@@ -17,9 +17,17 @@
  *   - Every call returns a status (GKV_OK == 0); gkv_last_error() gives the
  *     calling thread's message for its last failure.  A failing call leaves
  *     the pool unchanged (validation happens before any mutation).
- *   - K/V/Q and outputs are DEVICE pointers on the pool's GPU; id and length
- *     arrays are HOST pointers.  `stream` is a cudaStream_t (NULL = the
- *     legacy default stream).  Work is enqueued asynchronously.
+ *   - K/V/Q and outputs of the pool calls are device memory of the pool's
+ *     GPU, managed memory, or page-locked host memory mapped at the same
+ *     address (cudaHostAlloc / cudaMallocHost / cudaHostRegister): the
+ *     kernels read and write such host buffers in place over the host link,
+ *     so a caller holding host arrays needs no copies of its own.  Pageable
+ *     host memory cannot be reached by a kernel and is refused with
+ *     GKV_ERR_INVALID before anything is enqueued.  A host buffer must stay
+ *     valid and unchanged until the stream has finished the call.  The GDN
+ *     rollback and gkv_attend_noalloc take device memory only.  Id and
+ *     length arrays are HOST pointers.  `stream` is a cudaStream_t (NULL =
+ *     the legacy default stream).  Work is enqueued asynchronously.
  *   - Host bookkeeping (lengths, block tables, free list) is updated when the
  *     call returns; the device copy of the tables is updated in stream order.
  *   - A pool is not thread-safe: serialise calls on one pool (the reference
