@@ -118,9 +118,13 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kRows = 16;  // query rows per (sequence, kv head) item
 
+// dh 256 runs two CTAs per SM (32-key tiles, Q read from shared memory,
+// <= 204 registers): one consumer warp per SM sub-partition is latency-bound
+// on its MMA / softmax chain, two independent ones keep HBM streaming.
 template <int DH>
 struct Cfg {
-    static constexpr int TK = DH >= 512 ? 32 : 64;        // keys per tile
+    static constexpr int CTAS = DH == 256 ? 2 : 1;         // resident CTAs per SM
+    static constexpr int TK = DH >= 256 ? 32 : 64;        // keys per tile
     static constexpr int NCB = DH / 64;                    // 128-byte column blocks
     static constexpr int CH = DH / 8;                      // 16-byte chunks per row
     static constexpr int TILE_BYTES = TK * DH * 2;         // one K (or V) tile
@@ -129,7 +133,7 @@ struct Cfg {
     static constexpr int NT_QK = KPW / 8;                  // n8 tiles per warp in QK
     static constexpr int DPW = DH / kConsumerWarps;        // head-dim columns per warp in PV
     static constexpr int NT_PV = DPW / 8;
-    static constexpr bool Q_REGS = DH <= 256;              // keep Q fragments in registers
+    static constexpr bool Q_REGS = DH <= 128;              // keep Q fragments in registers
     static constexpr int TKP = TK + 8;                     // padded P row (halves)
     static constexpr int OFF_Q = NSTAGE * 2 * TILE_BYTES;
     static constexpr int OFF_P = OFF_Q + kRows * DH * 2;
@@ -141,6 +145,7 @@ struct Cfg {
     static_assert(TILE_BYTES % 1024 == 0, "tiles keep 1024-byte alignment");
     static_assert(NT_PV % 2 == 0, "P.V loads n8 tiles in pairs");
     static_assert(SMEM_ALLOC <= 227 * 1024, "fits one CTA per SM");
+    static_assert(CTAS * (SMEM_ALLOC + 1024) <= 228 * 1024, "CTAS CTAs fit one SM");
 };
 
 // Byte offset of (key t, 16-byte chunk c16) inside a K or V tile.  The tile
@@ -270,7 +275,7 @@ __device__ __forceinline__ int cta_of_unit(int64_t u, int64_t units, int64_t cta
 }
 
 template <int DH, bool TMA, bool FUSED, bool PROD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
     attend_kernel(const __grid_constant__ AttendParams p, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ InlineDesc d) {
     using C = Cfg<DH>;
@@ -839,9 +844,16 @@ int attend_tile_keys(int dh) {
 }
 
 int attend_grid(int dh, int P, int units, int sm_count) {
-    (void)dh;
     (void)P;
-    return units < sm_count ? units : sm_count;
+    int per_sm = 1;
+    switch (dh) {
+        case 64: per_sm = Cfg<64>::CTAS; break;
+        case 128: per_sm = Cfg<128>::CTAS; break;
+        case 256: per_sm = Cfg<256>::CTAS; break;
+        case 512: per_sm = Cfg<512>::CTAS; break;
+    }
+    const int cap = sm_count * per_sm;
+    return units < cap ? units : cap;
 }
 
 // dh 128 / 256 with the producer fusion: TMA (fused append or not) or the

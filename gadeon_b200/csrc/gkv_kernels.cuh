@@ -128,7 +128,8 @@ struct ProduceParams {
 
 // Host-side launchers (gkv_kernels.cu).
 cudaError_t launch_append(const AppendParams &p, cudaStream_t s);
-// Number of CTAs the attend launch will use for `units` work units.
+// Number of CTAs the attend launch will use for `units` work units (at
+// most sm_count times the CTAs one SM holds; INT32_MAX units: the maximum).
 int attend_grid(int dh, int P, int units, int sm_count);
 // Floats of partial-result scratch per slot.
 __host__ __device__ inline int64_t attend_partial_floats(int dh) { return 32 + 16 * (int64_t)dh; }

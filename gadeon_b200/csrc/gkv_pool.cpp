@@ -170,7 +170,8 @@ struct gkv_pool {
     float *d_partials = nullptr;
     int32_t *d_counters = nullptr;
     uint16_t *d_prod = nullptr;  // [2][max_seqs * KVH * dh] fp16 K/V rows of gkv_attn_step's unfused route
-    CUtensorMap tmk{}, tmv{};
+    CUtensorMap tmk{}, tmv{};  // chunk kernel: boxes of min(P, 64) rows
+    CUtensorMap tak{}, tav{};  // attend kernel: boxes of min(P, tile_keys) rows
     std::vector<int32_t> stack;  // free list; back() is the head
     std::vector<int32_t> ref;
     std::vector<Seq> seqs;
@@ -429,7 +430,7 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
     p.scale_log2 = scale * 1.4426950408889634f;
     if (prod) p.prod = *prod;
     const int grid = gkv::attend_grid(pool->cfg.head_dim, p.P, (int)units, pool->sm_count);
-    GKV_CUDA(gkv::launch_attend(p, &pool->tmk, &pool->tmv, pool->cfg.head_dim, grid, st, inl ? &desc : nullptr),
+    GKV_CUDA(gkv::launch_attend(p, &pool->tak, &pool->tav, pool->cfg.head_dim, grid, st, inl ? &desc : nullptr),
              "attend kernel launch");
     if (!inl) GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
     return GKV_OK;
@@ -603,7 +604,8 @@ int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out) {
     GKV_ALLOC(p->d_table, sizeof(int32_t) * (size_t)c.max_seqs * c.max_pages_per_seq);
     GKV_ALLOC(p->d_status, sizeof(int32_t));
     GKV_ALLOC(p->d_partials,
-              sizeof(float) * (items + p->sm_count) * gkv::attend_partial_floats(c.head_dim));
+              sizeof(float) * (items + gkv::attend_grid(c.head_dim, c.page_tokens, INT32_MAX, p->sm_count)) *
+                  gkv::attend_partial_floats(c.head_dim));
     GKV_ALLOC(p->d_counters, sizeof(int32_t) * items);
     if (gkv::producer_supported(c.head_dim)) GKV_ALLOC(p->d_prod, sizeof(uint16_t) * 2 * items * c.head_dim);
 #undef GKV_ALLOC
@@ -618,19 +620,26 @@ int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out) {
     }
     // TMA views of the pools: rows of head_dim halves, one row per
     // (page, kv head, slot); boxes of 64 columns x BH rows, 128B swizzle.
-    const int bh = std::min(c.page_tokens, p->tile_keys);
+    // The chunk kernel loads page groups of min(P, 64) rows, the attend
+    // kernel groups of min(P, its key tile).
     if (c.page_tokens >= 8) {
         const cuuint64_t dims[2] = {(cuuint64_t)c.head_dim,
                                     (cuuint64_t)c.num_pages * c.kv_heads * c.page_tokens};
         const cuuint64_t strides[1] = {(cuuint64_t)c.head_dim * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)bh};
         const cuuint32_t estr[2] = {1, 1};
-        for (int t = 0; t < 2; ++t) {
-            CUresult r = enc(t == 0 ? &p->tmk : &p->tmv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                             t == 0 ? (void *)p->d_k : (void *)p->d_v, dims, strides, box, estr,
+        struct View {
+            CUtensorMap *map;
+            void *base;
+            int bh;
+        } views[4] = {{&p->tmk, p->d_k, std::min(c.page_tokens, 64)},
+                      {&p->tmv, p->d_v, std::min(c.page_tokens, 64)},
+                      {&p->tak, p->d_k, std::min(c.page_tokens, p->tile_keys)},
+                      {&p->tav, p->d_v, std::min(c.page_tokens, p->tile_keys)}};
+        for (const View &vw : views) {
+            const cuuint32_t box[2] = {64, (cuuint32_t)vw.bh};
+            CUresult r = enc(vw.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vw.base, dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) {
                 free_device(p);
                 delete p;
