@@ -52,6 +52,12 @@ METRIC = "KV append+attend tok/s (paged GQA decode, config 2)"
 UNIT = "tok/s"
 
 
+# DRAM bytes (read + write) per algorithmic byte of the config-2 attend
+# launch, from `ncu --set full` of one launch of the same per-layer workload
+# (64 sequences, 1 layer): 2.2970 GB measured / 2.2898 GB algorithmic.
+NCU_C2_TRAFFIC_PER_ALGO_BYTE = 2.2970 / 2.2898
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -383,7 +389,10 @@ def run_ours(args, rank, world, local):
             "parallelism": f"dp{world} (sequences sharded, no hot-path collective)",
         },
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                     "traffic": NCU_C2_TRAFFIC_PER_ALGO_BYTE * bytes_per_launch,
+                     "traffic_source": "ncu dram__bytes_read+write of one launch of the same per-layer workload "
+                                       "(bench.py --seqs 64 --layers 1), scaled by algorithmic bytes",
                      "kernel": "attend_kernel<256,TMA,fused append>", "bytes_per_launch": bytes_per_launch,
                      "launch_ms": attend_avg_ms, "launch_ms_max_rank": attend_max,
                      "launch_timing": "CUDA-event step time / layers (launches back to back, gaps included)"},
