@@ -46,7 +46,8 @@ sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 
-from gadeon_b200.workload import CONFIGS, append_bytes, contexts, decode_bytes, pool_pages  # noqa: E402
+from gadeon_b200.workload import (CONFIGS, append_bytes, contexts, decode_bytes, pool_pages,  # noqa: E402
+                                  weak_job_contexts, weak_rank_contexts)
 
 METRIC = "KV append+attend tok/s (paged GQA decode, config 2)"
 UNIT = "tok/s"
@@ -192,7 +193,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     cfg = CONFIGS[2]
-    ctx_all = np.concatenate([contexts(2, args.seed + 1000 * r, cfg.seqs) for r in range(world)])
+    ctx_all = weak_job_contexts(2, args.seed, cfg.seqs, world)
     threads = os.cpu_count() or 1
     steps = args.warmup + args.steps
     per_key, desc, cpu_s = cpu_sample(args.seed + 7, 16, steps, threads, cfg, ctx_all)
@@ -226,7 +227,7 @@ def run_ours(args, rank, world, local):
     L = args.layers or L
     S = args.seqs or S
     W, K = args.warmup, args.steps
-    ctx = contexts(2, args.seed + 1000 * rank, S)
+    ctx = weak_rank_contexts(2, args.seed, S, world, rank)
     steps_total = W + K + (0 if args.no_e2e else 2 * K) + 2  # e2e: zero-copy and staged legs
     max_pps = int(math.ceil((int(ctx.max()) + steps_total) / P)) + 2
     n_pages = pool_pages(ctx, P, steps_total)
@@ -384,7 +385,8 @@ def run_ours(args, rank, world, local):
             "workload": (f"config2 decode step: {S} seqs/GPU x {L} layers, append 1 + paged GQA decode attend"
                          + ("" if (S, L) == (cfg.seqs, cfg.layers) else " (REDUCED profiling case)")),
             "seqs_per_gpu": S, "layers": L, "n_heads": nH, "kv_heads": KVH, "head_dim": dh,
-            "page_tokens": P, "ctx": "U[1024,32768] seeded per rank", "ctx_mean": float(ctx.mean()),
+            "page_tokens": P, "ctx": ("U[1024,32768]: %d x %d job sequences token-balanced over the GPUs" % (S, world)
+                    if world > 1 else "U[1024,32768]"), "ctx_mean": float(ctx.mean()),
             "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)" % (float(ctx.sum()) * L * KVH * dh * 4 / 1e9),
             "parallelism": f"dp{world} (sequences sharded, no hot-path collective)",
         },
@@ -716,7 +718,7 @@ def run_config2_producer(args, rank, world, local):
     KVH, dh, G, nH = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads
     n_rot, base = 64, 1e7
     W, K = max(args.warmup, 3), args.steps
-    ctx = contexts(2, args.seed + 1000 * rank, S)
+    ctx = weak_rank_contexts(2, args.seed, S, world, rank)
     pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, W + K + 2, local)
     NS = W + K
     qg = torch.randn((L, S, nH, 2 * dh), generator=gen, device=dev)

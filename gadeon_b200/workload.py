@@ -110,6 +110,39 @@ def lpt_partition(tokens: Sequence[int], parts: int) -> List[List[int]]:
     return [sorted(o) for o in out]
 
 
+def capped_partition(tokens: Sequence[int], parts: int, per_part: int) -> List[List[int]]:
+    """Token-balanced partition with exactly per_part sequences per part
+    (len(tokens) == parts * per_part): sequences by context descending, each
+    to the least-loaded part that still has room (ties -> lowest index).
+    Returns the sequence indices of every part, ascending."""
+    if len(tokens) != parts * per_part:
+        raise ValueError(f"{len(tokens)} sequences do not fill {parts} parts of {per_part}")
+    order = sorted(range(len(tokens)), key=lambda i: (-int(tokens[i]), i))
+    load = [0] * parts
+    out: List[List[int]] = [[] for _ in range(parts)]
+    for i in order:
+        p = min((r for r in range(parts) if len(out[r]) < per_part), key=lambda r: (load[r], r))
+        out[p].append(i)
+        load[p] += int(tokens[i])
+    return [sorted(o) for o in out]
+
+
+def weak_job_contexts(cfg_id: int, seed: int, per_gpu: int, world: int) -> np.ndarray:
+    """Contexts of a weak-scaled job on `world` GPUs: per_gpu * world
+    sequences drawn from `seed`, in job order (world = 1: the one-GPU job)."""
+    return contexts(cfg_id, seed, per_gpu * world)
+
+
+def weak_rank_contexts(cfg_id: int, seed: int, per_gpu: int, world: int, rank: int) -> np.ndarray:
+    """This rank's sequences of the weak-scaled job: the job's contexts
+    token-balanced over the GPUs with per_gpu sequences each (the path
+    shards by sequence; every GPU streams the same number of K/V bytes)."""
+    job = weak_job_contexts(cfg_id, seed, per_gpu, world)
+    if world == 1:
+        return job
+    return job[capped_partition(job, world, per_gpu)[rank]]
+
+
 def pool_pages(ctx: Sequence[int], page_tokens: int, growth_tokens: int, factor: float = 1.25) -> int:
     """Physical pages for a layer pool: `factor` x the pages the contexts
     occupy, plus room for `growth_tokens` more per sequence."""

@@ -34,6 +34,25 @@ def test_assign_is_a_token_balanced_partition():
     assert 1 in shards[0] and shards == [[1, 2], [0, 3]]
 
 
+def test_weak_scaled_job_is_count_capped_and_token_balanced():
+    """Config 2 at N GPUs: 64*N job sequences, exactly 64 per rank, token
+    loads within 0.1% of each other; N=1 is the one-GPU job unchanged."""
+    from gadeon_b200.workload import capped_partition, weak_job_contexts, weak_rank_contexts
+    assert np.array_equal(weak_rank_contexts(2, 7, 64, 1, 0), contexts(2, 7, 64))
+    for world in (2, 4, 8):
+        job = weak_job_contexts(2, 7, 64, world)
+        parts = capped_partition(job, world, 64)
+        assert sorted(i for p in parts for i in p) == list(range(64 * world))
+        assert all(len(p) == 64 for p in parts)
+        assert imbalance(job, parts) < 1.001
+        for r in range(world):
+            assert np.array_equal(weak_rank_contexts(2, 7, 64, world, r), job[parts[r]])
+    with pytest.raises(ValueError):
+        capped_partition([1, 2, 3], 2, 2)
+    # the cap binds: without it LPT would give the long sequence's part fewer members
+    assert capped_partition([100, 1, 1, 1], 2, 2) == [[0, 1], [2, 3]]
+
+
 def _worker(rank, world, port, fail_rank, q):
     import torch
     import torch.distributed as dist
