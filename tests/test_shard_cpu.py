@@ -49,8 +49,9 @@ def test_weak_scaled_job_is_count_capped_and_token_balanced():
             assert np.array_equal(weak_rank_contexts(2, 7, 64, world, r), job[parts[r]])
     with pytest.raises(ValueError):
         capped_partition([1, 2, 3], 2, 2)
-    # the cap binds: without it LPT would give the long sequence's part fewer members
-    assert capped_partition([100, 1, 1, 1], 2, 2) == [[0, 1], [2, 3]]
+    # the cap binds: plain LPT would put all three short sequences beside each
+    # other; with two per part the last one joins the long sequence
+    assert capped_partition([100, 1, 1, 1], 2, 2) == [[0, 3], [1, 2]]
 
 
 def _worker(rank, world, port, fail_rank, q):
