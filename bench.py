@@ -960,6 +960,10 @@ def main():
     if world > 1:
         import torch
         import torch.distributed as dist
+        # NCCL writes its log (the version line included, at NCCL_DEBUG=WARN
+        # or VERSION) to stdout unless told otherwise: keep stdout to the one
+        # JSON line rank 0 prints
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
