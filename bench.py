@@ -945,8 +945,20 @@ def run_config7(args, rank, world, local):
         "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 2 + 2 + 1), "clocks": clk}), flush=True)
 
 
+def _json_only_stdout():
+    """Keep the process's stdout for the JSON line alone: Python's sys.stdout
+    moves to a duplicate of the original descriptor, and descriptor 1 itself
+    is pointed at stderr, so whatever a native library prints there (NCCL's
+    version banner at communicator set-up) lands on stderr."""
+    sys.stdout.flush()
+    fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(fd, "w", buffering=1)
+
+
 def main():
     args = parse_args()
+    _json_only_stdout()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -960,10 +972,6 @@ def main():
     if world > 1:
         import torch
         import torch.distributed as dist
-        # NCCL writes its log (the version line included, at NCCL_DEBUG=WARN
-        # or VERSION) to stdout unless told otherwise: keep stdout to the one
-        # JSON line rank 0 prints
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
