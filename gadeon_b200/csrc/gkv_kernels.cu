@@ -44,9 +44,14 @@ namespace {
 using namespace ptx;
 
 // ------------------------------------------------------------ append
-__global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
-    const TouchedPage tp = p.pages[blockIdx.x];
-    const AppendEntry e = p.entries[tp.entry];
+__global__ void __launch_bounds__(256)
+    append_kernel(const __grid_constant__ AppendParams p, const __grid_constant__ AppendInline d) {
+    // launched with programmatic stream serialization: everything below
+    // waits for the previous kernel's memory; the next may start its set-up
+    grid_dep_launch_dependents();
+    grid_dep_wait();
+    const TouchedPage tp = (p.pages ? p.pages : d.pages)[blockIdx.x];
+    const AppendEntry e = (p.entries ? p.entries : d.entries)[tp.entry];
     const int P = p.P, dh = p.dh, KVH = p.kvh;
     const int CH = dh >> 3;  // 16-byte chunks per row
     const int64_t page_lo = (int64_t)tp.pidx * P;
@@ -819,10 +824,19 @@ cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const 
 
 }  // namespace
 
-cudaError_t launch_append(const AppendParams &p, cudaStream_t s) {
+cudaError_t launch_append(const AppendParams &p, cudaStream_t s, const AppendInline *inl) {
     if (p.n_pages <= 0) return cudaSuccess;
-    append_kernel<<<p.n_pages, 256, 0, s>>>(p);
-    return cudaGetLastError();
+    static const AppendInline empty_desc{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)p.n_pages);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, append_kernel, p, inl ? *inl : empty_desc);
 }
 
 cudaError_t launch_compact(const CompactParams &p, cudaStream_t s) {

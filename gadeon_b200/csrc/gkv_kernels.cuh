@@ -37,9 +37,19 @@ struct TouchedPage {
 constexpr int32_t PAGE_EXISTING = -1;
 constexpr int32_t PAGE_NEW = -2;
 
+// An append touching at most kAppendInlinePages pages of at most
+// kAppendInlineEntries sequences carries its descriptor in the kernel's
+// parameter block (no upload before the launch).
+constexpr int kAppendInlineEntries = 128;
+constexpr int kAppendInlinePages = 256;
+struct AppendInline {
+    AppendEntry entries[kAppendInlineEntries];
+    TouchedPage pages[kAppendInlinePages];
+};
+
 struct AppendParams {
-    const AppendEntry *entries;
-    const TouchedPage *pages;
+    const AppendEntry *entries;  // null: AppendInline::entries
+    const TouchedPage *pages;    // null: AppendInline::pages
     int32_t n_pages;
     const uint16_t *k_src;  // token-major [rows, KVH, dh] or head-major [KVH, rows, dh]
     const uint16_t *v_src;
@@ -127,7 +137,8 @@ struct ProduceParams {
 };
 
 // Host-side launchers (gkv_kernels.cu).
-cudaError_t launch_append(const AppendParams &p, cudaStream_t s);
+// inl: the inline descriptor when p.entries / p.pages are null.
+cudaError_t launch_append(const AppendParams &p, cudaStream_t s, const AppendInline *inl = nullptr);
 // Number of CTAs the attend launch will use for `units` work units (at
 // most sm_count times the CTAs one SM holds; INT32_MAX units: the maximum).
 int attend_grid(int dh, int P, int units, int sm_count);

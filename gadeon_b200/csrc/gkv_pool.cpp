@@ -294,15 +294,26 @@ int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
     if (pages.empty()) return GKV_OK;
     const size_t eb = entries.size() * sizeof(gkv::AppendEntry);
     const size_t pb = pages.size() * sizeof(gkv::TouchedPage);
-    cudaError_t err;
-    const int slot = pool->staging.acquire(eb + pb, &err);
-    if (slot < 0) return cuda_fail(err, "descriptor staging");
-    memcpy(pool->staging.host(slot), entries.data(), eb);
-    memcpy(pool->staging.host(slot) + eb, pages.data(), pb);
-    GKV_CUDA(pool->staging.upload(slot, eb + pb, st), "descriptor upload");
+    // small appends (decode rows, MTP drafts) carry the descriptor in the
+    // kernel's parameter block; large ones (prefill chunks) upload it
+    const bool inl = entries.size() <= (size_t)gkv::kAppendInlineEntries &&
+                     pages.size() <= (size_t)gkv::kAppendInlinePages;
+    gkv::AppendInline desc;
     gkv::AppendParams p{};
-    p.entries = reinterpret_cast<const gkv::AppendEntry *>(pool->staging.dev(slot));
-    p.pages = reinterpret_cast<const gkv::TouchedPage *>(pool->staging.dev(slot) + eb);
+    int slot = -1;
+    if (inl) {
+        memcpy(desc.entries, entries.data(), eb);
+        memcpy(desc.pages, pages.data(), pb);
+    } else {
+        cudaError_t err;
+        slot = pool->staging.acquire(eb + pb, &err);
+        if (slot < 0) return cuda_fail(err, "descriptor staging");
+        memcpy(pool->staging.host(slot), entries.data(), eb);
+        memcpy(pool->staging.host(slot) + eb, pages.data(), pb);
+        GKV_CUDA(pool->staging.upload(slot, eb + pb, st), "descriptor upload");
+        p.entries = reinterpret_cast<const gkv::AppendEntry *>(pool->staging.dev(slot));
+        p.pages = reinterpret_cast<const gkv::TouchedPage *>(pool->staging.dev(slot) + eb);
+    }
     p.n_pages = (int32_t)pages.size();
     p.k_src = static_cast<const uint16_t *>(k);
     p.v_src = static_cast<const uint16_t *>(v);
@@ -314,8 +325,8 @@ int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
     p.kvh = pool->cfg.kv_heads;
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
-    GKV_CUDA(gkv::launch_append(p, st), "append kernel launch");
-    GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
+    GKV_CUDA(gkv::launch_append(p, st, inl ? &desc : nullptr), "append kernel launch");
+    if (!inl) GKV_CUDA(pool->staging.done(slot, st), "descriptor event");
     return GKV_OK;
 }
 
