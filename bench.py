@@ -72,6 +72,8 @@ def parse_args():
     # a line measured with them is not the config-2 number
     ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: config 2's 6)")
+    ap.add_argument("--gdn-f32", action="store_true",
+                    help="configs 6/7: GDN state and conv tail in fp32 (default fp16, the reference's storage)")
     ap.add_argument("--producer", action="store_true",
                     help="config 2 through gkv_attn_step: raw fp32 q|gate, k, v projections, RMSNorm + RoPE "
                          "+ output gate fused into the decode step (Qwen3.5 attention layer)")
@@ -771,8 +773,9 @@ def run_config6(args, rank, world, local):
     """GDN rollback beside config 3: per step, every one of 128 sequences
     (per GPU) rolls back the recurrent state and conv tail of its 3 GDN
     layers to an accepted length m ~ U{1..5} (seeded).  One state launch and
-    one conv launch cover all (sequence, layer) items; fp32 state, inputs
-    far larger than L2."""
+    one conv launch cover all (sequence, layer) items; the state and conv
+    tail stored in fp16 as the reference stores them (fp32 with --gdn-f32),
+    inputs far larger than L2."""
     import torch
     import torch.distributed as dist
     import gadeon_b200 as gk
@@ -785,13 +788,15 @@ def run_config6(args, rank, world, local):
     W, K = max(args.warmup, 3), max(args.steps, 50)
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 31 * rank)
-    s0 = torch.randn((n, H, D, D), generator=gen, device=dev) * 0.1
+    sdt = torch.float32 if args.gdn_f32 else torch.float16
+    sb = 4 if args.gdn_f32 else 2
+    s0 = (torch.randn((n, H, D, D), generator=gen, device=dev) * 0.1).to(sdt)
     out = torch.empty_like(s0)
     kk = torch.randn((n, H, Cw, D), generator=gen, device=dev) / math.sqrt(D)
     delta = torch.randn((n, H, Cw, D), generator=gen, device=dev) * 0.5
     gcum = torch.cumsum(-torch.rand((n, H, Cw), generator=gen, device=dev) * 0.7, dim=-1)
     proj = torch.randn((n, Cw, CD), generator=gen, device=dev)
-    pre = torch.randn((n, CD, T), generator=gen, device=dev)
+    pre = torch.randn((n, CD, T), generator=gen, device=dev).to(sdt)
     conv = torch.empty_like(pre)
     rng = np.random.default_rng(args.seed + 17 * rank)
     ms_acc = rng.integers(1, Cw + 1, size=(W + K, n)).astype(np.int32)
@@ -807,8 +812,8 @@ def run_config6(args, rank, world, local):
 
     ms, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
-    bpl = statistics.mean(rollback_bytes(ms_acc[W + i], g)[0] for i in range(K))
-    step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g)) for i in range(K))
+    bpl = statistics.mean(rollback_bytes(ms_acc[W + i], g, sb)[0] for i in range(K))
+    step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)) for i in range(K))
     hbm, kind = peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -816,10 +821,11 @@ def run_config6(args, rank, world, local):
         ns = 8
         a = [x[:ns].cpu().numpy() for x in (s0, delta, kk, gcum)]
         mm = ms_acc[0, :ns]
-        O.mtp_rollback(mm, *a)
+        orc = O.mtp_rollback if args.gdn_f32 else O.mtp_rollback_f16
+        orc(mm, *a)
         reps, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < 10.0:
-            O.mtp_rollback(mm, *a)
+            orc(mm, *a)
             reps += 1
         dt = (time.perf_counter() - t0) / reps
         cpu = {"value": ns / g.layers / dt, "unit": "seq/s", "cores": 1, "kind": "port",
@@ -833,12 +839,14 @@ def run_config6(args, rank, world, local):
         "metric": "GDN MTP rollback: sequences rolled back/s (all GDN layers of one attention block)",
         "value": seqs * world / (ms * 1e-3), "unit": "seq/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded torch.randn state, keys, deltas; gates = negative cumsums)",
+        "dtype": "f32 compute, " + ("f32 state" if args.gdn_f32 else "fp16 state and conv tail (reference storage)"),
+        "data": "synthetic (seeded torch.randn state, keys, deltas; gates = negative cumsums)",
         "config": {"workload": f"config6: {seqs} seqs/GPU x {n // seqs} GDN layers; value heads {H}, "
                                f"DK=DV={D}, C={Cw}, conv {CD}x{T} taps; m ~ U{{1..{Cw}}}",
                    "step_bytes": step_bytes, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None, "kernel": "mtp_rollback_kernel",
+                     "peak_kind": kind, "traffic": None,
+                     "kernel": "mtp_rollback_fast_kernel<%s>" % ("float" if args.gdn_f32 else "half"),
                      "bytes_per_launch": bpl, "launch_ms": launch_ms},
         "step_gbs": step_bytes / (ms * 1e-3) / 1e9,
         "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * 2, "clocks": clk}), flush=True)
@@ -878,13 +886,15 @@ def run_config7(args, rank, world, local):
     out4 = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
     n_items = S * g.layers
     H, D, Cw = g.value_heads, g.head_dim, nq
-    s0 = torch.randn((n_items, H, D, D), generator=gen, device=dev) * 0.1
+    # GDN state and conv tail in fp16, as the reference stores them (fp32 with --gdn-f32)
+    sdt = torch.float32 if args.gdn_f32 else torch.float16
+    s0 = (torch.randn((n_items, H, D, D), generator=gen, device=dev) * 0.1).to(sdt)
     s_out = torch.empty_like(s0)
     gk_ = torch.randn((n_items, H, Cw, D), generator=gen, device=dev) / math.sqrt(D)
     gd = torch.randn((n_items, H, Cw, D), generator=gen, device=dev) * 0.5
     gc = torch.cumsum(-torch.rand((n_items, H, Cw), generator=gen, device=dev) * 0.7, dim=-1)
     proj = torch.randn((n_items, Cw, g.conv_dim), generator=gen, device=dev)
-    pre = torch.randn((n_items, g.conv_dim, g.taps), generator=gen, device=dev)
+    pre = torch.randn((n_items, g.conv_dim, g.taps), generator=gen, device=dev).to(sdt)
     conv = torch.empty_like(pre)
     rng = np.random.default_rng(args.seed + 17 * rank)
     acc = rng.integers(1, nq + 1, size=(W + K, S))  # m = accepted drafts + 1
@@ -927,13 +937,15 @@ def run_config7(args, rank, world, local):
         assert p_.device_status() == 0
     if rank != 0:
         return
-    rb = statistics.mean(sum(rollback_bytes(np.repeat(acc[W + i], g.layers), g)) for i in range(K))
+    rb = statistics.mean(sum(rollback_bytes(np.repeat(acc[W + i], g.layers), g, 4 if args.gdn_f32 else 2))
+                         for i in range(K))
     cycle_bytes = sum(att_bytes) / K + append_bytes(S * nq, cfg) + append_bytes(int(acc[W:].sum() / K), cfg) + rb
     print(json.dumps({
         "metric": "MTP cycle: committed tokens/s (drafts + verify + rollback + drafter rewind, config 3 geometry)",
         "value": committed * world / (K * ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 accumulate, fp16 K/V/Q storage, f32 GDN state", "data": "synthetic (seeded)",
+        "dtype": "f32 accumulate, fp16 K/V/Q storage, " + ("f32 GDN state" if args.gdn_f32 else "fp16 GDN state"),
+        "data": "synthetic (seeded)",
         "config": {"workload": f"config7: {S} seqs/GPU at ctx 8192, 1 attention layer + its drafter pool + "
                                f"{g.layers} GDN layers; {n_draft} drafts, verify {nq} rows, m ~ U{{1..{nq}}}",
                    "mean_committed_per_seq_cycle": committed / (K * S), "l2": "inputs larger than L2"},

@@ -13,6 +13,7 @@
 // items are (sequence, GDN layer) pairs of a batch, each with its own m.
 // The per-item m travels in the kernel parameters, so a call allocates
 // nothing and needs no upload.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <utility>
 
@@ -29,18 +30,73 @@ namespace {
 constexpr int kMaxItemsPerLaunch = 2048;
 constexpr int kMaxChunk = 64;  // verify width C
 
+// State storage T: float (fp32 in and out) or __half -- the reference's own
+// storage (Engine.rollbackGDN reads the fp16 gdnState arrays, rebuilds in
+// fp32 and writes them back through fp16Array, Engine.swift:2697-2705):
+// widened exactly on load, rounded to nearest even on store, the fp32
+// arithmetic in between unchanged.
+template <typename T>
 struct RollbackParams {
     int32_t H, DK, DV, C;
-    const float *s0, *delta, *k, *gcum;
-    float *out;
+    const T *s0;
+    const float *delta, *k, *gcum;
+    T *out;
     int32_t m[kMaxItemsPerLaunch];
 };
 
+template <typename T>
 struct ConvParams {
     int32_t CD, taps, C;
-    const float *proj, *pre;
-    float *out;
+    const float *proj;
+    const T *pre;
+    T *out;
     int32_t m[kMaxItemsPerLaunch];
+};
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// COLS consecutive state elements moved as one 8- or 16-byte access.
+template <typename T, int COLS>
+struct Cols;
+template <>
+struct Cols<float, 4> {
+    using raw = float4;
+    __device__ static void unpack(const raw &r, float (&v)[4]) { v[0] = r.x, v[1] = r.y, v[2] = r.z, v[3] = r.w; }
+    __device__ static raw pack(const float (&v)[4]) { return make_float4(v[0], v[1], v[2], v[3]); }
+};
+__device__ __forceinline__ float2 h2_to_f2(uint32_t x) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&x));
+}
+__device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+template <>
+struct Cols<__half, 4> {
+    using raw = uint2;
+    __device__ static void unpack(const raw &r, float (&v)[4]) {
+        const float2 a = h2_to_f2(r.x), b = h2_to_f2(r.y);
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+    }
+    __device__ static raw pack(const float (&v)[4]) { return make_uint2(f2_to_h2(v[0], v[1]), f2_to_h2(v[2], v[3])); }
+};
+template <>
+struct Cols<__half, 8> {
+    using raw = uint4;
+    __device__ static void unpack(const raw &r, float (&v)[8]) {
+        const float2 a = h2_to_f2(r.x), b = h2_to_f2(r.y), c = h2_to_f2(r.z), d = h2_to_f2(r.w);
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y, v[4] = c.x, v[5] = c.y, v[6] = d.x, v[7] = d.y;
+    }
+    __device__ static raw pack(const float (&v)[8]) {
+        return make_uint4(f2_to_h2(v[0], v[1]), f2_to_h2(v[2], v[3]), f2_to_h2(v[4], v[5]), f2_to_h2(v[6], v[7]));
+    }
 };
 
 // One CTA per (item, value head): the head's [DK, DV] state streams through
@@ -49,8 +105,8 @@ struct ConvParams {
 constexpr int kRollThreads = 256;
 constexpr int kUnroll = 4;
 
-__device__ __forceinline__ float4 rollback_elem(const RollbackParams &p, const float *w, float eM, const float *kk,
-                                                const float *dd, int m, int e4, float4 s) {
+__device__ __forceinline__ float4 rollback_elem(const RollbackParams<float> &p, const float *w, float eM,
+                                                const float *kk, const float *dd, int m, int e4, float4 s) {
     const int i = e4 * 4 / p.DV, j = e4 * 4 % p.DV;
     // reference order: out = eM * s0, then out += (w_t * k_t[i]) * delta_t[j]
     // for t ascending, each multiply and add rounded on its own
@@ -68,8 +124,9 @@ __device__ __forceinline__ float4 rollback_elem(const RollbackParams &p, const f
 
 // Any DV: one element per thread step, same operation order as the vector
 // path.
-__device__ __forceinline__ float rollback_scalar(const RollbackParams &p, const float *w, float eM, const float *kk,
-                                                 const float *dd, int m, int e, float s) {
+template <typename T>
+__device__ __forceinline__ float rollback_scalar(const RollbackParams<T> &p, const float *w, float eM,
+                                                 const float *kk, const float *dd, int m, int e, float s) {
     const int i = e / p.DV, j = e % p.DV;
     float o = __fmul_rn(eM, s);
     for (int t = 0; t < m; ++t)
@@ -77,8 +134,9 @@ __device__ __forceinline__ float rollback_scalar(const RollbackParams &p, const 
     return o;
 }
 
-template <bool VEC>
-__global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid_constant__ RollbackParams p) {
+// VEC (fp32 only): float4 rows; otherwise one element at a time.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid_constant__ RollbackParams<T> p) {
     __shared__ float w[kMaxChunk];
     __shared__ float eM;
     const int hs = blockIdx.x;  // item * H + head
@@ -92,6 +150,7 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid
     const float *dd = p.delta + (int64_t)hs * p.C * p.DV;
     const float e = eM;
     if constexpr (VEC) {
+        static_assert(sizeof(T) == 4, "float4 rows of an fp32 state");
         const int nv4 = p.DK * p.DV / 4;
         const float4 *s4 = reinterpret_cast<const float4 *>(p.s0 + sbase);
         float4 *o4 = reinterpret_cast<float4 *>(p.out + sbase);
@@ -111,14 +170,17 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_kernel(const __grid
     } else {
         const int n = p.DK * p.DV;
         for (int x = threadIdx.x; x < n; x += kRollThreads)
-            p.out[sbase + x] = rollback_scalar(p, w, e, kk, dd, m, x, p.s0[sbase + x]);
+            p.out[sbase + x] = from_f32<T>(rollback_scalar(p, w, e, kk, dd, m, x, to_f32(p.s0[sbase + x])));
     }
 }
 
 // grid (ceil(CD / 256), items): thread = one channel c of one item, all its
 // taps; reads of proj rows and writes of the [CD, taps] tail are coalesced
-// across the warp's consecutive channels.
-__global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constant__ ConvParams p) {
+// across the warp's consecutive channels.  fp16 storage: a proj value is
+// rounded to nearest even (Float16(val), Engine.swift:2733), a carried tap
+// is copied as it was.
+template <typename T>
+__global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constant__ ConvParams<T> p) {
     const int item = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= p.CD) return;
@@ -127,22 +189,33 @@ __global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constan
     const int64_t tail = ((int64_t)item * p.CD + c) * p.taps;
     for (int t = 0; t < p.taps; ++t) {
         const int pos = m - p.taps + t;
-        p.out[tail + t] = pos >= 0 ? __ldcs(proj + (int64_t)pos * p.CD) : __ldcs(p.pre + tail + m + t);
+        p.out[tail + t] = pos >= 0 ? from_f32<T>(__ldcs(proj + (int64_t)pos * p.CD)) : p.pre[tail + m + t];
     }
 }
 
-// Fast path for the verify widths MTP uses (C <= kFastC) and DV % 4 == 0,
-// DV <= 4 * kRollThreads, DK <= kFastDK: thread = one float4 column group cg
-// of the state and rows r0, r0 + rstride, ...; its delta_t[cg] for t < m
-// live in registers, the m rows of w_t * k_t (the reference's wk) in shared
-// memory, read as warp-wide broadcasts when a warp covers one row.  The
-// state streams through kFastUnroll float4 loads in flight per thread; the
+// Fast path for the verify widths MTP uses (C <= kFastC), DV a multiple of
+// COLS with DV <= COLS * kRollThreads, DK <= kFastDK: thread = one group cg
+// of COLS state columns and rows r0, r0 + rstride, ...; its delta_t[cg] for
+// t < m live in registers, the m rows of w_t * k_t (the reference's wk) in
+// shared memory, read as warp-wide broadcasts when a warp covers one row.
+// The state streams through UNROLL 16-byte loads in flight per thread; the
 // first batch is issued before the prologue so its latency overlaps it.
 constexpr int kFastC = 8;
 constexpr int kFastDK = 256;
-constexpr int kFastUnroll = 4;  // 8 needs 80 registers: 3 CTAs/SM and 0.89 of the HBM copy rate; 4 reaches 0.94
+constexpr int kFastUnroll = 4;  // fp32: 8 needs 80 registers, 3 CTAs/SM and 0.89 of the HBM copy rate; 4 reaches 0.94
+// fp16 state kernel shape, measured on config 6 (128 sequences x 3 GDN layers,
+// 32 heads of 128 x 128, C = 5): state launch 0.164 ms with 128 threads x 8
+// columns x 4 loads in flight (74 registers); 256 threads: 0.206 ms; 8 loads:
+// 0.178 ms; 4 columns x 8 loads: 0.186 ms; 64 threads: 0.162 ms.  Smaller CTAs
+// win because each pays a fixed prologue (gate weights, wk rows, delta) on
+// half the bytes an fp32 CTA streams.
+constexpr int kF16Cols = 8;       // fp16 columns per thread (one 16-byte access)
+constexpr int kF16Unroll = 4;     // state loads in flight per thread
+constexpr int kF16Threads = 128;
+constexpr int kF16NarrowC = 5;              // verify width of the MTP cycle (token + 4 drafts)
 
-__global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams p) {
+// fp32 state: thread = one float4 column group (64 registers, 4 CTAs/SM).
+__global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_f32_kernel(const __grid_constant__ RollbackParams<float> p) {
     __shared__ float kw[kFastC][kFastDK];
     __shared__ float eM_s;
     const int hs = blockIdx.x;
@@ -207,18 +280,91 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_kernel(const _
     }
 }
 
+// fp16 state: thread = COLS columns moved as one 8- or 16-byte access, the
+// same arithmetic per element as the fp32 kernel.
+template <typename T, int COLS, int UNROLL, int MAXC, int THREADS>
+__global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams<T> p) {
+    using V = Cols<T, COLS>;
+    using R = typename V::raw;
+    __shared__ float kw[kFastC][kFastDK];
+    __shared__ float eM_s;
+    const int hs = blockIdx.x;
+    const int m = p.m[hs / p.H];
+    const int ncg = p.DV / COLS;
+    const int rstride = THREADS / ncg;
+    const int cg = threadIdx.x % ncg, r0 = threadIdx.x / ncg;
+    const bool active = r0 < rstride;
+    const int64_t sbase = (int64_t)hs * p.DK * p.DV;
+    const R *s4 = reinterpret_cast<const R *>(p.s0 + sbase);
+    R *o4 = reinterpret_cast<R *>(p.out + sbase);
+    R s[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const int i = r0 + u * rstride;
+        if (active && i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
+    }
+    // prologue: gate weights, wk rows, this thread's delta columns
+    const float *g = p.gcum + (int64_t)hs * p.C;
+    const float gLast = g[m - 1];
+    const float *kk = p.k + (int64_t)hs * p.C * p.DK;
+    for (int x = threadIdx.x; x < m * p.DK; x += THREADS) {
+        const int t = x / p.DK, i = x - t * p.DK;
+        kw[t][i] = __fmul_rn(expf(gLast - g[t]), kk[x]);
+    }
+    if (threadIdx.x == 0) eM_s = expf(gLast);
+    float d[MAXC][COLS];
+    const float4 *d4 = reinterpret_cast<const float4 *>(p.delta + (int64_t)hs * p.C * p.DV);
+#pragma unroll
+    for (int t = 0; t < MAXC; ++t)
+        if (t < m) {
+#pragma unroll
+            for (int q = 0; q < COLS / 4; ++q) {
+                const float4 x = __ldg(d4 + (t * ncg + cg) * (COLS / 4) + q);
+                d[t][4 * q] = x.x, d[t][4 * q + 1] = x.y, d[t][4 * q + 2] = x.z, d[t][4 * q + 3] = x.w;
+            }
+        }
+    __syncthreads();
+    if (!active) return;
+    const float eM = eM_s;
+    for (int base = r0;; base += UNROLL * rstride) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int i = base + u * rstride;
+            if (i < p.DK) {
+                float o[COLS];
+                V::unpack(s[u], o);
+#pragma unroll
+                for (int c = 0; c < COLS; ++c) o[c] = __fmul_rn(eM, o[c]);
+#pragma unroll
+                for (int t = 0; t < MAXC; ++t) {
+                    if (t < m) {
+                        const float wk = kw[t][i];
+#pragma unroll
+                        for (int c = 0; c < COLS; ++c) o[c] = __fadd_rn(o[c], __fmul_rn(wk, d[t][c]));
+                    }
+                }
+                __stcs(o4 + (int64_t)i * ncg + cg, V::pack(o));
+            }
+        }
+        const int next = base + UNROLL * rstride;
+        if (next >= p.DK) break;
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int i = next + u * rstride;
+            if (i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
+        }
+    }
+}
+
 bool misaligned(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 
-}  // namespace
-}  // namespace gkv
-
-extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV,
-                                int32_t C, const float *s0, const float *delta, const float *k,
-                                const float *gcum, float *out, void *stream) {
-    using gkv::report_error;
+template <typename T>
+int mtp_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                      const T *s0, const float *delta, const float *k, const float *gcum, T *out, void *stream) {
+    constexpr bool F16 = sizeof(T) == 2;
     if (n_items < 0 || H < 1 || DK < 1 || DV < 1 || C < 1)
         return report_error(GKV_ERR_INVALID, "n_items=%d H=%d DK=%d DV=%d C=%d", n_items, H, DK, DV, C);
-    if (C > gkv::kMaxChunk) return report_error(GKV_ERR_UNSUPPORTED, "C=%d > %d", C, gkv::kMaxChunk);
+    if (C > kMaxChunk) return report_error(GKV_ERR_UNSUPPORTED, "C=%d > %d", C, kMaxChunk);
     if (H > (1 << 20)) return report_error(GKV_ERR_CAPACITY, "H=%d", H);
     if ((int64_t)DK * DV > (1LL << 30)) return report_error(GKV_ERR_CAPACITY, "DK*DV=%lld", (long long)DK * DV);
     if (n_items == 0) return GKV_OK;
@@ -226,21 +372,23 @@ extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, in
     for (const auto &b : {std::make_pair((const void *)s0, "s0"), std::make_pair((const void *)delta, "delta"),
                           std::make_pair((const void *)k, "k"), std::make_pair((const void *)gcum, "gcum"),
                           std::make_pair((const void *)out, "out")})
-        if (const int rc = gkv::check_reachable(b.first, -1, false, b.second)) return rc;
-    if ((reinterpret_cast<uintptr_t>(s0) | reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(k) |
-         reinterpret_cast<uintptr_t>(gcum) | reinterpret_cast<uintptr_t>(out)) & 3)
+        if (const int rc = check_reachable(b.first, -1, false, b.second)) return rc;
+    if ((reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(gcum)) & 3)
         return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
-    // float4 path: rows of DV a multiple of 4 floats on 16-byte boundaries
-    const bool vec = DV % 4 == 0 && !gkv::misaligned(s0) && !gkv::misaligned(delta) && !gkv::misaligned(out);
-    const bool fast = vec && C <= gkv::kFastC && DK <= gkv::kFastDK && DV <= 4 * gkv::kRollThreads;
+    if ((reinterpret_cast<uintptr_t>(s0) | reinterpret_cast<uintptr_t>(out)) & (sizeof(T) - 1))
+        return report_error(GKV_ERR_INVALID, "state arrays must be %d-byte aligned", (int)sizeof(T));
+    // 16-byte rows: fp32 as float4 (DV % 4 == 0), fp16 as 8 halves (DV % 8 == 0)
+    constexpr int COLS = F16 ? kF16Cols : 4;
+    const bool vec = DV % COLS == 0 && !misaligned(s0) && !misaligned(delta) && !misaligned(out);
+    const bool fast = vec && C <= kFastC && DK <= kFastDK && DV <= COLS * (F16 ? kF16Threads : kRollThreads);
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     // items per launch: what the parameter block's m[] holds
-    const int32_t per = gkv::kMaxItemsPerLaunch;
+    const int32_t per = kMaxItemsPerLaunch;
     for (int32_t first = 0; first < n_items; first += per) {
         const int32_t cnt = n_items - first < per ? n_items - first : per;
-        gkv::RollbackParams p{};
+        RollbackParams<T> p{};
         p.H = H;
         p.DK = DK;
         p.DV = DV;
@@ -253,36 +401,47 @@ extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, in
         p.out = out + hs0 * DK * DV;
         for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
         const unsigned blocks = (unsigned)((int64_t)cnt * H);
-        if (fast)
-            gkv::mtp_rollback_fast_kernel<<<blocks, gkv::kRollThreads, 0, st>>>(p);
-        else if (vec)
-            gkv::mtp_rollback_kernel<true><<<blocks, gkv::kRollThreads, 0, st>>>(p);
-        else
-            gkv::mtp_rollback_kernel<false><<<blocks, gkv::kRollThreads, 0, st>>>(p);
+        if constexpr (!F16) {
+            if (fast)
+                mtp_rollback_fast_f32_kernel<<<blocks, kRollThreads, 0, st>>>(p);
+            else if (vec)
+                mtp_rollback_kernel<T, true><<<blocks, kRollThreads, 0, st>>>(p);
+            else
+                mtp_rollback_kernel<T, false><<<blocks, kRollThreads, 0, st>>>(p);
+        } else {
+            if (fast && C <= kF16NarrowC)
+                mtp_rollback_fast_kernel<T, COLS, kF16Unroll, kF16NarrowC, kF16Threads>
+                    <<<blocks, kF16Threads, 0, st>>>(p);
+            else if (fast)
+                mtp_rollback_fast_kernel<T, COLS, kF16Unroll, kFastC, kF16Threads><<<blocks, kF16Threads, 0, st>>>(p);
+            else
+                mtp_rollback_kernel<T, false><<<blocks, kRollThreads, 0, st>>>(p);
+        }
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "mtp_rollback launch: %s", cudaGetErrorString(e));
     }
     return GKV_OK;
 }
 
-extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
-                                 const float *proj, const float *pre, float *out, void *stream) {
-    using gkv::report_error;
+template <typename T>
+int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
+                       const float *proj, const T *pre, T *out, void *stream) {
     if (n_items < 0 || conv_dim < 1 || taps < 1 || C < 1)
         return report_error(GKV_ERR_INVALID, "n_items=%d conv_dim=%d taps=%d C=%d", n_items, conv_dim, taps, C);
     if (n_items == 0) return GKV_OK;
     if (!m || !proj || !pre || !out) return report_error(GKV_ERR_INVALID, "null pointer");
     for (const auto &b : {std::make_pair((const void *)proj, "proj"), std::make_pair((const void *)pre, "pre"),
                           std::make_pair((const void *)out, "out")})
-        if (const int rc = gkv::check_reachable(b.first, -1, false, b.second)) return rc;
-    if ((reinterpret_cast<uintptr_t>(proj) | reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(out)) & 3)
-        return report_error(GKV_ERR_INVALID, "fp32 arrays must be 4-byte aligned");
+        if (const int rc = check_reachable(b.first, -1, false, b.second)) return rc;
+    if ((reinterpret_cast<uintptr_t>(proj) & 3) ||
+        ((reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(out)) & (sizeof(T) - 1)))
+        return report_error(GKV_ERR_INVALID, "proj must be 4-byte aligned, pre/out %d-byte", (int)sizeof(T));
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    for (int32_t first = 0; first < n_items; first += gkv::kMaxItemsPerLaunch) {
-        const int32_t cnt = n_items - first < gkv::kMaxItemsPerLaunch ? n_items - first : gkv::kMaxItemsPerLaunch;
-        gkv::ConvParams p{};
+    for (int32_t first = 0; first < n_items; first += kMaxItemsPerLaunch) {
+        const int32_t cnt = n_items - first < kMaxItemsPerLaunch ? n_items - first : kMaxItemsPerLaunch;
+        ConvParams<T> p{};
         p.CD = conv_dim;
         p.taps = taps;
         p.C = C;
@@ -291,9 +450,36 @@ extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv
         p.out = out + (int64_t)first * conv_dim * taps;
         for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
         const dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)cnt);
-        gkv::conv_rollback_kernel<<<grid, 256, 0, st>>>(p);
+        conv_rollback_kernel<T><<<grid, 256, 0, st>>>(p);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "conv_rollback launch: %s", cudaGetErrorString(e));
     }
     return GKV_OK;
+}
+
+}  // namespace
+}  // namespace gkv
+
+extern "C" int gkv_mtp_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV,
+                                int32_t C, const float *s0, const float *delta, const float *k,
+                                const float *gcum, float *out, void *stream) {
+    return gkv::mtp_rollback_impl<float>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, out, stream);
+}
+
+extern "C" int gkv_mtp_rollback_f16(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV,
+                                    int32_t C, const void *s0, const float *delta, const float *k,
+                                    const float *gcum, void *out, void *stream) {
+    return gkv::mtp_rollback_impl<__half>(n_items, m, H, DK, DV, C, static_cast<const __half *>(s0), delta, k,
+                                          gcum, static_cast<__half *>(out), stream);
+}
+
+extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
+                                 const float *proj, const float *pre, float *out, void *stream) {
+    return gkv::conv_rollback_impl<float>(n_items, m, conv_dim, taps, C, proj, pre, out, stream);
+}
+
+extern "C" int gkv_conv_rollback_f16(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps,
+                                     int32_t C, const float *proj, const void *pre, void *out, void *stream) {
+    return gkv::conv_rollback_impl<__half>(n_items, m, conv_dim, taps, C, proj, static_cast<const __half *>(pre),
+                                           static_cast<__half *>(out), stream);
 }

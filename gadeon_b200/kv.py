@@ -47,7 +47,7 @@ EXPORTED = (
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
-    "gkv_rewind_append",
+    "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16",
 )
 
 
@@ -113,6 +113,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_state_header": (C.c_int, [P, i64, i64p]),
         "gkv_state_read_header": (C.c_int, [P, i64, i64p]),
         "gkv_conv_rollback": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
+        "gkv_mtp_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
+        "gkv_conv_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -474,42 +476,51 @@ def host_flash_decode(q, pool: PagePool, G: int, stream=None):
 def mtp_rollback(m, s0, delta, k, gcum, out=None, stream=None):
     """``MtpRollback.stateAfter`` (LLM/src/CoreML/MtpRollback.swift:47-60) on the
     GPU for a batch of items (sequence x GDN layer): s0 [n, H, DK, DV],
-    delta [n, H, C, DV], k [n, H, C, DK], gcum [n, H, C] fp32 CUDA tensors,
-    m = accepted prefix per item (1..C).  Returns S_m [n, H, DK, DV] fp32."""
+    delta [n, H, C, DV], k [n, H, C, DK], gcum [n, H, C] CUDA tensors,
+    m = accepted prefix per item (1..C).  Returns S_m [n, H, DK, DV] in s0's
+    dtype: fp32, or fp16 -- the reference's state storage
+    (``gkv_mtp_rollback_f16``: widened, computed in fp32, rounded)."""
     import torch
     L = load_library()
     n, H, DK, DV = (int(x) for x in s0.shape)
     Cw = int(gcum.shape[-1])
+    f16 = str(s0.dtype) == "torch.float16"
+    _check_shape("s0", s0, (n, H, DK, DV), ("float16",) if f16 else ("float32",))
     _check_shape("delta", delta, (n, H, Cw, DV), ("float32",))
     _check_shape("k", k, (n, H, Cw, DK), ("float32",))
     _check_shape("gcum", gcum, (n, H, Cw), ("float32",))
     if out is None:
         out = torch.empty_like(s0)
-    _check_shape("out", out, (n, H, DK, DV), ("float32",))
+    _check_shape("out", out, (n, H, DK, DV), ("float16",) if f16 else ("float32",))
     mm = _i32(m)
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
-    _check(L.gkv_mtp_rollback(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k),
-                              _dev_ptr(gcum), _dev_ptr(out), _stream_ptr(stream)))
+    fn = L.gkv_mtp_rollback_f16 if f16 else L.gkv_mtp_rollback
+    _check(fn(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k),
+              _dev_ptr(gcum), _dev_ptr(out), _stream_ptr(stream)))
     return out
 
 
 def conv_rollback(m, proj, pre, out=None, stream=None):
     """``Engine.convFromProj`` (LLM/src/CoreML/Engine.swift:2719-2740) on the GPU
-    for a batch: proj [n, C, CD], pre [n, CD, taps] fp32 -> [n, CD, taps]."""
+    for a batch: proj [n, C, CD] fp32, pre [n, CD, taps] -> [n, CD, taps] in
+    pre's dtype (fp32, or fp16 as the reference stores the conv tail)."""
     import torch
     L = load_library()
     n, Cw, CD = (int(x) for x in proj.shape)
     taps = int(pre.shape[-1])
-    _check_shape("pre", pre, (n, CD, taps), ("float32",))
+    f16 = str(pre.dtype) == "torch.float16"
+    dt = ("float16",) if f16 else ("float32",)
+    _check_shape("proj", proj, (n, Cw, CD), ("float32",))
+    _check_shape("pre", pre, (n, CD, taps), dt)
     if out is None:
         out = torch.empty_like(pre)
-    _check_shape("out", out, (n, CD, taps), ("float32",))
+    _check_shape("out", out, (n, CD, taps), dt)
     mm = _i32(m)
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
-    _check(L.gkv_conv_rollback(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out),
-                               _stream_ptr(stream)))
+    fn = L.gkv_conv_rollback_f16 if f16 else L.gkv_conv_rollback
+    _check(fn(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out), _stream_ptr(stream)))
     return out
 
 

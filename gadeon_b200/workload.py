@@ -69,14 +69,19 @@ class GdnConfig:
 GDN = GdnConfig()
 
 
-def rollback_bytes(m: Sequence[int], g: GdnConfig) -> tuple:
+def rollback_bytes(m: Sequence[int], g: GdnConfig, state_bytes: int = 4) -> tuple:
     """Algorithmic HBM bytes of one rollback call pair over items with
-    accepted lengths m: (state kernel, conv kernel).  The state is read and
-    written once; only the m accepted rows of k and delta and the gate row
-    are read; the conv tail is written once and each tap read once."""
+    accepted lengths m: (state kernel, conv kernel).  The state (elements of
+    state_bytes: 4 fp32, 2 fp16) is read and written once; only the m
+    accepted rows of k and delta (fp32) and the gate row are read; the conv
+    tail (state_bytes per element) is written once and each tap read once --
+    from the fp32 projection rows or the carried tail."""
     H, D = g.value_heads, g.head_dim
-    state = sum(H * (2 * D * D + int(x) * 2 * D + g.chunk) * 4 for x in m)
-    conv = len(m) * g.conv_dim * g.taps * 2 * 4
+    state = sum(H * (2 * D * D * state_bytes + (int(x) * 2 * D + g.chunk) * 4) for x in m)
+    conv = 0
+    for x in m:
+        from_proj = min(int(x), g.taps)  # taps at positions m - taps + t >= 0
+        conv += g.conv_dim * (g.taps * state_bytes + from_proj * 4 + (g.taps - from_proj) * state_bytes)
     return state, conv
 
 

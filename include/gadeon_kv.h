@@ -242,6 +242,27 @@ int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim,
                       int32_t taps, int32_t C, const float *proj,
                       const float *pre, float *out, void *stream);
 
+/* gkv_mtp_rollback with the state stored as the reference stores it: fp16
+ * (Engine.rollbackGDN, Engine.swift:2697-2705, reads the fp16 gdnState rec
+ * arrays through floats() and writes MtpRollback.stateAfter's result back
+ * through fp16Array).  s0 / out: fp16 [n_items, H, DK, DV], 2-byte aligned;
+ * delta, k, gcum fp32 as above.  Each element is widened exactly, computed
+ * in fp32 in the same order as gkv_mtp_rollback, and rounded to nearest
+ * even: out == fp16(gkv_mtp_rollback(fp32(s0))) bit for bit.  Half the
+ * state bytes of the fp32 entry point. */
+int gkv_mtp_rollback_f16(int32_t n_items, const int32_t *m, int32_t H,
+                         int32_t DK, int32_t DV, int32_t C, const void *s0,
+                         const float *delta, const float *k,
+                         const float *gcum, void *out, void *stream);
+
+/* gkv_conv_rollback with the fp16 conv tail of the reference
+ * (convFromProj, Engine.swift:2719-2740, writes Float16(val)): pre / out
+ * fp16 [n_items, conv_dim, taps]; proj fp32.  A proj value is rounded to
+ * nearest even, a carried tap is copied unchanged. */
+int gkv_conv_rollback_f16(int32_t n_items, const int32_t *m, int32_t conv_dim,
+                          int32_t taps, int32_t C, const float *proj,
+                          const void *pre, void *out, void *stream);
+
 /* Size of the library's static scratch array used by gkv_attend_noalloc
  * (held on every GPU that loads the library until the process exits), and
  * the largest batch that entry point takes. */

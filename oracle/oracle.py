@@ -247,6 +247,22 @@ def mtp_rollback(m, s0, delta, k, gcum) -> np.ndarray:
     return out
 
 
+def mtp_rollback_f16(m, s0_f16, delta, k, gcum) -> np.ndarray:
+    """The reference's storage boundary around stateAfter
+    (LLM/src/CoreML/Engine.swift:2697-2705): the fp16 state widened exactly
+    (floats()), rebuilt in fp32, stored back rounded to nearest even
+    (fp16Array).  s0_f16 / result: float16 [n,H,DK,DV]."""
+    s0 = np.asarray(s0_f16, dtype=np.float16).astype(np.float32)
+    return mtp_rollback(m, s0, delta, k, gcum).astype(np.float16)
+
+
+def conv_rollback_f16(m, proj, pre_f16) -> np.ndarray:
+    """convFromProj with the fp16 conv tail (Engine.swift:2719-2740: the pre
+    tail read through floats(), each tap stored as Float16(val))."""
+    pre = np.asarray(pre_f16, dtype=np.float16).astype(np.float32)
+    return conv_rollback(m, proj, pre).astype(np.float16)
+
+
 def conv_rollback(m, proj, pre) -> np.ndarray:
     """Engine.convFromProj restated: proj [n,C,CD], pre [n,CD,taps] -> [n,CD,taps]."""
     proj = np.ascontiguousarray(proj, dtype=np.float32)

@@ -15,7 +15,7 @@ HEADER = os.path.join(ROOT, "include", "gadeon_kv.h")
 def declared_symbols():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(gkv_[a-z_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(gkv_[a-z0-9_]+)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")

@@ -96,6 +96,36 @@ def test_oracle_matches_closed_form(oracle):
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
 
 
+def half_ulp_f16(x):
+    """Half the spacing of fp16 numbers at |x| (the error of one rounding)."""
+    x = np.abs(np.asarray(x, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(x, 2.0 ** -14)))
+    return 2.0 ** (e - 10) / 2
+
+
+@pytest.mark.parametrize("case", kat_cases(), ids=lambda c: c[0])
+def test_oracle_f16_storage_known_answers(oracle, case):
+    """The reference stores the state in fp16 (Engine.swift:2697-2705): with
+    S0 and the result in fp16 the known answers hold to their tolerance plus
+    one fp16 rounding."""
+    _, m, C, k, d, g, want = case
+    mm, s0, delta, kk, gcum = kat_arrays(m, C, k, d, g)
+    got = oracle.mtp_rollback_f16(mm, s0.astype(np.float16), delta, kk, gcum)
+    assert got.dtype == np.float16
+    want = np.array(want, dtype=np.float64)
+    assert np.all(np.abs(got.reshape(-1).astype(np.float64) - want) <= KAT_TOL + half_ulp_f16(want))
+
+
+def test_oracle_conv_tail_f16(oracle):
+    rng = np.random.default_rng(6)
+    n, C, CD, taps = 5, 5, 16, 3
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float16)
+    m = np.array([1, 2, 3, 4, 5], dtype=np.int32)
+    got = oracle.conv_rollback_f16(m, proj, pre)
+    assert np.array_equal(got, conv_closed_form(m, proj, pre.astype(np.float32)).astype(np.float16))
+
+
 def test_oracle_conv_tail(oracle):
     rng = np.random.default_rng(4)
     n, C, CD, taps = 7, 5, 24, 3
@@ -197,3 +227,68 @@ def test_gpu_rollback_rejects_bad_arguments(cuda):
     with pytest.raises(gk.GkvError) as e:
         gk.conv_rollback([0, 1], proj, pre)
     assert e.value.code == gk.GKV_ERR_INVALID
+
+
+# ---------------------------------------------------------------- GPU: fp16 state storage
+
+F16_SHAPES = [
+    (32, 128, 128, 5), (16, 128, 128, 8), (2, 256, 64, 3),  # fast path (DV % 8 == 0, C <= 8)
+    (4, 64, 96, 17), (2, 8, 12, 4), (3, 5, 6, 7),           # element-wise path
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,DK,DV,C", F16_SHAPES)
+def test_gpu_f16_state_is_the_rounded_fp32_rollback(cuda, oracle, H, DK, DV, C):
+    """gkv_mtp_rollback_f16 == fp16(gkv_mtp_rollback(fp32(s0))) bit for bit:
+    the same fp32 arithmetic in the same order, one rounding at the store;
+    and within one fp16 ulp of the oracle (whose expf may differ by an ulp)."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n = max(C, 6)
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(40 + C, n, H, DK, DV, C, m)
+    s16 = s0.astype(np.float16)
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    got = gk.mtp_rollback(m, _dev(torch, s16), *dev)
+    ref32 = gk.mtp_rollback(m, _dev(torch, s16.astype(np.float32)), *dev)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float16
+    got = got.cpu().numpy()
+    assert np.array_equal(got.view(np.uint16), ref32.cpu().numpy().astype(np.float16).view(np.uint16))
+    want = oracle.mtp_rollback_f16(m, s16, delta, k, gcum).astype(np.float64)
+    got = got.astype(np.float64)
+    # one fp16 ulp at the larger magnitude (values that round to +0 / -0 compare equal)
+    diff = np.abs(got - want)
+    assert np.all(diff <= 2 * half_ulp_f16(np.maximum(np.abs(got), np.abs(want)))), diff.max()
+    assert (diff > 0).mean() < 0.01, (diff > 0).mean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", kat_cases(), ids=lambda c: c[0])
+def test_gpu_f16_reference_known_answers(cuda, case):
+    import gadeon_b200 as gk
+    torch = cuda
+    _, m, C, k, d, g, want = case
+    mm, s0, delta, kk, gcum = kat_arrays(m, C, k, d, g)
+    out = gk.mtp_rollback(mm, _dev(torch, s0.astype(np.float16)), _dev(torch, delta), _dev(torch, kk),
+                          _dev(torch, gcum))
+    torch.cuda.synchronize()
+    want = np.array(want, dtype=np.float64)
+    got = out.cpu().numpy().reshape(-1).astype(np.float64)
+    assert np.all(np.abs(got - want) <= KAT_TOL + half_ulp_f16(want)), (got, want)
+
+
+@pytest.mark.gpu
+def test_gpu_conv_tail_f16_bit_exact(cuda, oracle):
+    import gadeon_b200 as gk
+    torch = cuda
+    rng = np.random.default_rng(7)
+    n, C, CD, taps = 2100, 5, 104, 3
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float16)
+    m = rng.integers(1, C + 1, n).astype(np.int32)
+    got = gk.conv_rollback(m, _dev(torch, proj), _dev(torch, pre))
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float16
+    assert np.array_equal(got.cpu().numpy().view(np.uint16), oracle.conv_rollback_f16(m, proj, pre).view(np.uint16))
