@@ -62,15 +62,9 @@ __device__ __forceinline__ float from_f32<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
-// COLS consecutive state elements moved as one 8- or 16-byte access.
+// COLS consecutive fp16 state elements moved as one 16-byte access.
 template <typename T, int COLS>
 struct Cols;
-template <>
-struct Cols<float, 4> {
-    using raw = float4;
-    __device__ static void unpack(const raw &r, float (&v)[4]) { v[0] = r.x, v[1] = r.y, v[2] = r.z, v[3] = r.w; }
-    __device__ static raw pack(const float (&v)[4]) { return make_float4(v[0], v[1], v[2], v[3]); }
-};
 __device__ __forceinline__ float2 h2_to_f2(uint32_t x) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&x));
 }
@@ -78,15 +72,6 @@ __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
 }
-template <>
-struct Cols<__half, 4> {
-    using raw = uint2;
-    __device__ static void unpack(const raw &r, float (&v)[4]) {
-        const float2 a = h2_to_f2(r.x), b = h2_to_f2(r.y);
-        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
-    }
-    __device__ static raw pack(const float (&v)[4]) { return make_uint2(f2_to_h2(v[0], v[1]), f2_to_h2(v[2], v[3])); }
-};
 template <>
 struct Cols<__half, 8> {
     using raw = uint4;
@@ -280,6 +265,41 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_f32_kernel(con
     }
 }
 
+// The stream loop of the fp16 kernel for a compile-time accepted length M:
+// rows r0, r0 + rstride, ... of the head, UNROLL loads in flight (the first
+// batch already loaded into s), out = eM*s then += wk_t*delta_t, t < M.
+template <typename V, typename R, int COLS, int UNROLL, int MAXC, int M>
+__device__ __forceinline__ void roll_rows(int DK, int r0, int rstride, int ncg, int cg, float eM,
+                                          const float (&kw)[kFastC][kFastDK], const float (&d)[MAXC][COLS],
+                                          R (&s)[UNROLL], const R *s4, R *o4) {
+    for (int base = r0;; base += UNROLL * rstride) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int i = base + u * rstride;
+            if (i < DK) {
+                float o[COLS];
+                V::unpack(s[u], o);
+#pragma unroll
+                for (int c = 0; c < COLS; ++c) o[c] = __fmul_rn(eM, o[c]);
+#pragma unroll
+                for (int t = 0; t < M; ++t) {
+                    const float wk = kw[t][i];
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c) o[c] = __fadd_rn(o[c], __fmul_rn(wk, d[t][c]));
+                }
+                __stcs(o4 + (int64_t)i * ncg + cg, V::pack(o));
+            }
+        }
+        const int next = base + UNROLL * rstride;
+        if (next >= DK) break;
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int i = next + u * rstride;
+            if (i < DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
+        }
+    }
+}
+
 // fp16 state: thread = COLS columns moved as one 8- or 16-byte access, the
 // same arithmetic per element as the fp32 kernel.
 template <typename T, int COLS, int UNROLL, int MAXC, int THREADS>
@@ -326,33 +346,24 @@ __global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid
     __syncthreads();
     if (!active) return;
     const float eM = eM_s;
-    for (int base = r0;; base += UNROLL * rstride) {
-#pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int i = base + u * rstride;
-            if (i < p.DK) {
-                float o[COLS];
-                V::unpack(s[u], o);
-#pragma unroll
-                for (int c = 0; c < COLS; ++c) o[c] = __fmul_rn(eM, o[c]);
-#pragma unroll
-                for (int t = 0; t < MAXC; ++t) {
-                    if (t < m) {
-                        const float wk = kw[t][i];
-#pragma unroll
-                        for (int c = 0; c < COLS; ++c) o[c] = __fadd_rn(o[c], __fmul_rn(wk, d[t][c]));
-                    }
-                }
-                __stcs(o4 + (int64_t)i * ncg + cg, V::pack(o));
-            }
-        }
-        const int next = base + UNROLL * rstride;
-        if (next >= p.DK) break;
-#pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int i = next + u * rstride;
-            if (i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
-        }
+    // m is the same for the whole CTA: a copy of the stream loop per m issues
+    // exactly m multiply-add steps per element instead of MAXC guarded ones
+    switch (m) {
+#define GKV_ROLL_CASE(M) \
+    case M:              \
+        if constexpr (M <= MAXC) roll_rows<V, R, COLS, UNROLL, MAXC, M>(p.DK, r0, rstride, ncg, cg, eM, kw, d, s, s4, o4); \
+        break;
+        GKV_ROLL_CASE(1)
+        GKV_ROLL_CASE(2)
+        GKV_ROLL_CASE(3)
+        GKV_ROLL_CASE(4)
+        GKV_ROLL_CASE(5)
+        GKV_ROLL_CASE(6)
+        GKV_ROLL_CASE(7)
+        GKV_ROLL_CASE(8)
+#undef GKV_ROLL_CASE
+        default:
+            break;
     }
 }
 
