@@ -18,6 +18,7 @@ from .kv import (  # noqa: F401
     BlockPool,
     GkvError,
     PagePool,
+    check_bounded_wait,
     conv_rollback,
     host_flash_decode,
     load_library,

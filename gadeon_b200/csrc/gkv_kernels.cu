@@ -822,7 +822,25 @@ cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const 
     return cudaLaunchKernelEx(&cfg, kern, p, *tk, *tv, desc ? *desc : empty_desc);
 }
 
+// Failure-detection probe: one thread waits, through the same bounded wait
+// every kernel uses, on an mbarrier that nothing ever arrives on.  The wait
+// gives up after limit_ns, records DEV_ERR_WAIT_TIMEOUT in *status and the
+// kernel returns -- no fault, no trap, no hang.
+__global__ void bounded_wait_probe_kernel(int *status, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+    mbar_wait_for(&bar, 0, &abort_flag, status, limit_ns);
+}
+
 }  // namespace
+
+cudaError_t launch_bounded_wait_probe(int *status, uint64_t limit_ns, cudaStream_t s) {
+    bounded_wait_probe_kernel<<<1, 1, 0, s>>>(status, limit_ns);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_append(const AppendParams &p, cudaStream_t s, const AppendInline *inl) {
     if (p.n_pages <= 0) return cudaSuccess;

@@ -137,6 +137,8 @@ struct ProduceParams {
 };
 
 // Host-side launchers (gkv_kernels.cu).
+// One bounded wait on an mbarrier nothing arrives on (gkv_check_bounded_wait).
+cudaError_t launch_bounded_wait_probe(int *status, uint64_t limit_ns, cudaStream_t s);
 // inl: the inline descriptor when p.entries / p.pages are null.
 cudaError_t launch_append(const AppendParams &p, cudaStream_t s, const AppendInline *inl = nullptr);
 // Number of CTAs the attend launch will use for `units` work units (at

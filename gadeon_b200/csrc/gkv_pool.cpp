@@ -1118,6 +1118,25 @@ int gkv_export_page(gkv_pool *pool, int32_t page_id, void *k_host, void *v_host)
     return GKV_OK;
 }
 
+int gkv_check_bounded_wait(int32_t device, int64_t limit_ns, int32_t *status) {
+    if (!status) return fail(GKV_ERR_INVALID, "null status");
+    if (limit_ns < 1000000 || limit_ns > 10000000000ll)
+        return fail(GKV_ERR_INVALID, "limit_ns=%lld (1 ms .. 10 s)", (long long)limit_ns);
+    int count = 0;
+    GKV_CUDA(cudaGetDeviceCount(&count), "device count");
+    if (device < 0 || device >= count) return fail(GKV_ERR_INVALID, "device %d of %d", device, count);
+    DeviceGuard guard(device);
+    int32_t *d = nullptr;
+    GKV_CUDA(cudaMalloc(&d, sizeof(int32_t)), "probe status");
+    cudaError_t e = cudaMemset(d, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = gkv::launch_bounded_wait_probe(d, (uint64_t)limit_ns, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(status, d, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_fail(e, "bounded-wait probe");
+    return GKV_OK;
+}
+
 int gkv_device_status(gkv_pool *pool, int32_t *status) {
     if (!pool || !status) return fail(GKV_ERR_INVALID, "null argument");
     DeviceGuard guard(pool->cfg.device);

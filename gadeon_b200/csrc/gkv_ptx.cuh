@@ -75,19 +75,24 @@ __device__ __forceinline__ uint64_t global_ns() {
 // records DEV_ERR_WAIT_TIMEOUT, raises the CTA's abort flag and gives up.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *status) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              int *status, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             atomicOr(status, DEV_ERR_WAIT_TIMEOUT);
             *abort_flag = 1;
             return false;
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status) {
+    return mbar_wait_for(bar, parity, abort_flag, status, kWaitLimitNs);
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,

@@ -47,7 +47,7 @@ EXPORTED = (
     "gkv_export_free_list", "gkv_page_refcount", "gkv_export_page", "gkv_device_status",
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
-    "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16",
+    "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16", "gkv_check_bounded_wait",
 )
 
 
@@ -115,6 +115,7 @@ def load_library(path: str = LIB_PATH):
         "gkv_conv_rollback": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
         "gkv_mtp_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
         "gkv_conv_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
+        "gkv_check_bounded_wait": (C.c_int, [i32, i64, i32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -522,6 +523,16 @@ def conv_rollback(m, proj, pre, out=None, stream=None):
     fn = L.gkv_conv_rollback_f16 if f16 else L.gkv_conv_rollback
     _check(fn(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out), _stream_ptr(stream)))
     return out
+
+
+def check_bounded_wait(device: int = 0, limit_ns: int = 50_000_000) -> int:
+    """``gkv_check_bounded_wait``: one device wait on a barrier nothing
+    arrives on; returns the status bits it left (1 = the wait ran out and
+    gave up, as designed)."""
+    L = load_library()
+    st = C.c_int32()
+    _check(L.gkv_check_bounded_wait(int(device), int(limit_ns), C.byref(st)))
+    return st.value
 
 
 def rope_table(n_rot: int, base: float, positions) -> tuple:

@@ -312,6 +312,15 @@ int gkv_export_page(gkv_pool *pool, int32_t page_id, void *k_host,
  * errors surface through Metal command buffers, MetalGolden.swift:384). */
 int gkv_device_status(gkv_pool *pool, int32_t *status);
 
+/* Failure-detection check (no reference counterpart): on `device`, one
+ * thread waits -- through the bounded wait every kernel of this library
+ * uses on its mbarriers -- on a barrier that nothing ever arrives on.  The
+ * wait gives up after limit_ns (1 ms .. 10 s), records the timeout and
+ * returns, so the context stays usable; *status receives the status bits
+ * (1 = a bounded wait ran out, the expected result).  Synchronizes the
+ * device. */
+int gkv_check_bounded_wait(int32_t device, int64_t limit_ns, int32_t *status);
+
 #ifdef __cplusplus
 }
 #endif
