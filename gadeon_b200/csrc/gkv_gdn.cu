@@ -178,6 +178,90 @@ __global__ void __launch_bounds__(256) conv_rollback_kernel(const __grid_constan
     }
 }
 
+// Vector form for conv_dim % 8 == 0, taps <= 4 and 16-byte aligned arrays:
+// thread = 8 consecutive channels of one item with all their taps, so its
+// slice of the [CD, taps] tail is 8*TAPS contiguous elements (a multiple of
+// 16 bytes for fp16 and fp32) moved with 16-byte loads and stores; the proj
+// row slices are two float4 loads per tap.  Same values as the scalar kernel.
+constexpr int kConvVecThreads = 128;
+
+// Element e of a slice kept as 32-bit words in registers (compile-time e):
+// fp32 one element per word, fp16 two (raw bits, so carried taps are copied
+// exactly).
+template <typename T>
+struct Words {
+    static constexpr int PER = 4 / (int)sizeof(T);
+    __device__ __forceinline__ static uint32_t get(const uint32_t *w, int e) {
+        return PER == 1 ? w[e] : (w[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+    }
+    __device__ __forceinline__ static void set(uint32_t *w, int e, uint32_t bits) {
+        if (PER == 1)
+            w[e] = bits;
+        else if (e & 1)
+            w[e >> 1] = (w[e >> 1] & 0x0000ffffu) | (bits << 16);
+        else
+            w[e >> 1] = (w[e >> 1] & 0xffff0000u) | bits;
+    }
+    __device__ __forceinline__ static uint32_t bits_of(float x) {
+        if (PER == 1) return __float_as_uint(x);
+        return (uint32_t)__half_as_ushort(__float2half_rn(x));
+    }
+};
+
+// One thread's slice for an accepted length m with KEEP = max(TAPS - m, 0)
+// carried taps: out tap t < KEEP is carried tap t + (TAPS - KEEP) = m + t of
+// pre; out tap t >= KEEP is projection row m - TAPS + t (>= 0).
+template <typename T, int TAPS, int KEEP>
+__device__ __forceinline__ void conv_slice(const ConvParams<T> &p, int item, int c0, int64_t tail, int m) {
+    using W = Words<T>;
+    constexpr int NW = 8 * TAPS / W::PER;
+    uint32_t pre[NW], out[NW];
+    if constexpr (KEEP > 0) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.pre + tail);
+#pragma unroll
+        for (int v = 0; v < NW / 4; ++v) {
+            const uint4 x = __ldcs(src + v);
+            pre[4 * v] = x.x, pre[4 * v + 1] = x.y, pre[4 * v + 2] = x.z, pre[4 * v + 3] = x.w;
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < NW; ++w) out[w] = 0u;
+#pragma unroll
+    for (int t = 0; t < TAPS; ++t) {
+        if (t < KEEP) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) W::set(out, c * TAPS + t, W::get(pre, c * TAPS + t + (TAPS - KEEP)));
+        } else {
+            const float4 *row =
+                reinterpret_cast<const float4 *>(p.proj + ((int64_t)item * p.C + (m - TAPS + t)) * p.CD + c0);
+            const float4 a = __ldcs(row), b = __ldcs(row + 1);
+            const float r[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int c = 0; c < 8; ++c) W::set(out, c * TAPS + t, W::bits_of(r[c]));
+        }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(p.out + tail);
+#pragma unroll
+    for (int v = 0; v < NW / 4; ++v) __stcs(dst + v, make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]));
+}
+
+template <typename T, int TAPS>
+__global__ void __launch_bounds__(kConvVecThreads) conv_rollback_vec_kernel(const __grid_constant__ ConvParams<T> p) {
+    static_assert((8 * TAPS / Words<T>::PER) % 4 == 0, "whole 16-byte vectors");
+    const int item = blockIdx.y;
+    const int c0 = (blockIdx.x * kConvVecThreads + threadIdx.x) * 8;
+    if (c0 >= p.CD) return;
+    const int m = p.m[item];
+    const int64_t tail = ((int64_t)item * p.CD + c0) * TAPS;
+    switch (m >= TAPS ? 0 : TAPS - m) {  // carried taps kept
+        case 0: conv_slice<T, TAPS, 0>(p, item, c0, tail, m); break;
+        case 1: if constexpr (TAPS > 1) conv_slice<T, TAPS, 1>(p, item, c0, tail, m); break;
+        case 2: if constexpr (TAPS > 2) conv_slice<T, TAPS, 2>(p, item, c0, tail, m); break;
+        case 3: if constexpr (TAPS > 3) conv_slice<T, TAPS, 3>(p, item, c0, tail, m); break;
+        default: break;
+    }
+}
+
 // Fast path for the verify widths MTP uses (C <= kFastC), DV a multiple of
 // COLS with DV <= COLS * kRollThreads, DK <= kFastDK: thread = one group cg
 // of COLS state columns and rows r0, r0 + rstride, ...; its delta_t[cg] for
@@ -449,6 +533,7 @@ int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int3
         return report_error(GKV_ERR_INVALID, "proj must be 4-byte aligned, pre/out %d-byte", (int)sizeof(T));
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
+    const bool vec = conv_dim % 8 == 0 && taps <= 4 && !misaligned(proj) && !misaligned(pre) && !misaligned(out);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     for (int32_t first = 0; first < n_items; first += kMaxItemsPerLaunch) {
         const int32_t cnt = n_items - first < kMaxItemsPerLaunch ? n_items - first : kMaxItemsPerLaunch;
@@ -460,8 +545,18 @@ int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int3
         p.pre = pre + (int64_t)first * conv_dim * taps;
         p.out = out + (int64_t)first * conv_dim * taps;
         for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
-        const dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)cnt);
-        conv_rollback_kernel<T><<<grid, 256, 0, st>>>(p);
+        if (vec) {
+            const dim3 vgrid((unsigned)((conv_dim / 8 + kConvVecThreads - 1) / kConvVecThreads), (unsigned)cnt);
+            switch (taps) {
+                case 1: conv_rollback_vec_kernel<T, 1><<<vgrid, kConvVecThreads, 0, st>>>(p); break;
+                case 2: conv_rollback_vec_kernel<T, 2><<<vgrid, kConvVecThreads, 0, st>>>(p); break;
+                case 3: conv_rollback_vec_kernel<T, 3><<<vgrid, kConvVecThreads, 0, st>>>(p); break;
+                default: conv_rollback_vec_kernel<T, 4><<<vgrid, kConvVecThreads, 0, st>>>(p); break;
+            }
+        } else {
+            const dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)cnt);
+            conv_rollback_kernel<T><<<grid, 256, 0, st>>>(p);
+        }
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "conv_rollback launch: %s", cudaGetErrorString(e));
     }

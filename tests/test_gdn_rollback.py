@@ -292,3 +292,24 @@ def test_gpu_conv_tail_f16_bit_exact(cuda, oracle):
     torch.cuda.synchronize()
     assert got.dtype == torch.float16
     assert np.array_equal(got.cpu().numpy().view(np.uint16), oracle.conv_rollback_f16(m, proj, pre).view(np.uint16))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("CD,taps", [(96, 1), (96, 2), (64, 4), (20, 3), (64, 5)])
+@pytest.mark.parametrize("f16", [False, True])
+def test_gpu_conv_tail_shapes(cuda, oracle, CD, taps, f16):
+    """Vector path (conv_dim % 8 == 0, taps <= 4) for every tap count, the
+    element-wise path otherwise; m from 1 to C covers all-carried, mixed and
+    all-projected tails.  Bit for bit with the oracle."""
+    import gadeon_b200 as gk
+    torch = cuda
+    rng = np.random.default_rng(CD * 10 + taps)
+    n, C = 300, 6
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float16 if f16 else np.float32)
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    got = gk.conv_rollback(m, _dev(torch, proj), _dev(torch, pre))
+    torch.cuda.synchronize()
+    want = oracle.conv_rollback_f16(m, proj, pre) if f16 else oracle.conv_rollback(m, proj, pre)
+    assert np.array_equal(got.cpu().numpy().view(np.uint16 if f16 else np.uint32),
+                          want.view(np.uint16 if f16 else np.uint32))
