@@ -342,11 +342,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
             uint8_t *sV = sK + C::TILE_BYTES;
             if constexpr (TMA) {
                 const int ngroups = (nkeys + (1 << lbh) - 1) >> lbh;
-                // fused decode append: the last tile of an item holds the new
-                // row (position len-1); its page id comes from the descriptor,
-                // since the table entry of a fresh page may be written by
-                // another CTA's prologue
-                const bool fuse_here = FUSED && w.j == w.e.ntiles - 1;
+                // fused append: a tile holding new rows (positions >= len -
+                // n_q) takes their pages' ids from the descriptor, since the
+                // table entry of a fresh page may be written by another CTA's
+                // prologue
+                const bool fuse_here = FUSED && t0 + TK > w.e.len - p.n_q;
                 FusedTail ft{};
                 if constexpr (FUSED) {
                     if (fuse_here) ft = tails[w.b];
@@ -355,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                 if (lane < ngroups) {  // table read before the wait hides its latency
                     const int tg = t0 + (lane << lbh);
                     int pid;
-                    if (fuse_here && (tg >> lP) == ft.pidx) pid = ft.pid;
+                    if (fuse_here && (tg >> lP) == ft.pidx[0]) pid = ft.pid[0];
+                    else if (fuse_here && (tg >> lP) == ft.pidx[1]) pid = ft.pid[1];
                     else pid = __ldg(trow + (tg >> lP));
                     if (pid < 0 || pid >= p.num_pages) {
                         atomicOr(p.status, DEV_ERR_BAD_PAGE);
@@ -365,8 +366,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                 }
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) break;
                 // the consumers store this CTA's new rows (and zero fresh
-                // pages) while the ring fills; only the tile holding a new
-                // row waits for those stores
+                // pages) while the ring fills; only a tile holding new rows
+                // waits for those stores
                 if (fuse_here && !mbar_wait(rows_done, 0, abort_flag, p.status)) break;
                 if (lane == 0)
                     mbar_expect_tx(&full[stage], (uint32_t)(ngroups << lbh) * DH * 2 * 2);
@@ -430,56 +431,65 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
     const int rq0 = min(lr, R - 1) / G, rq1 = min(lr + 8, R - 1) / G;
 
     if constexpr (FUSED) {
-        // Fused decode append, while the producer's first loads are in
-        // flight: for every item whose last key tile (it holds the new row,
-        // position len-1) this CTA owns, write that kv head's row -- and zero
-        // the rest of its slab when the page is fresh (PagePool.zeroPage) --
-        // then fence the stores against the TMA read of that tile.
+        // Fused append, while the producer's first loads are in flight: for
+        // every key tile of this CTA that holds new rows (positions len-n_q ..
+        // len-1, the last one or two tiles of an item), write that kv head's
+        // rows; for a fresh page whose first row lies in the tile, zero its
+        // rows past the sequence end (PagePool.zeroPage) and record its
+        // table entry.  Each row has exactly one writer.  Then fence the
+        // stores against the TMA reads of those tiles.
         UnitWalker a = w;
         int u = u_begin, n_own = 0;
         while (u < u_end) {
-            const int item_last = a.e.unit_base + a.kvh * a.e.ntiles + a.e.ntiles - 1;
-            if (item_last < u_end) {
-                const FusedTail ft = tails[a.b];
-                const int slot = (a.e.len - 1) & (p.P - 1);
-                const int64_t slab = ((int64_t)ft.pid * KVH + a.kvh) * p.P * DH;
-                uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
-                uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
-                const int rows = ft.fresh ? p.P : 1;
-                if constexpr (PROD) {
-                    // every other row of a fresh page is zeroed by all
-                    // threads; one warp builds the new K/V row from the raw
-                    // projections (items round-robin over the warps)
-                    if (ft.fresh)
-                        for (int i = tid; i < rows * C::CH; i += 128)
-                            if (i / C::CH != slot) {
-                                kd[i] = make_uint4(0u, 0u, 0u, 0u);
-                                vd[i] = make_uint4(0u, 0u, 0u, 0u);
-                            }
-                    if (warp == n_own % kConsumerWarps) {
-                        const int64_t row = (int64_t)a.b * KVH + a.kvh;
-                        const int64_t tok = (int64_t)a.b * p.n_q + p.n_q - 1;  // the new row's token
-                        const int hr = p.prod.n_rot >> 1;
-                        float kv[DH / 32];
-                        produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps,
-                                        p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr, p.prod.n_rot, lane,
-                                        kv);
-                        store_row_f16<DH>(p.k_pool_w + slab + (int64_t)slot * DH, lane, kv);
-                        copy_row_f16<DH>(p.v_pool_w + slab + (int64_t)slot * DH, p.prod.v_raw + row * DH, lane);
+            const int item_first = a.e.unit_base + a.kvh * a.e.ntiles;
+            const int item_last = item_first + a.e.ntiles - 1;
+            const int len = a.e.len, p0 = len - p.n_q;  // first new position
+            const FusedTail ft = tails[a.b];
+            for (int jj = p0 / TK; jj <= (len - 1) / TK; ++jj) {
+                if (item_first + jj < u_begin || item_first + jj >= u_end) continue;  // another CTA's tile
+                const int t_lo = max(p0, jj * TK), t_hi = min(len, jj * TK + TK);   // new rows here
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                    if (ft.pidx[s] < 0) continue;
+                    const int pg = ft.pidx[s] * p.P;  // the page's first position
+                    const int64_t slab = ((int64_t)ft.pid[s] * KVH + a.kvh) * p.P * DH;
+                    uint4 *kd = reinterpret_cast<uint4 *>(p.k_pool_w + slab);
+                    uint4 *vd = reinterpret_cast<uint4 *>(p.v_pool_w + slab);
+                    const int r_lo = max(t_lo, pg), r_hi = min(t_hi, pg + p.P);
+                    if constexpr (PROD) {
+                        // one warp builds each new K/V row from the raw
+                        // projections (rows round-robin over the warps)
+                        for (int pos = r_lo; pos < r_hi; ++pos, ++n_own) {
+                            if (warp != n_own % kConsumerWarps) continue;
+                            const int r = pos - p0;
+                            const int64_t tok = (int64_t)a.b * p.n_q + r;
+                            const int64_t row = tok * KVH + a.kvh;
+                            const int hr = p.prod.n_rot >> 1;
+                            float kv[DH / 32];
+                            produce_row<DH>(p.prod.k_raw + row * DH, p.prod.k_norm, p.prod.eps,
+                                            p.prod.rope_cos + tok * hr, p.prod.rope_sin + tok * hr, p.prod.n_rot,
+                                            lane, kv);
+                            store_row_f16<DH>(p.k_pool_w + slab + (int64_t)(pos - pg) * DH, lane, kv);
+                            copy_row_f16<DH>(p.v_pool_w + slab + (int64_t)(pos - pg) * DH, p.prod.v_raw + row * DH,
+                                             lane);
+                        }
+                    } else {
+                        for (int i = tid; i < (r_hi - r_lo) * C::CH; i += 128) {
+                            const int pos = r_lo + i / C::CH, c = i % C::CH;
+                            const int64_t src = (((int64_t)a.b * p.n_q + (pos - p0)) * KVH + a.kvh) * C::CH + c;
+                            kd[(pos - pg) * C::CH + c] = reinterpret_cast<const uint4 *>(p.k_new)[src];
+                            vd[(pos - pg) * C::CH + c] = reinterpret_cast<const uint4 *>(p.v_new)[src];
+                        }
                     }
-                    ++n_own;
-                } else {
-                    const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_new + ((int64_t)a.b * KVH + a.kvh) * DH);
-                    const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_new + ((int64_t)a.b * KVH + a.kvh) * DH);
-                    for (int i = tid; i < rows * C::CH; i += 128) {
-                        const int row = ft.fresh ? i / C::CH : slot, c = i % C::CH;
-                        const bool mine = row == slot;
-                        kd[row * C::CH + c] = mine ? ks[c] : make_uint4(0u, 0u, 0u, 0u);
-                        vd[row * C::CH + c] = mine ? vs[c] : make_uint4(0u, 0u, 0u, 0u);
+                    if (ft.fresh[s] && pg >= jj * TK && pg < jj * TK + TK) {
+                        for (int i = tid; i < (pg + p.P - len) * C::CH; i += 128) {  // rows past the end
+                            kd[(len - pg) * C::CH + i] = make_uint4(0u, 0u, 0u, 0u);
+                            vd[(len - pg) * C::CH + i] = make_uint4(0u, 0u, 0u, 0u);
+                        }
+                        if (a.kvh == 0 && tid == 0)
+                            p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx[s]] = ft.pid[s];
                     }
                 }
-                if (ft.fresh && a.kvh == 0 && tid == 0)
-                    p.table_w[(int64_t)a.e.seq_id * p.table_stride + ft.pidx] = ft.pid;
             }
             // next item
             u = item_last + 1;

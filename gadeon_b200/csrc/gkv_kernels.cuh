@@ -69,12 +69,14 @@ struct AttendEntry {
     int32_t ntiles;     // key tiles per kv head = ceil(len / TK)
 };
 
-// Fused decode append: where sequence b's new row (position len-1) goes.
+// Fused append: the pages sequence b's n_q new rows (positions len-n_q ..
+// len-1, n_q <= P) land on, in position order -- at most two: the partly
+// filled tail page and one fresh page.
 struct FusedTail {
-    int32_t pid;   // physical page holding position len-1
-    int32_t pidx;  // its logical index in the sequence
-    int32_t fresh; // 1: the page was just allocated (zero-fill + table entry)
-    int32_t pad;
+    int32_t pid[2];    // physical pages
+    int32_t pidx[2];   // their logical indices in the sequence; pidx[1] < 0: one page
+    int32_t fresh[2];  // 1: just allocated (zero-filled, table entry written here)
+    int32_t pad[2];
 };
 
 // Producer fusion (gkv_attn_step; q_gate == nullptr turns it off): the
@@ -106,9 +108,9 @@ struct AttendParams {
     const AttendEntry *entries;  // null: InlineDesc::entries
     int32_t n_seqs;
     int32_t total_units;
-    // fused decode append (fused = 1): k_new/v_new [n_seqs, KVH, dh] fp16,
-    // written into the pool before the last key tile of each (sequence, kv
-    // head) is loaded; tails (null: InlineDesc::tails) say where
+    // fused append (fused = 1): k_new/v_new [n_seqs * n_q, KVH, dh] fp16, the
+    // n_q new rows of every sequence, written into the pool before the key
+    // tiles holding them are loaded; tails (null: InlineDesc::tails) say where
     int32_t fused;
     const FusedTail *tails;
     const uint16_t *k_new, *v_new;

@@ -287,6 +287,26 @@ int plan_append(gkv_pool *pool, int32_t n, const int32_t *ids, const int32_t *n_
     return GKV_OK;
 }
 
+// The fused append's pages per sequence, in position order: true when every
+// sequence's new rows land on one or two pages none of which is a shared
+// (copy-on-write) tail -- the rows can then ride in the attend kernel.
+bool fused_tails(const std::vector<gkv::TouchedPage> &pages, int32_t n_seqs, std::vector<gkv::FusedTail> &tails) {
+    tails.assign(n_seqs, gkv::FusedTail{{-1, -1}, {-1, -1}, {0, 0}, {0, 0}});
+    std::vector<int> cnt(n_seqs, 0);
+    for (const gkv::TouchedPage &tp : pages) {
+        if (tp.src_pid >= 0) return false;
+        int &c = cnt[tp.entry];
+        if (c == 2) return false;
+        tails[tp.entry].pid[c] = tp.pid;
+        tails[tp.entry].pidx[c] = tp.pidx;
+        tails[tp.entry].fresh[c] = tp.src_pid == gkv::PAGE_NEW ? 1 : 0;
+        ++c;
+    }
+    for (int32_t i = 0; i < n_seqs; ++i)
+        if (cnt[i] == 0) return false;
+    return true;
+}
+
 // Uploads entries+pages and launches the append kernel.
 int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
                    const std::vector<gkv::TouchedPage> &pages, const void *k, const void *v,
@@ -809,19 +829,13 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // Single-token decode with TMA-staged pages and no shared tail page: the
-    // append rides inside the attend kernel (one launch per layer).  Each
-    // sequence then touched exactly one page, in batch order.
-    bool fuse = n_q == 1 && pool->cfg.page_tokens >= 8 &&
-                (pool->cfg.head_dim == 128 || pool->cfg.head_dim == 256) && (int32_t)pages.size() == n_seqs;
-    for (size_t i = 0; fuse && i < pages.size(); ++i)
-        fuse = pages[i].entry == (int32_t)i && pages[i].src_pid < 0;
-    if (fuse) {
-        std::vector<gkv::FusedTail> tails(n_seqs);
-        for (int32_t i = 0; i < n_seqs; ++i)
-            tails[i] = {pages[i].pid, pages[i].pidx, pages[i].src_pid == gkv::PAGE_NEW ? 1 : 0, 0};
-        return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st, tails.data(), k, v);
-    }
+    // Decode and verify steps of the split-K kernel (n_q*group <= 16, n_q <=
+    // P) with TMA-staged pages and no shared tail page: the append rides
+    // inside the attend kernel (one launch per layer).
+    std::vector<gkv::FusedTail> tails;
+    const bool fuse = (int64_t)n_q * group <= 16 && n_q <= pool->cfg.page_tokens && pool->cfg.page_tokens >= 8 &&
+                      (pool->cfg.head_dim == 128 || pool->cfg.head_dim == 256) && fused_tails(pages, n_seqs, tails);
+    if (fuse) return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st, tails.data(), k, v);
     rc = enqueue_append(pool, entries, pages, k, v, 0, st);
     if (rc) return rc;
     return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st);
@@ -861,12 +875,8 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     gkv::ProducerArgs prod{q_gate, k_raw, v_raw, q_norm, k_norm, rope_cos, rope_sin, n_rot, eps};
     // Same fusion rule as gkv_append_attend: TMA-staged pages and no shared
     // tail page -> the attend kernel's prologue builds and writes the rows.
-    bool fuse = pool->cfg.page_tokens >= 8 && (int32_t)pages.size() == n_seqs;
-    for (size_t i = 0; fuse && i < pages.size(); ++i) fuse = pages[i].entry == (int32_t)i && pages[i].src_pid < 0;
-    if (fuse) {
-        std::vector<gkv::FusedTail> tails(n_seqs);
-        for (int32_t i = 0; i < n_seqs; ++i)
-            tails[i] = {pages[i].pid, pages[i].pidx, pages[i].src_pid == gkv::PAGE_NEW ? 1 : 0, 0};
+    std::vector<gkv::FusedTail> tails;
+    if (pool->cfg.page_tokens >= 8 && fused_tails(pages, n_seqs, tails)) {
         return enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, st, tails.data(), nullptr,
                               nullptr, &prod);
     }

@@ -79,3 +79,36 @@ def test_descriptor_inline_and_uploaded(cuda, oracle, n_seqs):
     got, want = pr.attend(ids, 4, G)
     assert_attn_close(got, want, f"verify n={n_seqs}")
     pr.check_state()
+
+
+@pytest.mark.parametrize("P,dh,n_q,G", [(8, 256, 4, 4), (8, 128, 8, 2), (16, 256, 4, 4), (16, 128, 16, 1),
+                                        (64, 256, 3, 4), (128, 128, 5, 2)])
+def test_fused_verify_append(cuda, oracle, P, dh, n_q, G):
+    """gkv_append_attend with n_q > 1 on the split-K kernel writes the n_q
+    draft rows inside the attend launch: rows straddling a page boundary, a
+    fresh page starting among them, pages larger than the key tile, and a
+    cloned (shared) tail that takes the two-kernel path.  Tables, free list
+    and page bytes bit-exact; outputs within tolerance of the causal verify
+    restatement (Engine.swift:2620-2646)."""
+    torch = cuda
+    pr = Pair(cuda, oracle, kvh=2, dh=dh, P=P, num_pages=900, seed=61)
+    ctx = [1, P - 2, P - 1, P, 2 * P + 1, 300]
+    ids = [pr.new_seq() for _ in ctx]
+    pr.append(ids, ctx)
+    for step in range(6):
+        if step == 2:  # share a partial tail: this step appends through the unfused path
+            c = pr.gpu.clone(ids[4])
+            assert pr.orc.clone(ids[4]) == c
+            pr.seqs.append(c)
+            ids.append(c)
+        k, v = pr.rows(len(ids) * n_q)
+        q = oracle.normal_f16(71, step, (len(ids), n_q, 2 * G, dh))
+        got = pr.gpu.append_attend(ids, n_q, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+        assert pr.orc.append(ids, [n_q] * len(ids), k, v) == 0
+        want = pr.orc.attend_causal(ids, n_q, q, G, dh ** -0.5)
+        assert_attn_close(got.cpu().numpy(), want, f"fused verify step {step}")
+        pr.check_state()
+        # the rejected drafts go (Engine.decodeSpecStep's truncate)
+        keep = [pr.gpu.length(s) - (step + s) % (n_q + 1) for s in ids]
+        pr.truncate(ids, keep)
+        pr.check_state(pages=False)

@@ -21,8 +21,8 @@ from test_gpu_parity import Pair, dev_f16
 
 pytestmark = pytest.mark.gpu
 
-OPS = ["new", "append", "decode", "verify", "chunk", "truncate", "clone", "release", "rewind"]
-WEIGHTS = np.array([1.0, 3.0, 4.0, 1.5, 0.5, 2.0, 1.0, 0.7, 1.0])
+OPS = ["new", "append", "decode", "verify", "chunk", "truncate", "clone", "release", "rewind", "fverify"]
+WEIGHTS = np.array([1.0, 3.0, 4.0, 1.5, 0.5, 2.0, 1.0, 0.7, 1.0, 1.5])
 
 
 @pytest.mark.parametrize("seed,P,dh,num_pages,grow", [(11, 8, 128, 260, 3), (12, 16, 256, 200, 3), (13, 16, 128, 120, 3),
@@ -84,6 +84,23 @@ def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow):
             assert pr.orc.append(ids, [1] * len(ids), k, v) == 0
             want = pr.orc.attend_causal(ids, 1, q, G, dh ** -0.5, n_threads=8)
             assert_attn_close(got.cpu().numpy(), want, f"step {step} decode")
+        elif op == "fverify":
+            # drafts appended and verified in one call (fused into the attend
+            # launch unless a tail page is shared)
+            ids = subset(4)
+            n_q = int(rng.integers(2, 9))
+            k, v = pr.rows(len(ids) * n_q)
+            q = oracle.normal_f16(seed, 5000 + step, (len(ids), n_q, kvh * G, dh))
+            try:
+                got = pr.gpu.append_attend(ids, n_q, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+            except GkvError as e:
+                assert e.code == GKV_ERR_NO_PAGES, e
+                assert pr.orc.append(ids, [n_q] * len(ids), k, v) != 0
+                refused += 1
+                continue
+            assert pr.orc.append(ids, [n_q] * len(ids), k, v) == 0
+            want = pr.orc.attend_causal(ids, n_q, q, G, dh ** -0.5, n_threads=8)
+            assert_attn_close(got.cpu().numpy(), want, f"step {step} fused verify n_q={n_q}")
         elif op in ("verify", "chunk"):
             n_q = int(rng.integers(2, 9)) if op == "verify" else int(rng.integers(9, 48))
             ids = [s for s in live if pr.gpu.length(s) >= n_q]
