@@ -370,7 +370,7 @@ def run_ours(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        per_key, desc, cpu_s = cpu_sample(args.seed + 7, 16, 6, 1, cfg, ctx)
+        per_key, desc, cpu_s = cpu_sample(args.seed + 7, 32, 15, 1, cfg, ctx)  # ~10 s of one core
         job_keys = float(ctx.sum()) * L
         cpu_step = per_key * job_keys
         cpu = {"value": S / cpu_step, "unit": UNIT, "cores": 1, "kind": "port",
