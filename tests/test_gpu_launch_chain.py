@@ -59,7 +59,8 @@ def test_back_to_back_fused_steps_two_pools(cuda, oracle):
 @pytest.mark.parametrize("n_seqs", [128, 129, 200])
 def test_descriptor_inline_and_uploaded(cuda, oracle, n_seqs):
     """Around the 128-sequence inline limit: plain decode attend, fused
-    append + attend and MTP verify (4 drafts x G=4 rows) all match."""
+    decode append + attend and fused MTP verify (4 drafts x G=4 rows) all
+    match."""
     torch = cuda
     G, dh, P, kvh = 4, 128, 16, 2
     pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=n_seqs * 8, max_seqs=n_seqs, seed=5)
@@ -75,9 +76,14 @@ def test_descriptor_inline_and_uploaded(cuda, oracle, n_seqs):
     assert pr.orc.append(ids, [1] * n_seqs, k, v) == 0
     want = pr.orc.attend_causal(ids, 1, q, G, dh ** -0.5)
     assert_attn_close(got.cpu().numpy(), want, f"fused n={n_seqs}")
-    pr.append(ids, [4] * n_seqs)
-    got, want = pr.attend(ids, 4, G)
-    assert_attn_close(got, want, f"verify n={n_seqs}")
+    # verify rows appended in the same call (fused: the two-page tails travel
+    # inline up to 128 sequences, uploaded beyond)
+    k, v = pr.rows(n_seqs * 4)
+    q = oracle.normal_f16(32, n_seqs, (n_seqs, 4, kvh * G, dh))
+    got = pr.gpu.append_attend(ids, 4, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+    assert pr.orc.append(ids, [4] * n_seqs, k, v) == 0
+    want = pr.orc.attend_causal(ids, 4, q, G, dh ** -0.5)
+    assert_attn_close(got.cpu().numpy(), want, f"fused verify n={n_seqs}")
     pr.check_state()
 
 
