@@ -380,15 +380,22 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 for (int c = 0; c < TT; ++c)
                     if (t0 + c > lim) s[c] = -INFINITY * sgn;
             }
-            // extreme of the raw scores (max for scale > 0), 8 chains
-            float ex[8];
+            // extreme of the raw scores, 8 chains: the max for scale >= 0 (no
+            // sign products in the usual case), the min for a negative scale
+            float ex[8], ext;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) ex[u] = s[u] * sgn;
+            for (int u = 0; u < 8; ++u) ex[u] = s[u];
+            if (sl >= 0.f) {
 #pragma unroll
-            for (int c = 8; c < TT; ++c) ex[c & 7] = fmaxf(ex[c & 7], s[c] * sgn);
-            const float e01 = fmaxf(ex[0], ex[1]), e23 = fmaxf(ex[2], ex[3]);
-            const float e45 = fmaxf(ex[4], ex[5]), e67 = fmaxf(ex[6], ex[7]);
-            const float ext = fmaxf(fmaxf(e01, e23), fmaxf(e45, e67)) * sgn;
+                for (int c = 8; c < TT; ++c) ex[c & 7] = fmaxf(ex[c & 7], s[c]);
+                ext = fmaxf(fmaxf(fmaxf(ex[0], ex[1]), fmaxf(ex[2], ex[3])),
+                            fmaxf(fmaxf(ex[4], ex[5]), fmaxf(ex[6], ex[7])));
+            } else {
+#pragma unroll
+                for (int c = 8; c < TT; ++c) ex[c & 7] = fminf(ex[c & 7], s[c]);
+                ext = fminf(fminf(fminf(ex[0], ex[1]), fminf(ex[2], ex[3])),
+                            fminf(fminf(ex[4], ex[5]), fminf(ex[6], ex[7])));
+            }
             const float mt = ext == -INFINITY * sgn ? -INFINITY : ext * sl;
             const float m_new = fmaxf(m_ref, mt);
             const bool raise = m_new > m_ref + 8.f;  // lazy: keep m_ref unless it grew by > 2^8
@@ -419,23 +426,26 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 }
             }
             uint8_t *sP = smem + C::OFF_P;
-            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            // packed fp32x2 FMA / add (each lane rounded as fmaf / + would)
+            float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+            const float2 sl2 = make_float2(sl, sl), nmu2 = make_float2(nmu, nmu);
 #pragma unroll
             for (int ch = 0; ch < TT / 8; ++ch) {  // 16-byte chunks of 8 keys
                 uint32_t w4[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const float a0 = fast_exp2(fmaf(s[ch * 8 + 2 * u], sl, nmu));
-                    const float a1 = fast_exp2(fmaf(s[ch * 8 + 2 * u + 1], sl, nmu));
-                    ps[(2 * u) & 7] += a0;
-                    ps[(2 * u + 1) & 7] += a1;
+                    const float2 x = __ffma2_rn(make_float2(s[ch * 8 + 2 * u], s[ch * 8 + 2 * u + 1]), sl2, nmu2);
+                    const float a0 = fast_exp2(x.x), a1 = fast_exp2(x.y);
+                    ps2[u] = __fadd2_rn(ps2[u], make_float2(a0, a1));
                     w4[u] = pack_half2(a0, a1);
                 }
                 // P atom (ch / 8) holds keys 64*(ch/8) .. +63 of all rows
                 *reinterpret_cast<uint4 *>(sP + (ch >> 3) * M * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) =
                     make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            l = l * factor + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+            l = l * factor + (((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
+                              ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y)));
             const int nkeys = min(TT, kend - t0);
             if (j == nt - 1 && (PAIR || nkeys < TT)) {
                 // last tile: once this CTA's part of V landed, zero its rows
