@@ -467,8 +467,11 @@ def host_flash_decode(q, pool: PagePool, G: int, stream=None):
     """``hostFlashDecode(q:pool:G:)`` (PagedAttention.swift:317-366) on the GPU:
     q [kv_heads, G, head_dim] fp16 -> [kv_heads*G*head_dim] fp32, the newest
     query attending every one of the pool's ``length`` keys with
-    scale = head_dim^-0.5."""
+    scale = head_dim^-0.5.  An empty pool gives zeros, as the Swift (:323)."""
     bp = pool.block_pool
+    if pool.length == 0:
+        import torch
+        return torch.zeros(bp.kv_heads * G * bp.head_dim, dtype=torch.float32, device=q.device)
     qq = q.reshape(1, 1, bp.kv_heads * G, bp.head_dim)
     out = bp.attend([pool.seq_id], 1, G, qq, scale=bp.head_dim ** -0.5, stream=stream)
     return out.reshape(-1)

@@ -1,0 +1,51 @@
+"""The header-only C++ layer (include/gadeon_kv.hpp, the Swift PagePool /
+hostFlashDecode interface of LLM/src/CoreML/PagedAttention.swift:21-366 over
+the C ABI).  CPU: the header compiles under -Wall -Wextra -Werror at C++11
+and C++17, and tests/cpp/test_pagepool.cpp builds and links against the
+product library and the oracle.  GPU: that program runs its oracle-checked
+scenario (state bit-exact, attention within the path's tolerance, the
+throwing paths) and must exit 0."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+INC = ["-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA, "include")]
+WARN = ["-Wall", "-Wextra", "-Werror"]
+
+
+@pytest.mark.parametrize("std", ["c++11", "c++17"])
+def test_header_compiles(std):
+    src = '#include "gadeon_kv.hpp"\nint main() { return gadeon::check(GKV_OK), 0; }\n'
+    r = subprocess.run(["g++", f"-std={std}", *WARN, *INC, "-x", "c++", "-", "-fsyntax-only"],
+                       input=src, text=True, capture_output=True)
+    assert r.returncode == 0, r.stderr
+
+
+def build_test_program(out_dir):
+    from gadeon_b200 import build
+    build.build()
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle")], check=True)
+    exe = os.path.join(out_dir, "test_pagepool")
+    libdirs = [os.path.join(ROOT, "gadeon_b200"), os.path.join(ROOT, "oracle"), os.path.join(CUDA, "lib64")]
+    cmd = ["g++", "-std=c++17", "-O1", *WARN, *INC, os.path.join(ROOT, "tests", "cpp", "test_pagepool.cpp"),
+           "-o", exe, "-L", libdirs[0], "-lgadeonkv", "-L", libdirs[1], "-loracle", "-L", libdirs[2], "-lcudart",
+           "-Wl,-rpath," + ":".join(libdirs)]
+    r = subprocess.run(cmd, text=True, capture_output=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_program_builds(tmp_path):
+    exe = build_test_program(str(tmp_path))
+    assert os.access(exe, os.X_OK)
+
+
+@pytest.mark.gpu
+def test_program_passes_on_gpu(tmp_path):
+    exe = build_test_program(str(tmp_path))
+    r = subprocess.run([exe], text=True, capture_output=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "all checks passed" in r.stdout

@@ -318,3 +318,52 @@ def test_anti_vacuity_table_matters(cuda, oracle):
     want = pr.orc.attend_causal([a, b], 1, qq, 4, 256 ** -0.5)
     assert_attn_close(got, want, "anti-vacuity")
     assert np.abs(got[0] - got[1]).max() > 1e-2
+
+
+def test_pagepool_view_and_host_flash_decode(cuda, oracle):
+    """The per-sequence PagePool view (PagedAttention.swift:21-287) and
+    host_flash_decode (:317-366) driven like the Swift: an empty pool decodes
+    to zeros (:323), then seed / append / clone / truncate, each followed by
+    a decode against the oracle's hostFlashDecode restatement."""
+    from gadeon_b200 import PagePool, host_flash_decode
+    torch = cuda
+    kvh, dh, P, G = 2, 256, 8, 4
+    pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=64, seed=77)
+
+    def decode(pool, oseq, stream):
+        q = oracle.normal_f16(55, stream, (kvh, G, dh))
+        got = host_flash_decode(dev_f16(torch, q), pool, G).cpu().numpy()
+        want = pr.orc.flash_decode(oseq, q, G, dh ** -0.5).reshape(-1)
+        assert_attn_close(got, want, f"host_flash_decode at length {pool.length}")
+
+    a = PagePool(pr.gpu)
+    assert a.seq_id == pr.orc.seq_create()
+    assert (a.P, a.kv_heads, a.dh) == (P, kvh, dh)
+    zero = host_flash_decode(dev_f16(torch, oracle.normal_f16(55, 0, (kvh, G, dh))), a, G)
+    assert zero.shape == (kvh * G * dh,) and not bool(zero.any())
+    K = oracle.normal_f16(3, 1, (kvh, 13, dh))
+    V = oracle.normal_f16(3, 2, (kvh, 13, dh))
+    a.seed(dev_f16(torch, K), dev_f16(torch, V), 13)
+    assert pr.orc.seed(a.seq_id, K, V, 13) == 0
+    decode(a, a.seq_id, 1)
+    for t in range(5):  # 13 -> 18: across the page boundary at 16
+        k, v = pr.rows(1)
+        a.append(dev_f16(torch, k[0]), dev_f16(torch, v[0]))
+        assert pr.orc.append([a.seq_id], [1], k, v) == 0
+        decode(a, a.seq_id, 2 + t)
+    assert a.length == 18 and a.page_count == 3
+    b = a.clone()
+    assert b.seq_id == pr.orc.clone(a.seq_id)
+    a.truncate(9)
+    pr.orc.truncate([a.seq_id], [9])
+    pr.seqs += [a.seq_id, b.seq_id]
+    pr.check_state()
+    decode(a, a.seq_id, 10)
+    decode(b, b.seq_id, 11)
+    K2, V2 = b.compact()
+    c = PagePool.from_compact(pr.gpu, K2, V2, b.length)
+    oK, oV = pr.orc.compact(b.seq_id)
+    assert c.seq_id == pr.orc.from_compact(oK, oV, b.length)
+    pr.seqs.append(c.seq_id)
+    pr.check_state()
+    decode(c, c.seq_id, 12)
