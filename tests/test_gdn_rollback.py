@@ -313,3 +313,54 @@ def test_gpu_conv_tail_shapes(cuda, oracle, CD, taps, f16):
     want = oracle.conv_rollback_f16(m, proj, pre) if f16 else oracle.conv_rollback(m, proj, pre)
     assert np.array_equal(got.cpu().numpy().view(np.uint16 if f16 else np.uint32),
                           want.view(np.uint16 if f16 else np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("in_place", [False, True])
+def test_gpu_f16_many_heads(cuda, oracle, in_place):
+    """fp16 state, 128 x 128 heads at C = 5 over a batch of 5,120 heads (far
+    more CTAs than fit on the GPU at once), with and without out == s0:
+    equal bit for bit to the fp32-storage path rounded once; a slice of the
+    items against the oracle."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n, H, DK, DV, C = 160, 32, 128, 128, 5   # 5,120 heads
+    rng = np.random.default_rng(11 + in_place)
+    m = rng.integers(1, C + 1, n).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(77, n, H, DK, DV, C, m)
+    s16 = s0.astype(np.float16)
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    ref32 = gk.mtp_rollback(m, _dev(torch, s16.astype(np.float32)), *dev).cpu().numpy().astype(np.float16)
+    d16 = _dev(torch, s16)
+    got = gk.mtp_rollback(m, d16, *dev, out=d16 if in_place else None)
+    torch.cuda.synchronize()
+    if in_place:
+        assert got.data_ptr() == d16.data_ptr()
+    got = got.cpu().numpy()
+    assert np.array_equal(got.view(np.uint16), ref32.view(np.uint16))
+    sl = slice(0, 4)
+    want = oracle.mtp_rollback_f16(m[sl], s16[sl], delta[sl], k[sl], gcum[sl]).astype(np.float64)
+    diff = np.abs(got[sl].astype(np.float64) - want)
+    assert np.all(diff <= 2 * half_ulp_f16(np.maximum(np.abs(got[sl]), np.abs(want)))), diff.max()
+
+
+@pytest.mark.gpu
+def test_gpu_f16_unaligned_state_takes_the_elementwise_kernel(cuda, oracle):
+    """A state array 8 bytes off a 16-byte boundary cannot be moved in
+    16-byte columns: the call falls back to the element-wise kernel, same
+    bits."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n, H, DK, DV, C = 6, 4, 128, 128, 5
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(78, n, H, DK, DV, C, m)
+    s16 = s0.astype(np.float16)
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    flat = torch.zeros(s16.size + 4, dtype=torch.float16, device="cuda")
+    flat[4:] = _dev(torch, s16).reshape(-1)
+    odd = flat[4:].view(s16.shape)
+    assert odd.data_ptr() % 16 == 8
+    got = gk.mtp_rollback(m, odd, *dev)
+    aligned = gk.mtp_rollback(m, _dev(torch, s16), *dev)
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy().view(np.uint16), aligned.cpu().numpy().view(np.uint16))
