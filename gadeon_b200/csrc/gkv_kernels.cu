@@ -13,8 +13,8 @@
 //                   verify loop (LLM/src/CoreML/Engine.swift:2620-2646) and
 //                   Metal attn_head / attn_batch
 //                   (Kernels.metal:1339-1439, :1767-1793).
-//   compact_kernel  page-strided -> [KVH, len, dh] (PagePool.compact,
-//                   PagedAttention.swift:225-252).
+//   compact_kernel  page-strided window -> [KVH, rows, dh] (PagePool.compact,
+//                   PagedAttention.swift:225-252, and tileAt, :151-161).
 //
 // attend_kernel design (B200):
 //   * work unit = one TK-key tile of one (sequence, kv head); units are laid
@@ -100,21 +100,26 @@ __global__ void __launch_bounds__(256)
 // ------------------------------------------------------------ compact
 __global__ void __launch_bounds__(256) compact_kernel(const CompactParams p) {
     const int CH = p.dh >> 3;
-    const int64_t total = 2ll * p.kvh * p.len * CH;
+    const int64_t total = 2ll * p.kvh * p.rows * CH;
     const int64_t page_elems = (int64_t)p.kvh * p.P * p.dh;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % CH);
         int64_t rest = i / CH;
-        const int64_t t = rest % p.len;
-        rest /= p.len;
+        const int64_t r = rest % p.rows;
+        rest /= p.rows;
         const int h = (int)(rest % p.kvh);
         const int kv = (int)(rest / p.kvh);
-        const int32_t pid = p.table[t / p.P];
-        const uint16_t *src = (kv ? p.v_pool : p.k_pool) + pid * page_elems +
-                              ((int64_t)h * p.P + t % p.P) * p.dh;
-        uint16_t *dst = (kv ? p.V : p.K) + ((int64_t)h * p.len + t) * p.dh;
-        reinterpret_cast<uint4 *>(dst)[c] = reinterpret_cast<const uint4 *>(src)[c];
+        uint16_t *dst = (kv ? p.V : p.K) + ((int64_t)h * p.rows + r) * p.dh;
+        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+        if (r < p.count) {
+            const int64_t t = p.start + r;
+            const int32_t pid = p.table[t / p.P];
+            const uint16_t *src = (kv ? p.v_pool : p.k_pool) + pid * page_elems +
+                                  ((int64_t)h * p.P + t % p.P) * p.dh;
+            x = reinterpret_cast<const uint4 *>(src)[c];
+        }
+        reinterpret_cast<uint4 *>(dst)[c] = x;
     }
 }
 
@@ -868,8 +873,8 @@ cudaError_t launch_append(const AppendParams &p, cudaStream_t s, const AppendInl
 }
 
 cudaError_t launch_compact(const CompactParams &p, cudaStream_t s) {
-    if (p.len <= 0) return cudaSuccess;
-    const int64_t total = 2ll * p.kvh * p.len * (p.dh / 8);
+    if (p.rows <= 0) return cudaSuccess;
+    const int64_t total = 2ll * p.kvh * p.rows * (p.dh / 8);
     const int64_t blocks = (total + 255) / 256;
     compact_kernel<<<(unsigned)(blocks < 65535 * 16 ? blocks : 65535 * 16), 256, 0, s>>>(p);
     return cudaGetLastError();

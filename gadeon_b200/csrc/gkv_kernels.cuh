@@ -180,11 +180,14 @@ bool chunk_supported(int dh, int P, int G);
 cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tmap_k,
                          const CUtensorMap *tmap_v, int dh, cudaStream_t s);
 
+// A window of a sequence into head-major [KVH, rows, dh]: output row r < count
+// is position start + r, rows count..rows-1 are zero.  compact() is the
+// window (0, len, len); tileAt() is (start, count, tile_p).
 struct CompactParams {
     const int32_t *table;  // row of the sequence
     const uint16_t *k_pool, *v_pool;
-    uint16_t *K, *V;       // [KVH, len, dh]
-    int64_t len;
+    uint16_t *K, *V;       // [KVH, rows, dh]
+    int64_t start, count, rows;
     int32_t kvh, dh, P;
 };
 cudaError_t launch_compact(const CompactParams &p, cudaStream_t s);

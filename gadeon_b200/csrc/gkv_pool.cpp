@@ -1045,11 +1045,44 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stre
     p.v_pool = pool->d_v;
     p.K = static_cast<uint16_t *>(K);
     p.V = static_cast<uint16_t *>(V);
-    p.len = s->len;
+    p.start = 0;
+    p.count = p.rows = s->len;
     p.kvh = pool->cfg.kv_heads;
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
     GKV_CUDA(gkv::launch_compact(p, static_cast<cudaStream_t>(stream)), "compact kernel launch");
+    return GKV_OK;
+}
+
+int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, int32_t tile_p, void *K, void *V,
+                void *stream) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    const Seq *s = pool->seq(seq_id);
+    if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
+    if (tile_p < 1 || count < 0 || count > tile_p)
+        return fail(GKV_ERR_INVALID, "count=%lld tile_p=%d (need 0 <= count <= tile_p, tile_p >= 1)",
+                    (long long)count, tile_p);
+    if (start < 0 || start + count > s->len)
+        return fail(GKV_ERR_BAD_SEQ, "window [%lld, %lld) outside sequence %d of length %lld", (long long)start,
+                    (long long)(start + count), seq_id, (long long)s->len);
+    if (!K || !V) return fail(GKV_ERR_INVALID, "null K/V");
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
+    if (rc) return rc;
+    DeviceGuard guard(pool->cfg.device);
+    gkv::CompactParams p{};
+    p.table = pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq;
+    p.k_pool = pool->d_k;
+    p.v_pool = pool->d_v;
+    p.K = static_cast<uint16_t *>(K);
+    p.V = static_cast<uint16_t *>(V);
+    p.start = start;
+    p.count = count;
+    p.rows = tile_p;
+    p.kvh = pool->cfg.kv_heads;
+    p.dh = pool->cfg.head_dim;
+    p.P = pool->cfg.page_tokens;
+    GKV_CUDA(gkv::launch_compact(p, static_cast<cudaStream_t>(stream)), "tile kernel launch");
     return GKV_OK;
 }
 

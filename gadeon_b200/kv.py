@@ -8,7 +8,7 @@ Two layers:
 * :class:`PagePool` -- the reference's per-sequence cache object
   (leok7v/gadeon ``PagePool``, LLM/src/CoreML/PagedAttention.swift:21-287):
   ``append(k, v)``, ``seed``, ``truncate(to)``, ``clone()``, ``compact()``,
-  ``from_compact``, ``length``, ``page_count``; and :func:`host_flash_decode`,
+  ``from_compact``, ``tile_at``, ``length``, ``page_count``; and :func:`host_flash_decode`,
   the drop-in for ``hostFlashDecode(q:pool:G:)`` (:317-366).
 
 Device tensors are torch CUDA tensors (torch is the device-memory and stream
@@ -48,6 +48,7 @@ EXPORTED = (
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
     "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16", "gkv_check_bounded_wait",
+    "gkv_tile_at",
 )
 
 
@@ -116,6 +117,7 @@ def load_library(path: str = LIB_PATH):
         "gkv_mtp_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
         "gkv_conv_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, P, P, P, P]),
         "gkv_check_bounded_wait": (C.c_int, [i32, i64, i32p]),
+        "gkv_tile_at": (C.c_int, [P, i32, i64, i64, i32, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -360,6 +362,17 @@ class BlockPool:
         _check(_lib.gkv_compact_seq(self._h, seq, _dev_ptr(K), _dev_ptr(V), _stream_ptr(stream)))
         return K, V
 
+    def tile_at(self, seq: int, start: int, count: int, tile_p: int, stream=None):
+        """``gkv_tile_at``: positions [start, start + count) as head-major
+        [kv_heads, tile_p, head_dim] fp16 K and V device tensors, rows
+        count..tile_p-1 zero."""
+        import torch
+        dev = torch.device("cuda", self.device)
+        K = torch.empty((self.kv_heads, tile_p, self.head_dim), dtype=torch.float16, device=dev)
+        V = torch.empty_like(K)
+        _check(_lib.gkv_tile_at(self._h, seq, start, count, tile_p, _dev_ptr(K), _dev_ptr(V), _stream_ptr(stream)))
+        return K, V
+
     def from_compact(self, K, V, length: int, stream=None) -> int:
         for name, t in (("K", K), ("V", V)):
             _check_shape(name, t, (self.kv_heads, length, self.head_dim), _F16)
@@ -453,6 +466,11 @@ class PagePool:
     def compact(self, stream=None):
         """compact() (:225-252): (k, v) [kv_heads, length, head_dim] fp16."""
         return self.block_pool.compact(self.seq_id, stream)
+
+    def tile_at(self, start: int, count: int, tile_p: int, stream=None):
+        """tileAt(_:_:_:) (:151-161): (K, V) [kv_heads, tile_p, head_dim] fp16,
+        positions [start, start + count), rows past count zero."""
+        return self.block_pool.tile_at(self.seq_id, start, count, tile_p, stream)
 
     @staticmethod
     def from_compact(block_pool: BlockPool, k, v, length: int, stream=None) -> "PagePool":

@@ -184,6 +184,17 @@ int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream);
 int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V,
                     void *stream);
 
+/* PagePool.tileAt(_:_:_:) (PagedAttention.swift:151-161): positions
+ * [start, start + count) of the sequence into head-major
+ * [kv_heads, tile_p, head_dim] fp16 K and V tiles, rows count..tile_p-1
+ * zero -- the key window of one carry tile of pagedFlashCarry, which calls
+ * it with start = i*tile_p and count = min(tile_p, length - start)
+ * (:466-481).  Needs 0 <= count <= tile_p and start + count <= length
+ * (else GKV_ERR_INVALID / GKV_ERR_BAD_SEQ).  The window may span pages (the
+ * reference's never does: its page size is a multiple of tile_p). */
+int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count,
+                int32_t tile_p, void *K, void *V, void *stream);
+
 /* PagePool.fromCompact (PagedAttention.swift:256-264): a new sequence seeded
  * from head-major [kv_heads, length, head_dim] fp16 device buffers. */
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V,

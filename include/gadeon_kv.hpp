@@ -12,6 +12,7 @@
  *     truncate(to:)          :181-189 -> truncate(to)
  *     clone()                :199-210 -> clone()
  *     compact()              :225-252 -> compact() (host vectors)
+ *     tileAt(_:_:_:)         :151-161 -> tileAt(start, count, tileP, K, V)
  *     fromCompact(k:v:length:P:kvHeads:dh:) :256-264
  *                                     -> PagePool::fromCompact(pool, k, v, length)
  *   hostFlashDecode(q:pool:G:)        :317-366 -> hostFlashDecode(q, pool, G, ...)
@@ -207,6 +208,12 @@ public:
             std::memcpy(v.data(), buf.data() + 40 + n * 2, (size_t)n * 2);
         }
         return {std::move(k), std::move(v)};
+    }
+    /* tileAt(_:_:_:) -- positions [start, start + count) into head-major
+     * [kvHeads, tileP, dh] fp16 tiles K and V (device or page-locked),
+     * rows count..tileP-1 zero. */
+    void tileAt(int64_t start, int64_t count, int tileP, void *K, void *V, cudaStream_t s = nullptr) const {
+        check(gkv_tile_at(bp_->handle(), id_, start, count, tileP, K, V, s));
     }
     /* fromCompact(k:v:length:P:kvHeads:dh:) -- a new sequence of bp seeded
      * from host [kvHeads, length, dh] fp16 (through gkv_deserialize's pool

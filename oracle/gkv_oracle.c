@@ -438,6 +438,32 @@ int orc_compact(OrcPool *p, int seq, uint16_t *K, uint16_t *V) {
     return ORC_OK;
 }
 
+/* tileAt(start, count, tileP) (PagedAttention.swift:151-161, copyWindow
+ * :164-176): positions [start, start+count) into [KVH, tileP, dh] K and V,
+ * rows count..tileP-1 zero (zeroPage).  The reference reads the window from
+ * one page (its P is a multiple of tileP); this reads each row from its own
+ * page, the same bytes when the window lies in one page. */
+int orc_tile_at(OrcPool *p, int seq, int64_t start, int64_t count, int tile_p,
+                uint16_t *K, uint16_t *V) {
+    OrcSeq *s = get_seq(p, seq);
+    if (!s) return ORC_ERR_BAD_SEQ;
+    if (tile_p < 1 || count < 0 || count > tile_p) return ORC_ERR_INVALID;
+    if (start < 0 || start + count > s->len) return ORC_ERR_BAD_SEQ;
+    int P = p->P, dh = p->dh;
+    memset(K, 0, (size_t)p->kvh * tile_p * dh * 2);
+    memset(V, 0, (size_t)p->kvh * tile_p * dh * 2);
+    for (int h = 0; h < p->kvh; h++)
+        for (int64_t r = 0; r < count; r++) {
+            int64_t t = start + r;
+            int32_t pid = s->pages[t / P];
+            int64_t src = ((int64_t)h * P + t % P) * dh;
+            int64_t dst = ((int64_t)h * tile_p + r) * dh;
+            memcpy(K + dst, kpage(p, pid) + src, dh * 2);
+            memcpy(V + dst, vpage(p, pid) + src, dh * 2);
+        }
+    return ORC_OK;
+}
+
 /* fromCompact: a new sequence seeded from [KVH, length, dh]. */
 int orc_from_compact(OrcPool *p, const uint16_t *K, const uint16_t *V,
                      int64_t length) {

@@ -63,6 +63,7 @@ def lib():
         "orc_truncate": (C.c_int, [P, C.c_int, i32p, i64p]),
         "orc_clone": (C.c_int, [P, C.c_int]),
         "orc_compact": (C.c_int, [P, C.c_int, u16p, u16p]),
+        "orc_tile_at": (C.c_int, [P, C.c_int, C.c_int64, C.c_int64, C.c_int, u16p, u16p]),
         "orc_from_compact": (C.c_int, [P, u16p, u16p, C.c_int64]),
         "orc_seq_length": (C.c_int64, [P, C.c_int]),
         "orc_seq_pages": (C.c_int32, [P, C.c_int, i32p]),
@@ -170,6 +171,16 @@ class OraclePool:
         rc = lib().orc_compact(self._h, seq, _ptr(K, C.c_uint16), _ptr(V, C.c_uint16))
         if rc:
             raise ValueError(f"orc_compact rc={rc}")
+        return K, V
+
+    def tile_at(self, seq: int, start: int, count: int, tile_p: int):
+        """PagePool.tileAt (PagedAttention.swift:151-161): (K, V) tiles
+        [KVH, tile_p, dh], rows >= count zero; raises on a bad window."""
+        K = np.zeros((self.kv_heads, tile_p, self.head_dim), dtype=np.uint16)
+        V = np.zeros_like(K)
+        rc = lib().orc_tile_at(self._h, seq, start, count, tile_p, _ptr(K, C.c_uint16), _ptr(V, C.c_uint16))
+        if rc:
+            raise ValueError(f"orc_tile_at rc={rc}")
         return K, V
 
     def from_compact(self, K: np.ndarray, V: np.ndarray, length: int) -> int:

@@ -15,6 +15,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <algorithm>
 #include <cstdlib>
 #include <vector>
 
@@ -30,6 +31,7 @@ int orc_truncate(OrcPool *p, int n, const int32_t *seq_ids, const int64_t *new_l
 int orc_clone(OrcPool *p, int src);
 int orc_seq_release(OrcPool *p, int seq);
 int orc_compact(OrcPool *p, int seq, uint16_t *K, uint16_t *V);
+int orc_tile_at(OrcPool *p, int seq, int64_t start, int64_t count, int tile_p, uint16_t *K, uint16_t *V);
 int orc_from_compact(OrcPool *p, const uint16_t *K, const uint16_t *V, int64_t length);
 int64_t orc_seq_length(OrcPool *p, int seq);
 int32_t orc_seq_pages(OrcPool *p, int seq, int32_t *out);
@@ -211,6 +213,24 @@ void run() {
     check_decode(a, o, oa, 700, "decode after truncate");
     check_decode(b, o, ob, 701, "decode of the clone");
     check_free_list(bp, o, "after clone + truncate");
+
+    // tileAt over the carry windows of pagedFlashCarry (start = i*tileP,
+    // count = min(tileP, length - start)), bit for bit
+    for (int tileP : {8, 32}) {
+        const int64_t n = b.length();
+        const size_t elems = (size_t)KVH * tileP * DH;
+        Dev<uint16_t> tk(elems), tv(elems);
+        std::vector<uint16_t> ok(elems), ov(elems);
+        for (int64_t start = 0; start < n; start += tileP) {
+            const int64_t count = std::min<int64_t>(tileP, n - start);
+            b.tileAt(start, count, tileP, tk.p, tv.p);
+            orc_tile_at(o, ob, start, count, tileP, ok.data(), ov.data());
+            CHECK(tk.host(elems) == ok && tv.host(elems) == ov, "tileAt(%lld, %lld, %d) not bit-exact",
+                  (long long)start, (long long)count, tileP);
+        }
+        CHECK(thrown_code([&] { b.tileAt(n - 1, 2, tileP, tk.p, tv.p); }) == GKV_ERR_BAD_SEQ,
+              "tileAt past the end");
+    }
 
     // compact() -> fromCompact round trip
     auto kv = b.compact();

@@ -367,3 +367,34 @@ def test_pagepool_view_and_host_flash_decode(cuda, oracle):
     pr.seqs.append(c.seq_id)
     pr.check_state()
     decode(c, c.seq_id, 12)
+
+
+@pytest.mark.parametrize("tile_p", [4, 16, 32, 512])
+def test_tile_at_carry_windows(cuda, oracle, tile_p):
+    """tileAt (PagedAttention.swift:151-161) through gkv_tile_at, bit for bit
+    against the oracle, over the windows pagedFlashCarry asks for
+    (start = i*tile_p, count = min(tile_p, length - start), :466-481): tiles
+    inside one page (4, 16) and spanning pages (32, 512), zero rows past the
+    sequence; the pool is left as it was; bad windows are refused."""
+    from gadeon_b200 import GKV_ERR_BAD_SEQ, GKV_ERR_INVALID, GkvError, PagePool
+    pr = Pair(cuda, oracle, kvh=2, dh=128, P=16, num_pages=64, seed=21)
+    s = pr.new_seq()
+    pr.seed(s, 77)
+    pr.append([s], [6])  # 83 positions over 6 pages, the last one partial
+    n = pr.gpu.length(s)
+    for start in range(0, n, tile_p):
+        count = min(tile_p, n - start)
+        gk_, gv = pr.gpu.tile_at(s, start, count, tile_p)
+        ok, ov = pr.orc.tile_at(s, start, count, tile_p)
+        as_u16 = lambda t: t.cpu().view(cuda.int16).numpy().view(np.uint16)
+        assert np.array_equal(as_u16(gk_), ok) and np.array_equal(as_u16(gv), ov), (start, count)
+    view = PagePool(pr.gpu, s)
+    k2, _ = view.tile_at(5, 3, 8)
+    assert np.array_equal(k2.cpu().view(cuda.int16).numpy().view(np.uint16), pr.orc.tile_at(s, 5, 3, 8)[0])
+    for start, count, tp, code in [(n - 2, 3, 8, GKV_ERR_BAD_SEQ), (-1, 1, 8, GKV_ERR_BAD_SEQ),
+                                   (0, 9, 8, GKV_ERR_INVALID), (0, 0, 0, GKV_ERR_INVALID)]:
+        with pytest.raises(GkvError) as e:
+            pr.gpu.tile_at(s, start, count, tp)
+        assert e.value.code == code, (start, count, tp)
+    cuda.cuda.synchronize()
+    pr.check_state()

@@ -215,3 +215,28 @@ def test_release_returns_pages(oracle):
     assert pool.seq_create() == s
     assert pool.append([s], [40], np.zeros((40, 1, 8), np.uint16), np.zeros((40, 1, 8), np.uint16)) == O.ORC_ERR_NO_PAGES
     assert len(pool.free_list()) == 8  # failed append mutates nothing
+
+
+def test_tile_at_windows(oracle):
+    """tileAt (PagedAttention.swift:151-161): rows [0, count) are positions
+    start.. of compact(), rows past count are zero (zeroPage), for windows
+    inside one page, spanning pages, and empty; the reference's carry loop
+    (:466-481) covers the sequence tile by tile."""
+    kvh, dh, P = 2, 16, 8
+    pool = oracle.OraclePool(kvh, dh, P, 32, 3)
+    s = pool.seq_create()
+    n = 45
+    K = oracle.normal_f16(1, 0, (kvh, n, dh))
+    V = oracle.normal_f16(1, 1, (kvh, n, dh))
+    assert pool.seed(s, K, V, n) == 0
+    for start, count, tile_p in [(0, 8, 8), (8, 8, 8), (40, 5, 8), (3, 10, 16), (13, 0, 4), (44, 1, 32)]:
+        tk, tv = pool.tile_at(s, start, count, tile_p)
+        assert np.array_equal(tk[:, :count], K[:, start:start + count])
+        assert np.array_equal(tv[:, :count], V[:, start:start + count])
+        assert not tk[:, count:].any() and not tv[:, count:].any()
+    tile_p = 16
+    got = np.concatenate([pool.tile_at(s, st, min(tile_p, n - st), tile_p)[0] for st in range(0, n, tile_p)], axis=1)
+    assert np.array_equal(got[:, :n], K) and not got[:, n:].any()
+    for start, count, tile_p in [(40, 6, 8), (-1, 1, 4), (0, 5, 4), (0, 1, 0)]:
+        with pytest.raises(ValueError):
+            pool.tile_at(s, start, count, tile_p)
