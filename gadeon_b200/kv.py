@@ -8,7 +8,8 @@ Two layers:
 * :class:`PagePool` -- the reference's per-sequence cache object
   (leok7v/gadeon ``PagePool``, LLM/src/CoreML/PagedAttention.swift:21-287):
   ``append(k, v)``, ``seed``, ``truncate(to)``, ``clone()``, ``compact()``,
-  ``from_compact``, ``tile_at``, ``length``, ``page_count``; and :func:`host_flash_decode`,
+  ``from_compact``, ``tile_at``, ``k_page`` / ``v_page``, ``floats32``,
+  ``length``, ``page_count``; and :func:`host_flash_decode`,
   the drop-in for ``hostFlashDecode(q:pool:G:)`` (:317-366).
 
 Device tensors are torch CUDA tensors (torch is the device-memory and stream
@@ -471,6 +472,29 @@ class PagePool:
         """tileAt(_:_:_:) (:151-161): (K, V) [kv_heads, tile_p, head_dim] fp16,
         positions [start, start + count), rows past count zero."""
         return self.block_pool.tile_at(self.seq_id, start, count, tile_p, stream)
+
+    def k_page(self, i: int):
+        """kPage(_:) (:80): page i of the sequence as stored, uint16
+        [kv_heads, P, head_dim] on the host (rows past the length included,
+        as the pool holds them).  Waits for the device."""
+        return self._page(i)[0]
+
+    def v_page(self, i: int):
+        """vPage(_:) (:81), as k_page."""
+        return self._page(i)[1]
+
+    def _page(self, i: int):
+        table = self.block_pool.export_table(self.seq_id)
+        if not 0 <= i < len(table):
+            raise GkvError(GKV_ERR_INVALID, f"page {i} of a sequence with {len(table)} pages")
+        return self.block_pool.export_page(int(table[i]))
+
+    def floats32(self, stream=None):
+        """floats32() (:46-62): (k, v), per kv head the sequence's rows as
+        fp32, [kv_heads, length * head_dim] (numpy, host)."""
+        K, V = self.compact(stream)
+        n = self.kv_heads
+        return (K.float().reshape(n, -1).cpu().numpy(), V.float().reshape(n, -1).cpu().numpy())
 
     @staticmethod
     def from_compact(block_pool: BlockPool, k, v, length: int, stream=None) -> "PagePool":

@@ -13,6 +13,8 @@
  *     clone()                :199-210 -> clone()
  *     compact()              :225-252 -> compact() (host vectors)
  *     tileAt(_:_:_:)         :151-161 -> tileAt(start, count, tileP, K, V)
+ *     kPage(_:), vPage(_:)   :80-81   -> kPage(i), vPage(i) (host vectors)
+ *     floats32()             :46-62   -> floats32() (host vectors)
  *     fromCompact(k:v:length:P:kvHeads:dh:) :256-264
  *                                     -> PagePool::fromCompact(pool, k, v, length)
  *   hostFlashDecode(q:pool:G:)        :317-366 -> hostFlashDecode(q, pool, G, ...)
@@ -58,6 +60,31 @@ struct Error : std::runtime_error {
 inline void check(int rc) {
     if (rc != GKV_OK) throw Error(rc, gkv_last_error());
 }
+
+namespace detail {
+/* IEEE binary16 bits -> binary32, exact (the widening floats32() does). */
+inline float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu, bits;
+    if (exp == 0x1fu) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else if (exp != 0) {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    } else if (man == 0) {
+        bits = sign;
+    } else {  // subnormal: normalise
+        int e = -1;
+        do {
+            man <<= 1;
+            ++e;
+        } while (!(man & 0x400u));
+        bits = sign | ((uint32_t)(112 - e) << 23) | ((man & 0x3ffu) << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, sizeof f);
+    return f;
+}
+}  // namespace detail
 
 inline void check_cuda(cudaError_t e, const char *what) {
     if (e != cudaSuccess) throw Error(GKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -215,6 +242,28 @@ public:
     void tileAt(int64_t start, int64_t count, int tileP, void *K, void *V, cudaStream_t s = nullptr) const {
         check(gkv_tile_at(bp_->handle(), id_, start, count, tileP, K, V, s));
     }
+    /* kPage(_:) / vPage(_:) -- page i of the sequence as stored,
+     * [kvHeads, P, dh] fp16 on the host (rows past length() included, as the
+     * pool holds them).  Waits for the device. */
+    std::vector<uint16_t> kPage(int i) const { return page(i).first; }
+    std::vector<uint16_t> vPage(int i) const { return page(i).second; }
+    /* floats32() -- per kv head, the sequence's rows widened to fp32:
+     * k[h] and v[h] hold length() * dh values. */
+    std::pair<std::vector<std::vector<float>>, std::vector<std::vector<float>>> floats32(
+        cudaStream_t s = nullptr) const {
+        const auto kv = compact(s);
+        const size_t per = kv.first.size() / (size_t)kvHeads();
+        std::vector<std::vector<float>> k((size_t)kvHeads()), v((size_t)kvHeads());
+        for (int h = 0; h < kvHeads(); ++h) {
+            k[h].resize(per);
+            v[h].resize(per);
+            for (size_t j = 0; j < per; ++j) {
+                k[h][j] = detail::half_to_float(kv.first[h * per + j]);
+                v[h][j] = detail::half_to_float(kv.second[h * per + j]);
+            }
+        }
+        return {std::move(k), std::move(v)};
+    }
     /* fromCompact(k:v:length:P:kvHeads:dh:) -- a new sequence of bp seeded
      * from host [kvHeads, length, dh] fp16 (through gkv_deserialize's pool
      * section reader, which takes host memory). */
@@ -244,6 +293,19 @@ public:
     }
 
 private:
+    std::pair<std::vector<uint16_t>, std::vector<uint16_t>> page(int i) const {
+        const int32_t n = pageCount();
+        if (i < 0 || i >= n)
+            throw Error(GKV_ERR_INVALID, "page " + std::to_string(i) + " of a sequence with " + std::to_string(n) +
+                                             " pages");
+        std::vector<int32_t> table((size_t)n);
+        int32_t got = 0;
+        check(gkv_export_table(bp_->handle(), id_, table.data(), n, &got));
+        const size_t elems = (size_t)kvHeads() * (size_t)P() * (size_t)dh();
+        std::vector<uint16_t> k(elems), v(elems);
+        check(gkv_export_page(bp_->handle(), table[(size_t)i], k.data(), v.data()));
+        return {std::move(k), std::move(v)};
+    }
     static void put_i64(uint8_t *&p, int64_t x) {
         for (int i = 0; i < 8; ++i) *p++ = (uint8_t)((uint64_t)x >> (8 * i));
     }

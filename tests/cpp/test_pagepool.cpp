@@ -36,6 +36,8 @@ int orc_from_compact(OrcPool *p, const uint16_t *K, const uint16_t *V, int64_t l
 int64_t orc_seq_length(OrcPool *p, int seq);
 int32_t orc_seq_pages(OrcPool *p, int seq, int32_t *out);
 int32_t orc_free_list(OrcPool *p, int32_t *out);
+const uint16_t *orc_page_k(OrcPool *p, int32_t pid);
+const uint16_t *orc_page_v(OrcPool *p, int32_t pid);
 int orc_flash_decode(OrcPool *p, int seq, const uint16_t *q, int G, float scale, float *out);
 void orc_fill_normal_f16(uint64_t seed, uint64_t stream, uint16_t *out, int64_t n);
 }
@@ -230,6 +232,27 @@ void run() {
         }
         CHECK(thrown_code([&] { b.tileAt(n - 1, 2, tileP, tk.p, tv.p); }) == GKV_ERR_BAD_SEQ,
               "tileAt past the end");
+    }
+
+    // kPage / vPage: the pages as stored; floats32: compact() widened
+    {
+        const auto table = orc_table(o, ob);
+        for (int i = 0; i < b.pageCount(); i += 2) {
+            const uint16_t *wk = orc_page_k(o, table[(size_t)i]), *wv = orc_page_v(o, table[(size_t)i]);
+            const size_t elems = (size_t)KVH * P * DH;
+            CHECK(b.kPage(i) == std::vector<uint16_t>(wk, wk + elems) &&
+                      b.vPage(i) == std::vector<uint16_t>(wv, wv + elems),
+                  "kPage/vPage(%d) not the stored page", i);
+        }
+        CHECK(thrown_code([&] { b.kPage(b.pageCount()); }) == GKV_ERR_INVALID, "kPage past the last page");
+        const auto f = b.floats32();
+        const auto c = b.compact();
+        const size_t per = (size_t)b.length() * DH;
+        bool same = f.first.size() == (size_t)KVH && f.first[1].size() == per;
+        for (size_t j = 0; same && j < per; ++j)
+            same = f.first[1][j] == gadeon::detail::half_to_float(c.first[per + j]) &&
+                   f.second[0][j] == gadeon::detail::half_to_float(c.second[j]);
+        CHECK(same, "floats32() is not compact() widened");
     }
 
     // compact() -> fromCompact round trip

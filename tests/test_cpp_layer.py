@@ -24,6 +24,22 @@ def test_header_compiles(std):
     assert r.returncode == 0, r.stderr
 
 
+def test_half_to_float_exhaustive(tmp_path):
+    """gadeon::detail::half_to_float (the widening of floats32()) equals
+    numpy's binary16 -> binary32 for all 65,536 bit patterns."""
+    import numpy as np
+    src = tmp_path / "h2f.cpp"
+    src.write_text('#include "gadeon_kv.hpp"\n#include <cstdio>\n'
+                   'int main() { for (unsigned h = 0; h < 65536; ++h) { float f = gadeon::detail::half_to_float('
+                   '(uint16_t)h); uint32_t b; std::memcpy(&b, &f, 4); std::printf("%u\\n", b); } return 0; }\n')
+    exe = str(tmp_path / "h2f")
+    r = subprocess.run(["g++", "-std=c++17", "-O1", *WARN, *INC, str(src), "-o", exe], text=True, capture_output=True)
+    assert r.returncode == 0, r.stderr
+    got = np.array(subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split(), dtype=np.uint64)
+    want = np.arange(65536, dtype=np.uint16).view(np.float16).astype(np.float32).view(np.uint32)
+    assert np.array_equal(got.astype(np.uint32), want)
+
+
 def build_test_program(out_dir):
     from gadeon_b200 import build
     build.build()

@@ -391,6 +391,14 @@ def test_tile_at_carry_windows(cuda, oracle, tile_p):
     view = PagePool(pr.gpu, s)
     k2, _ = view.tile_at(5, 3, 8)
     assert np.array_equal(k2.cpu().view(cuda.int16).numpy().view(np.uint16), pr.orc.tile_at(s, 5, 3, 8)[0])
+    # kPage / vPage (:80-81): the pages as stored, stale or zero rows included; floats32 (:46-62)
+    for i, pid in enumerate(pr.orc.pages(s)):
+        ok, ov = pr.orc.page_bytes(int(pid))
+        assert np.array_equal(view.k_page(i), ok) and np.array_equal(view.v_page(i), ov)
+    fk, fv = view.floats32()
+    ck, cv = pr.orc.compact(s)
+    assert np.array_equal(fk, oracle.f16_bits_to_f32(ck).reshape(2, -1))
+    assert np.array_equal(fv, oracle.f16_bits_to_f32(cv).reshape(2, -1))
     for start, count, tp, code in [(n - 2, 3, 8, GKV_ERR_BAD_SEQ), (-1, 1, 8, GKV_ERR_BAD_SEQ),
                                    (0, 9, 8, GKV_ERR_INVALID), (0, 0, 0, GKV_ERR_INVALID)]:
         with pytest.raises(GkvError) as e:
