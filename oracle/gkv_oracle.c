@@ -667,7 +667,7 @@ int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
 }
 
 /* ------------------------------------------------------------------ */
-/* GDN rollback after an accepted speculative prefix (SURVEY "next")   */
+/* GDN rollback after an accepted speculative prefix                   */
 /* ------------------------------------------------------------------ */
 
 /* MtpRollback.stateAfter (LLM/src/CoreML/MtpRollback.swift:20-60) for a
