@@ -804,17 +804,24 @@ def run_config6(args, rank, world, local):
     ms_acc = rng.integers(1, Cw + 1, size=(W + K, n)).astype(np.int32)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
 
+    fused = not args.gdn_f32  # fp16 storage: state and conv tail in one launch (gkv_gdn_rollback_f16)
+
     def step(i, ti):
         if ti is not None:
             ev[ti][0].record()
-        gk.mtp_rollback(ms_acc[i], s0, delta, kk, gcum, out=out)
+        if fused:
+            gk.gdn_rollback(ms_acc[i], s0, delta, kk, gcum, proj, pre, out=out, conv_out=conv)
+        else:
+            gk.mtp_rollback(ms_acc[i], s0, delta, kk, gcum, out=out)
         if ti is not None:
             ev[ti][1].record()
-        gk.conv_rollback(ms_acc[i], proj, pre, out=conv)
+        if not fused:
+            gk.conv_rollback(ms_acc[i], proj, pre, out=conv)
 
     ms, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
-    bpl = statistics.mean(rollback_bytes(ms_acc[W + i], g, sb)[0] for i in range(K))
+    # bytes of the timed launch: the state rollback, plus the conv tail when fused
+    bpl = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)[: 2 if fused else 1]) for i in range(K))
     step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)) for i in range(K))
     hbm, kind = peaks()
     cpu = None
@@ -848,10 +855,11 @@ def run_config6(args, rank, world, local):
                    "step_bytes": step_bytes, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "traffic": None,
-                     "kernel": "mtp_rollback_fast_kernel<%s>" % ("float" if args.gdn_f32 else "half"),
+                     "kernel": "gdn_rollback_f16_kernel (state + conv tail)" if fused
+                     else "mtp_rollback_fast_f32_kernel",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms},
         "step_gbs": step_bytes / (ms * 1e-3) / 1e9,
-        "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * 2, "clocks": clk}), flush=True)
+        "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * (1 if fused else 2), "clocks": clk}), flush=True)
 
 
 def run_config7(args, rank, world, local):
@@ -925,8 +933,11 @@ def run_config7(args, rank, world, local):
         lens = lens + m
         main.truncate(mids, lens)
         mm = np.repeat(m, g.layers).astype(np.int32)
-        gk.mtp_rollback(mm, s0, gd, gk_, gc, out=s_out)
-        gk.conv_rollback(mm, proj, pre, out=conv)
+        if args.gdn_f32:
+            gk.mtp_rollback(mm, s0, gd, gk_, gc, out=s_out)
+            gk.conv_rollback(mm, proj, pre, out=conv)
+        else:  # fp16 storage: state and conv tail in one launch
+            gk.gdn_rollback(mm, s0, gd, gk_, gc, proj, pre, out=s_out, conv_out=conv)
         drafter.rewind_append(dids, base, m, k4[: int(m.sum())], k4[: int(m.sum())])
         dlens = base + m
 
@@ -956,7 +967,7 @@ def run_config7(args, rank, world, local):
                      "kernel": "attend_kernel<256,TMA> (3 drafter decodes + 1 verify per cycle, fused appends)",
                      "bytes_per_cycle": sum(att_bytes) / K, "attend_ms_per_cycle": att_ms / K},
         "cycle_gbs": cycle_bytes / (ms * 1e-3) / 1e9,
-        "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 2 + 2 + 1), "clocks": clk}), flush=True)
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 1 + (2 if args.gdn_f32 else 1) + 1), "clocks": clk}), flush=True)
 
 
 def _json_only_stdout():

@@ -20,6 +20,7 @@ from .kv import (  # noqa: F401
     PagePool,
     check_bounded_wait,
     conv_rollback,
+    gdn_rollback,
     host_flash_decode,
     load_library,
     deserialize,

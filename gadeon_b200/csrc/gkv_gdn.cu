@@ -246,10 +246,9 @@ __device__ __forceinline__ void conv_slice(const ConvParams<T> &p, int item, int
 }
 
 template <typename T, int TAPS>
-__global__ void __launch_bounds__(kConvVecThreads) conv_rollback_vec_kernel(const __grid_constant__ ConvParams<T> p) {
+__device__ __forceinline__ void conv_vec_block(const ConvParams<T> &p, int item, int bx) {
     static_assert((8 * TAPS / Words<T>::PER) % 4 == 0, "whole 16-byte vectors");
-    const int item = blockIdx.y;
-    const int c0 = (blockIdx.x * kConvVecThreads + threadIdx.x) * 8;
+    const int c0 = (bx * kConvVecThreads + threadIdx.x) * 8;
     if (c0 >= p.CD) return;
     const int m = p.m[item];
     const int64_t tail = ((int64_t)item * p.CD + c0) * TAPS;
@@ -260,6 +259,12 @@ __global__ void __launch_bounds__(kConvVecThreads) conv_rollback_vec_kernel(cons
         case 3: if constexpr (TAPS > 3) conv_slice<T, TAPS, 3>(p, item, c0, tail, m); break;
         default: break;
     }
+}
+
+// grid (ceil(CD / 8 / 128), items)
+template <typename T, int TAPS>
+__global__ void __launch_bounds__(kConvVecThreads) conv_rollback_vec_kernel(const __grid_constant__ ConvParams<T> p) {
+    conv_vec_block<T, TAPS>(p, blockIdx.y, blockIdx.x);
 }
 
 // Fast path for the verify widths MTP uses (C <= kFastC), DV a multiple of
@@ -387,12 +392,11 @@ __device__ __forceinline__ void roll_rows(int DK, int r0, int rstride, int ncg, 
 // fp16 state: thread = COLS columns moved as one 8- or 16-byte access, the
 // same arithmetic per element as the fp32 kernel.
 template <typename T, int COLS, int UNROLL, int MAXC, int THREADS>
-__global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams<T> p) {
+__device__ __forceinline__ void state_fast_block(const RollbackParams<T> &p, int hs) {
     using V = Cols<T, COLS>;
     using R = typename V::raw;
     __shared__ float kw[kFastC][kFastDK];
     __shared__ float eM_s;
-    const int hs = blockIdx.x;
     const int m = p.m[hs / p.H];
     const int ncg = p.DV / COLS;
     const int rstride = THREADS / ncg;
@@ -451,11 +455,41 @@ __global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid
     }
 }
 
+template <typename T, int COLS, int UNROLL, int MAXC, int THREADS>
+__global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid_constant__ RollbackParams<T> p) {
+    state_fast_block<T, COLS, UNROLL, MAXC, THREADS>(p, blockIdx.x);
+}
+
+// The whole of Engine.rollbackGDN for a batch in one launch (fp16 storage):
+// blocks [0, state_blocks) roll back one (item, value head) state each,
+// the rest one 1,024-channel slice of an item's conv tail each.  The two
+// parts touch disjoint memory, so the conv blocks, dispatched last, fill the
+// state stream's tail instead of running as a launch of their own.
+struct GdnParams {
+    RollbackParams<__half> s;
+    ConvParams<__half> c;
+    int32_t state_blocks, conv_bx;
+};
+static_assert(kConvVecThreads == kF16Threads, "one block size for both parts");
+
+template <int MAXC, int TAPS>
+__global__ void __launch_bounds__(kF16Threads) gdn_rollback_f16_kernel(const __grid_constant__ GdnParams p) {
+    if ((int)blockIdx.x < p.state_blocks) {
+        state_fast_block<__half, kF16Cols, kF16Unroll, MAXC, kF16Threads>(p.s, blockIdx.x);
+    } else {
+        const int b = (int)blockIdx.x - p.state_blocks;
+        conv_vec_block<__half, TAPS>(p.c, b / p.conv_bx, b % p.conv_bx);
+    }
+}
+
 bool misaligned(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 
+// Argument checks of the state rollback; on success *fast tells whether
+// the 16-byte-column kernel applies (else the element-wise one).
 template <typename T>
-int mtp_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
-                      const T *s0, const float *delta, const float *k, const float *gcum, T *out, void *stream) {
+int check_state_args(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                     const T *s0, const float *delta, const float *k, const float *gcum, const T *out, bool *vec_out,
+                     bool *fast_out) {
     constexpr bool F16 = sizeof(T) == 2;
     if (n_items < 0 || H < 1 || DK < 1 || DV < 1 || C < 1)
         return report_error(GKV_ERR_INVALID, "n_items=%d H=%d DK=%d DV=%d C=%d", n_items, H, DK, DV, C);
@@ -478,23 +512,43 @@ int mtp_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, 
     const bool fast = vec && C <= kFastC && DK <= kFastDK && DV <= COLS * (F16 ? kF16Threads : kRollThreads);
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
+    *vec_out = vec;
+    *fast_out = fast;
+    return GKV_OK;
+}
+
+template <typename T>
+void fill_state_params(RollbackParams<T> &p, int32_t first, int32_t cnt, const int32_t *m, int32_t H, int32_t DK,
+                       int32_t DV, int32_t C, const T *s0, const float *delta, const float *k, const float *gcum,
+                       T *out) {
+    p.H = H;
+    p.DK = DK;
+    p.DV = DV;
+    p.C = C;
+    const int64_t hs0 = (int64_t)first * H;
+    p.s0 = s0 + hs0 * DK * DV;
+    p.delta = delta + hs0 * C * DV;
+    p.k = k + hs0 * C * DK;
+    p.gcum = gcum + hs0 * C;
+    p.out = out + hs0 * DK * DV;
+    for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+}
+
+template <typename T>
+int mtp_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                      const T *s0, const float *delta, const float *k, const float *gcum, T *out, void *stream) {
+    constexpr bool F16 = sizeof(T) == 2;
+    constexpr int COLS = F16 ? kF16Cols : 4;
+    bool vec = false, fast = false;
+    if (const int rc = check_state_args<T>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, out, &vec, &fast)) return rc;
+    if (n_items == 0) return GKV_OK;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     // items per launch: what the parameter block's m[] holds
     const int32_t per = kMaxItemsPerLaunch;
     for (int32_t first = 0; first < n_items; first += per) {
         const int32_t cnt = n_items - first < per ? n_items - first : per;
         RollbackParams<T> p{};
-        p.H = H;
-        p.DK = DK;
-        p.DV = DV;
-        p.C = C;
-        const int64_t hs0 = (int64_t)first * H;
-        p.s0 = s0 + hs0 * DK * DV;
-        p.delta = delta + hs0 * C * DV;
-        p.k = k + hs0 * C * DK;
-        p.gcum = gcum + hs0 * C;
-        p.out = out + hs0 * DK * DV;
-        for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+        fill_state_params<T>(p, first, cnt, m, H, DK, DV, C, s0, delta, k, gcum, out);
         const unsigned blocks = (unsigned)((int64_t)cnt * H);
         if constexpr (!F16) {
             if (fast)
@@ -519,8 +573,8 @@ int mtp_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, 
 }
 
 template <typename T>
-int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
-                       const float *proj, const T *pre, T *out, void *stream) {
+int check_conv_args(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C, const float *proj,
+                    const T *pre, const T *out, bool *vec_out) {
     if (n_items < 0 || conv_dim < 1 || taps < 1 || C < 1)
         return report_error(GKV_ERR_INVALID, "n_items=%d conv_dim=%d taps=%d C=%d", n_items, conv_dim, taps, C);
     if (n_items == 0) return GKV_OK;
@@ -533,18 +587,33 @@ int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int3
         return report_error(GKV_ERR_INVALID, "proj must be 4-byte aligned, pre/out %d-byte", (int)sizeof(T));
     for (int32_t i = 0; i < n_items; ++i)
         if (m[i] < 1 || m[i] > C) return report_error(GKV_ERR_INVALID, "m[%d]=%d outside 1..%d", i, m[i], C);
-    const bool vec = conv_dim % 8 == 0 && taps <= 4 && !misaligned(proj) && !misaligned(pre) && !misaligned(out);
+    *vec_out = conv_dim % 8 == 0 && taps <= 4 && !misaligned(proj) && !misaligned(pre) && !misaligned(out);
+    return GKV_OK;
+}
+
+template <typename T>
+void fill_conv_params(ConvParams<T> &p, int32_t first, int32_t cnt, const int32_t *m, int32_t conv_dim, int32_t taps,
+                      int32_t C, const float *proj, const T *pre, T *out) {
+    p.CD = conv_dim;
+    p.taps = taps;
+    p.C = C;
+    p.proj = proj + (int64_t)first * C * conv_dim;
+    p.pre = pre + (int64_t)first * conv_dim * taps;
+    p.out = out + (int64_t)first * conv_dim * taps;
+    for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+}
+
+template <typename T>
+int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,
+                       const float *proj, const T *pre, T *out, void *stream) {
+    bool vec = false;
+    if (const int rc = check_conv_args<T>(n_items, m, conv_dim, taps, C, proj, pre, out, &vec)) return rc;
+    if (n_items == 0) return GKV_OK;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     for (int32_t first = 0; first < n_items; first += kMaxItemsPerLaunch) {
         const int32_t cnt = n_items - first < kMaxItemsPerLaunch ? n_items - first : kMaxItemsPerLaunch;
         ConvParams<T> p{};
-        p.CD = conv_dim;
-        p.taps = taps;
-        p.C = C;
-        p.proj = proj + (int64_t)first * C * conv_dim;
-        p.pre = pre + (int64_t)first * conv_dim * taps;
-        p.out = out + (int64_t)first * conv_dim * taps;
-        for (int32_t i = 0; i < cnt; ++i) p.m[i] = m[first + i];
+        fill_conv_params<T>(p, first, cnt, m, conv_dim, taps, C, proj, pre, out);
         if (vec) {
             const dim3 vgrid((unsigned)((conv_dim / 8 + kConvVecThreads - 1) / kConvVecThreads), (unsigned)cnt);
             switch (taps) {
@@ -563,6 +632,52 @@ int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int3
     return GKV_OK;
 }
 
+// State and conv tail of every item in one launch when both take their
+// vector kernels; otherwise the two launches of the separate entry points.
+int gdn_rollback_f16_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                          const __half *s0, const float *delta, const float *k, const float *gcum, __half *s_out,
+                          int32_t conv_dim, int32_t taps, const float *proj, const __half *pre, __half *conv_out,
+                          void *stream) {
+    bool svec = false, sfast = false, cvec = false;
+    if (const int rc = check_state_args<__half>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, &svec, &sfast))
+        return rc;
+    if (const int rc = check_conv_args<__half>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, &cvec)) return rc;
+    if (n_items == 0) return GKV_OK;
+    if (!sfast || !cvec) {
+        if (const int rc = mtp_rollback_impl<__half>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, stream))
+            return rc;
+        return conv_rollback_impl<__half>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, stream);
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int32_t conv_bx = (conv_dim / 8 + kConvVecThreads - 1) / kConvVecThreads;
+    const bool narrow = C <= kF16NarrowC;
+    for (int32_t first = 0; first < n_items; first += kMaxItemsPerLaunch) {
+        const int32_t cnt = n_items - first < kMaxItemsPerLaunch ? n_items - first : kMaxItemsPerLaunch;
+        GdnParams p{};
+        fill_state_params<__half>(p.s, first, cnt, m, H, DK, DV, C, s0, delta, k, gcum, s_out);
+        fill_conv_params<__half>(p.c, first, cnt, m, conv_dim, taps, C, proj, pre, conv_out);
+        p.state_blocks = cnt * H;
+        p.conv_bx = conv_bx;
+        const unsigned blocks = (unsigned)((int64_t)cnt * H + (int64_t)cnt * conv_bx);
+#define GKV_GDN_LAUNCH(MAXC)                                                                                \
+    switch (taps) {                                                                                         \
+        case 1: gdn_rollback_f16_kernel<MAXC, 1><<<blocks, kF16Threads, 0, st>>>(p); break;                 \
+        case 2: gdn_rollback_f16_kernel<MAXC, 2><<<blocks, kF16Threads, 0, st>>>(p); break;                 \
+        case 3: gdn_rollback_f16_kernel<MAXC, 3><<<blocks, kF16Threads, 0, st>>>(p); break;                 \
+        default: gdn_rollback_f16_kernel<MAXC, 4><<<blocks, kF16Threads, 0, st>>>(p); break;                \
+    }
+        if (narrow) {
+            GKV_GDN_LAUNCH(kF16NarrowC)
+        } else {
+            GKV_GDN_LAUNCH(kFastC)
+        }
+#undef GKV_GDN_LAUNCH
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "gdn_rollback launch: %s", cudaGetErrorString(e));
+    }
+    return GKV_OK;
+}
+
 }  // namespace
 }  // namespace gkv
 
@@ -577,6 +692,15 @@ extern "C" int gkv_mtp_rollback_f16(int32_t n_items, const int32_t *m, int32_t H
                                     const float *gcum, void *out, void *stream) {
     return gkv::mtp_rollback_impl<__half>(n_items, m, H, DK, DV, C, static_cast<const __half *>(s0), delta, k,
                                           gcum, static_cast<__half *>(out), stream);
+}
+
+extern "C" int gkv_gdn_rollback_f16(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV,
+                                    int32_t C, const void *s0, const float *delta, const float *k,
+                                    const float *gcum, void *state_out, int32_t conv_dim, int32_t taps,
+                                    const float *proj, const void *pre, void *conv_out, void *stream) {
+    return gkv::gdn_rollback_f16_impl(n_items, m, H, DK, DV, C, static_cast<const __half *>(s0), delta, k, gcum,
+                                      static_cast<__half *>(state_out), conv_dim, taps, proj,
+                                      static_cast<const __half *>(pre), static_cast<__half *>(conv_out), stream);
 }
 
 extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,

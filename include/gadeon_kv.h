@@ -274,6 +274,19 @@ int gkv_conv_rollback_f16(int32_t n_items, const int32_t *m, int32_t conv_dim,
                           int32_t taps, int32_t C, const float *proj,
                           const void *pre, void *out, void *stream);
 
+/* The whole of Engine.rollbackGDN (Engine.swift:2678-2716) for a batch with
+ * fp16 storage: gkv_mtp_rollback_f16 of (s0, delta, k, gcum) -> state_out
+ * and gkv_conv_rollback_f16 of (proj, pre) -> conv_out, the same items and
+ * m, in one launch when both shapes take the vector kernels (DV % 8 == 0,
+ * C <= 8, DK <= 256, conv_dim % 8 == 0, taps <= 4, 16-byte aligned arrays),
+ * else as those two calls.  Results identical to the two calls. */
+int gkv_gdn_rollback_f16(int32_t n_items, const int32_t *m, int32_t H,
+                         int32_t DK, int32_t DV, int32_t C, const void *s0,
+                         const float *delta, const float *k, const float *gcum,
+                         void *state_out, int32_t conv_dim, int32_t taps,
+                         const float *proj, const void *pre, void *conv_out,
+                         void *stream);
+
 /* Size of the library's static scratch array used by gkv_attend_noalloc
  * (held on every GPU that loads the library until the process exits), and
  * the largest batch that entry point takes. */

@@ -364,3 +364,39 @@ def test_gpu_f16_unaligned_state_takes_the_elementwise_kernel(cuda, oracle):
     aligned = gk.mtp_rollback(m, _dev(torch, s16), *dev)
     torch.cuda.synchronize()
     assert np.array_equal(got.cpu().numpy().view(np.uint16), aligned.cpu().numpy().view(np.uint16))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,DK,DV,C,CD,taps", [
+    (32, 128, 128, 5, 8192, 3),   # Qwen3.5 GDN layer at the MTP verify width: one fused launch
+    (16, 128, 128, 8, 1024, 4),   # wide verify, 4 taps: fused
+    (4, 8, 12, 5, 64, 2),         # DV % 8 != 0: the two separate launches
+    (4, 128, 128, 5, 20, 3),      # conv_dim % 8 != 0: the two separate launches
+])
+def test_gpu_gdn_rollback_fused_equals_two_calls(cuda, oracle, H, DK, DV, C, CD, taps):
+    """gkv_gdn_rollback_f16 (Engine.rollbackGDN in one call) gives the state
+    and conv tail of gkv_mtp_rollback_f16 and gkv_conv_rollback_f16 bit for
+    bit, in place too, over a batch with every m; the conv tail also matches
+    the oracle bit for bit."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n = 3 * C + 1
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(90 + C, n, H, DK, DV, C, m)
+    rng = np.random.default_rng(91)
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float16)
+    d16, dpre = _dev(torch, s0.astype(np.float16)), _dev(torch, pre)
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    dproj = _dev(torch, proj)
+    want_s = gk.mtp_rollback(m, d16, *dev)
+    want_c = gk.conv_rollback(m, dproj, dpre)
+    got_s, got_c = gk.gdn_rollback(m, d16, *dev, dproj, dpre)
+    torch.cuda.synchronize()
+    u16 = lambda t: t.cpu().numpy().view(np.uint16)
+    assert np.array_equal(u16(got_s), u16(want_s))
+    assert np.array_equal(u16(got_c), u16(want_c))
+    assert np.array_equal(u16(got_c), oracle.conv_rollback_f16(m, proj, pre).view(np.uint16))
+    gk.gdn_rollback(m, d16, *dev, dproj, dpre, out=d16, conv_out=dpre)  # in place
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(d16), u16(want_s)) and np.array_equal(u16(dpre), u16(want_c))
