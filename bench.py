@@ -57,6 +57,10 @@ UNIT = "tok/s"
 # launch, from `ncu --set full` of one launch of the same per-layer workload
 # (64 sequences, 1 layer): 2.2970 GB measured / 2.2898 GB algorithmic.
 NCU_C2_TRAFFIC_PER_ALGO_BYTE = 2.2970 / 2.2898
+# The same for the fused fp16 GDN rollback launch of config 6 (full-size
+# workload, launches 6-8): 2.5335 GB measured / 2.6911 GB algorithmic; the
+# shortfall is written state still dirty in L2 when the launch ends.
+NCU_C6_TRAFFIC_PER_ALGO_BYTE = (845496320 + 843880448 + 844162560) / (895729664 + 897515520 + 897826816)
 
 
 def parse_args():
@@ -854,7 +858,7 @@ def run_config6(args, rank, world, local):
                                f"DK=DV={D}, C={Cw}, conv {CD}x{T} taps; m ~ U{{1..{Cw}}}",
                    "step_bytes": step_bytes, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None,
+                     "peak_kind": kind, "traffic": NCU_C6_TRAFFIC_PER_ALGO_BYTE * bpl if fused else None,
                      "kernel": "gdn_rollback_f16_kernel (state + conv tail)" if fused
                      else "mtp_rollback_fast_f32_kernel",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms},
