@@ -18,6 +18,8 @@
  *     fromCompact(k:v:length:P:kvHeads:dh:) :256-264
  *                                     -> PagePool::fromCompact(pool, k, v, length)
  *   hostFlashDecode(q:pool:G:)        :317-366 -> hostFlashDecode(q, pool, G, ...)
+ *   Engine.rollbackGDN (LLM/src/CoreML/Engine.swift:2678-2716) for a batch
+ *                                     -> rollbackGDN(...), fp16 state and conv tail
  *
  * The Swift PagePool owns its pages; here every PagePool is one sequence of
  * a BlockPool, the device-resident page store of one layer (the geometry
@@ -363,6 +365,20 @@ inline std::vector<float> hostFlashDecode(const std::vector<uint16_t> &q, const 
     if (rc != GKV_OK) throw Error(rc, msg);
     check_cuda(e, "hostFlashDecode staging");
     return out;
+}
+
+/* Engine.rollbackGDN for a batch of (sequence, GDN layer) items with the
+ * reference's fp16 storage: each item's recurrent state [H, DK, DV] rolled
+ * back to its accepted prefix m[i] (MtpRollback.stateAfter) and its conv
+ * tail [convDim, taps] rebuilt (convFromProj), in one launch where the
+ * shapes allow (gkv_gdn_rollback_f16).  m is a host array of nItems values
+ * in 1..C; every other pointer is device memory. */
+inline void rollbackGDN(int32_t nItems, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                        const void *s0, const float *delta, const float *k, const float *gcum, void *stateOut,
+                        int32_t convDim, int32_t taps, const float *proj, const void *pre, void *convOut,
+                        cudaStream_t s = nullptr) {
+    check(gkv_gdn_rollback_f16(nItems, m, H, DK, DV, C, s0, delta, k, gcum, stateOut, convDim, taps, proj, pre,
+                               convOut, s));
 }
 
 }  // namespace gadeon

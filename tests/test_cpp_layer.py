@@ -18,7 +18,11 @@ WARN = ["-Wall", "-Wextra", "-Werror"]
 
 @pytest.mark.parametrize("std", ["c++11", "c++17"])
 def test_header_compiles(std):
-    src = '#include "gadeon_kv.hpp"\nint main() { return gadeon::check(GKV_OK), 0; }\n'
+    src = ('#include "gadeon_kv.hpp"\nint main() { gadeon::check(GKV_OK);\n'
+           '  void (*f)(int32_t, const int32_t *, int32_t, int32_t, int32_t, int32_t, const void *, const float *,\n'
+           '            const float *, const float *, void *, int32_t, int32_t, const float *, const void *, void *,\n'
+           '            cudaStream_t) = gadeon::rollbackGDN;\n'
+           '  return f ? 0 : 1; }\n')
     r = subprocess.run(["g++", f"-std={std}", *WARN, *INC, "-x", "c++", "-", "-fsyntax-only"],
                        input=src, text=True, capture_output=True)
     assert r.returncode == 0, r.stderr
