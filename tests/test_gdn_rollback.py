@@ -400,3 +400,23 @@ def test_gpu_gdn_rollback_fused_equals_two_calls(cuda, oracle, H, DK, DV, C, CD,
     gk.gdn_rollback(m, d16, *dev, dproj, dpre, out=d16, conv_out=dpre)  # in place
     torch.cuda.synchronize()
     assert np.array_equal(u16(d16), u16(want_s)) and np.array_equal(u16(dpre), u16(want_c))
+
+
+@pytest.mark.gpu
+def test_gpu_gdn_rollback_fused_across_launch_chunks(cuda):
+    """2,100 items: the fused call splits at the 2,048 items a parameter
+    block holds; both launches equal the separate calls bit for bit."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n, H, DK, DV, C, CD, taps = 2100, 2, 128, 128, 5, 64, 3
+    m, s0, delta, k, gcum = random_batch(93, n, H, DK, DV, C)
+    rng = np.random.default_rng(94)
+    proj = _dev(torch, rng.standard_normal((n, C, CD)).astype(np.float32))
+    pre = _dev(torch, rng.standard_normal((n, CD, taps)).astype(np.float16))
+    d16 = _dev(torch, s0.astype(np.float16))
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    want_s, want_c = gk.mtp_rollback(m, d16, *dev), gk.conv_rollback(m, proj, pre)
+    got_s, got_c = gk.gdn_rollback(m, d16, *dev, proj, pre)
+    torch.cuda.synchronize()
+    u16 = lambda t: t.cpu().numpy().view(np.uint16)
+    assert np.array_equal(u16(got_s), u16(want_s)) and np.array_equal(u16(got_c), u16(want_c))
