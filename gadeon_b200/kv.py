@@ -465,6 +465,19 @@ class PagePool:
         """clone() (:199-210): shares full pages, copies a partial tail."""
         return PagePool(self.block_pool, self.block_pool.clone(self.seq_id, stream))
 
+    def snapshot(self, stream=None) -> "PagePool":
+        """MetalKVPool.snapshot() (MetalKVPool.swift:102-109): a bookmark that
+        shares the full pages and owns a copy of a partial tail -- clone()."""
+        return self.clone(stream)
+
+    def restore(self, snap: "PagePool", stream=None):
+        """MetalKVPool.restore(_:) (:110-120): this sequence becomes a copy of
+        the snapshot (shared full pages, its own tail copy), so the snapshot
+        stays intact and may be restored again.  The sequence id changes."""
+        new_id = self.block_pool.clone(snap.seq_id, stream)
+        self.block_pool.seq_release(self.seq_id)
+        self.seq_id = new_id
+
     def compact(self, stream=None):
         """compact() (:225-252): (k, v) [kv_heads, length, head_dim] fp16."""
         return self.block_pool.compact(self.seq_id, stream)

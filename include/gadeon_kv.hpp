@@ -14,6 +14,8 @@
  *     compact()              :225-252 -> compact() (host vectors)
  *     tileAt(_:_:_:)         :151-161 -> tileAt(start, count, tileP, K, V)
  *     kPage(_:), vPage(_:)   :80-81   -> kPage(i), vPage(i) (host vectors)
+ *   MetalKVPool.snapshot() / restore(_:) (LLM/src/Metal/MetalKVPool.swift:102-120)
+ *                                     -> snapshot(), restore(snap)
  *     floats32()             :46-62   -> floats32() (host vectors)
  *     fromCompact(k:v:length:P:kvHeads:dh:) :256-264
  *                                     -> PagePool::fromCompact(pool, k, v, length)
@@ -219,6 +221,17 @@ public:
         int32_t dst = -1;
         check(gkv_clone_seq(bp_->handle(), id_, &dst, s));
         return PagePool(*bp_, dst);
+    }
+    /* MetalKVPool.snapshot() (MetalKVPool.swift:102-109) -- clone(). */
+    PagePool snapshot(cudaStream_t s = nullptr) const { return clone(s); }
+    /* MetalKVPool.restore(_:) (:110-120) -- this sequence becomes a copy of
+     * snap (shared full pages, its own tail copy); snap stays intact and may
+     * be restored again.  The sequence id changes. */
+    void restore(const PagePool &snap, cudaStream_t s = nullptr) {
+        int32_t dst = -1;
+        check(gkv_clone_seq(bp_->handle(), snap.id_, &dst, s));
+        gkv_seq_release(bp_->handle(), id_);
+        id_ = dst;
     }
     /* compact() -- (k, v) as [kvHeads, length, dh] fp16 in host vectors.
      * Reads the pool's pool section for this one sequence (gkv_serialize:

@@ -198,7 +198,7 @@ void run() {
 
     // clone() of a partial tail, the clone grows, the original rolls back
     gadeon::PagePool b = a.clone();
-    const int ob = orc_clone(o, oa);
+    int ob = orc_clone(o, oa);
     CHECK(b.seqId() == ob, "clone ids %d vs %d", b.seqId(), ob);
     for (int t = 0; t < 12; ++t) {
         auto k = normal(500 + t, (size_t)KVH * DH), v = normal(600 + t, (size_t)KVH * DH);
@@ -254,6 +254,29 @@ void run() {
                    f.second[0][j] == gadeon::detail::half_to_float(c.second[j]);
         CHECK(same, "floats32() is not compact() widened");
     }
+
+    // MetalKVPool.snapshot / restore: a restore leaves the snapshot intact
+    {
+        gadeon::PagePool snap = b.snapshot();
+        const int osnap = orc_clone(o, ob);
+        CHECK(snap.seqId() == osnap, "snapshot ids %d vs %d", snap.seqId(), osnap);
+        auto k = normal(900, (size_t)KVH * DH), v = normal(901, (size_t)KVH * DH);
+        Dev<uint16_t> dk(k), dv(v);
+        b.append(dk.p, dv.p);
+        const int32_t one = 1;
+        orc_append(o, 1, &ob, &one, k.data(), v.data());
+        const int old = b.seqId();
+        b.restore(snap);
+        const int nb = orc_clone(o, osnap);
+        orc_seq_release(o, old);
+        CHECK(b.seqId() == nb, "restore ids %d vs %d", b.seqId(), nb);
+        ob = nb;
+        check_state(b, o, nb, "after restore");
+        check_state(snap, o, osnap, "snapshot after restore");
+        check_free_list(bp, o, "after restore");
+        orc_seq_release(o, osnap);  // snap's destructor releases it on the GPU side
+    }
+    check_free_list(bp, o, "after the snapshot is released");
 
     // compact() -> fromCompact round trip
     auto kv = b.compact();

@@ -406,3 +406,36 @@ def test_tile_at_carry_windows(cuda, oracle, tile_p):
         assert e.value.code == code, (start, count, tp)
     cuda.cuda.synchronize()
     pr.check_state()
+
+
+def test_snapshot_restore_twice(cuda, oracle):
+    """MetalKVPool.snapshot / restore (MetalKVPool.swift:102-120) through the
+    PagePool view: restore makes the live sequence a copy of the snapshot
+    with its own tail, so appends after a restore leave the snapshot intact
+    and it restores again to the same state; cache state bit-exact with the
+    oracle doing clone + release, attention within tolerance."""
+    from gadeon_b200 import PagePool
+    pr = Pair(cuda, oracle, kvh=2, dh=128, P=16, num_pages=64, seed=33)
+    s = pr.new_seq()
+    pr.seed(s, 37)  # partial tail page
+    live = PagePool(pr.gpu, s)
+    snap = live.snapshot()
+    assert snap.seq_id == pr.orc.clone(s)
+    pr.seqs.append(snap.seq_id)
+    for extra in (20, 5):
+        pr.append([live.seq_id], [extra])
+        pr.check_state()
+        old = live.seq_id
+        live.restore(snap)
+        nid = pr.orc.clone(snap.seq_id)
+        assert pr.orc.seq_release(old) == 0
+        assert live.seq_id == nid
+        pr.seqs = [x for x in pr.seqs if x != old] + [nid]
+        assert live.length == 37
+        pr.check_state()
+        got, want = pr.attend([live.seq_id, snap.seq_id], 1, 4)
+        assert_attn_close(got, want, f"after restore (+{extra})")
+        q1 = oracle.normal_f16(6, extra, (1, 1, 8, 128))
+        same = pr.gpu.attend([live.seq_id, snap.seq_id], 1, 4, dev_f16(cuda, np.concatenate([q1, q1])))
+        same = same.cpu().numpy()
+        assert np.array_equal(same[0], same[1])  # equal rows in the pages, equal bits out
