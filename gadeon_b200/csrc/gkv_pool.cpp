@@ -307,11 +307,35 @@ bool fused_tails(const std::vector<gkv::TouchedPage> &pages, int32_t n_seqs, std
     return true;
 }
 
+// True when an entry writes in place into a page that an earlier entry of
+// the same batch copies (two sequences sharing one partial tail page, both
+// appending: the first takes a copy, the last writes the original).  One CTA
+// per touched page would race the copy's reads against those writes.
+bool copy_source_written(const std::vector<gkv::TouchedPage> &pages) {
+    std::vector<int32_t> srcs;
+    for (const gkv::TouchedPage &tp : pages)
+        if (tp.src_pid >= 0) srcs.push_back(tp.src_pid);
+    if (srcs.empty()) return false;
+    std::sort(srcs.begin(), srcs.end());
+    for (const gkv::TouchedPage &tp : pages)
+        if (tp.src_pid < 0 && std::binary_search(srcs.begin(), srcs.end(), tp.pid)) return true;
+    return false;
+}
+
 // Uploads entries+pages and launches the append kernel.
 int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
                    const std::vector<gkv::TouchedPage> &pages, const void *k, const void *v,
                    int head_major, cudaStream_t st) {
     if (pages.empty()) return GKV_OK;
+    if (copy_source_written(pages)) {
+        // the copies (and their entries' rows on the copies) first, the
+        // in-place writes after them in stream order; every touched page is
+        // independent of the others, so the split changes nothing else
+        std::vector<gkv::TouchedPage> copies, rest;
+        for (const gkv::TouchedPage &tp : pages) (tp.src_pid >= 0 ? copies : rest).push_back(tp);
+        const int rc = enqueue_append(pool, entries, copies, k, v, head_major, st);
+        return rc ? rc : enqueue_append(pool, entries, rest, k, v, head_major, st);
+    }
     const size_t eb = entries.size() * sizeof(gkv::AppendEntry);
     const size_t pb = pages.size() * sizeof(gkv::TouchedPage);
     // small appends (decode rows, MTP drafts) carry the descriptor in the

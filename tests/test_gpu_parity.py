@@ -439,3 +439,53 @@ def test_snapshot_restore_twice(cuda, oracle):
         same = pr.gpu.attend([live.seq_id, snap.seq_id], 1, 4, dev_f16(cuda, np.concatenate([q1, q1])))
         same = same.cpu().numpy()
         assert np.array_equal(same[0], same[1])  # equal rows in the pages, equal bits out
+
+
+@pytest.mark.parametrize("lens", [(11, 9), (4, 30)])
+def test_shared_tail_copy_and_in_place_write_in_one_batch(cuda, oracle, lens):
+    """Two sequences share one partially filled tail page and both append in
+    the same batch: the first takes a copy-on-write copy of the whole page
+    (PagePool.clone's duplicate, PagedAttention.swift:199-210), the last then
+    owns the page and writes it in place.  The copy must hold the page as it
+    was before that write, as the reference's sequential order gives it --
+    (11, 9): the writer's slot is a valid row of the copier; (4, 30): only a
+    stale row.  24 such pairs in one batch; state bit-exact, attention within
+    tolerance."""
+    P, G = 32, 2
+    pr = Pair(cuda, oracle, kvh=2, dh=128, P=P, num_pages=400, max_seqs=96, seed=44)
+    ids, new_len = [], []
+    for _ in range(24):
+        a = pr.new_seq()
+        pr.seed(a, 40)  # a full first page and a partial second one
+        b = pr.gpu.clone(a)
+        assert pr.orc.clone(a) == b
+        pr.seqs.append(b)
+        ids += [a, b]
+        new_len += list(lens)
+    pr.truncate(ids, new_len)  # both back into the shared first page
+    pr.check_state()
+    for s in ids:
+        assert pr.gpu.page_refcount(int(pr.gpu.export_table(s)[0])) == 2
+    k, v = pr.rows(len(ids))
+    q = oracle.normal_f16(45, lens[0], (len(ids), 1, 2 * G, 128))
+    got = pr.gpu.append_attend(ids, 1, G, dev_f16(cuda, k), dev_f16(cuda, v), dev_f16(cuda, q)).cpu().numpy()
+    assert pr.orc.append(ids, [1] * len(ids), k, v) == 0
+    want = pr.orc.attend_causal(ids, 1, q, G, 128 ** -0.5)
+    pr.check_state()
+    assert_attn_close(got, want, f"shared tail {lens}")
+    # fresh shared pairs, then a plain batched append of 3 rows each (with
+    # lens (4, 30) the writer also crosses into a new page)
+    batch, batch_len = [], []
+    for _ in range(12):
+        a = pr.new_seq()
+        pr.seed(a, 40)
+        b = pr.gpu.clone(a)
+        assert pr.orc.clone(a) == b
+        pr.seqs.append(b)
+        batch += [a, b]
+        batch_len += list(lens)
+    pr.truncate(batch, batch_len)
+    pr.append(batch, [3] * len(batch))
+    pr.check_state()
+    got, want = pr.attend(batch, 3, G)
+    assert_attn_close(got, want, f"shared tail {lens}, 3-row append")

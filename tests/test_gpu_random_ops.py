@@ -26,7 +26,9 @@ WEIGHTS = np.array([1.0, 3.0, 4.0, 1.5, 0.5, 2.0, 1.0, 0.7, 1.0, 1.5])
 
 
 @pytest.mark.parametrize("seed,P,dh,num_pages,grow", [(11, 8, 128, 260, 3), (12, 16, 256, 200, 3), (13, 16, 128, 120, 3),
-                                                     (14, 16, 128, 48, 10)])
+                                                     (14, 16, 128, 48, 10),
+                                                     # two sequences sharing a partial tail page append in one batch
+                                                     (1010, 32, 128, 152, 2)])
 def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow):
     """grow: an append adds up to grow * P rows per sequence (10: the pool
     runs out now and then, and both sides must refuse the same appends)."""
@@ -117,7 +119,13 @@ def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow):
             if len(live) >= 10:
                 continue
             src = int(rng.choice(live))
-            c = pr.gpu.clone(src)
+            try:
+                c = pr.gpu.clone(src)
+            except GkvError as e:  # no free page for the tail copy: refused on both sides
+                assert e.code == GKV_ERR_NO_PAGES, e
+                assert pr.orc.clone(src) < 0, "oracle cloned where the GPU refused"
+                refused += 1
+                continue
             assert pr.orc.clone(src) == c
             pr.seqs.append(c)
             live.append(c)
