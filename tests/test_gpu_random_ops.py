@@ -25,18 +25,20 @@ OPS = ["new", "append", "decode", "verify", "chunk", "truncate", "clone", "relea
 WEIGHTS = np.array([1.0, 3.0, 4.0, 1.5, 0.5, 2.0, 1.0, 0.7, 1.0, 1.5])
 
 
-@pytest.mark.parametrize("seed,P,dh,num_pages,grow", [(11, 8, 128, 260, 3), (12, 16, 256, 200, 3), (13, 16, 128, 120, 3),
-                                                     (14, 16, 128, 48, 10),
-                                                     # two sequences sharing a partial tail page append in one batch
-                                                     (1010, 32, 128, 152, 2)])
-def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow):
+@pytest.mark.parametrize("seed,P,dh,num_pages,grow,kvh,G", [
+    (11, 8, 128, 260, 3, 2, 2), (12, 16, 256, 200, 3, 2, 2), (13, 16, 128, 120, 3, 2, 2),
+    (14, 16, 128, 48, 10, 2, 2),
+    (1010, 32, 128, 152, 2, 2, 2),  # two sequences sharing a partial tail page append in one batch
+    (15, 16, 256, 220, 3, 4, 4),    # config 3's heads: verify rows fill the 16-row tile
+])
+def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow, kvh, G):
     """grow: an append adds up to grow * P rows per sequence (10: the pool
     runs out now and then, and both sides must refuse the same appends)."""
     from gadeon_b200 import GKV_ERR_NO_PAGES, GkvError
     torch = cuda
     rng = np.random.default_rng(seed)
-    kvh, G = 2, 2
-    pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=num_pages, max_seqs=16, seed=seed)
+    # block-table rows longer than the pool, so running out of pages is the only refusal
+    pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=num_pages, max_seqs=16, max_pps=2 * num_pages, seed=seed)
     live = []
     counts = {op: 0 for op in OPS}
     refused = 0
