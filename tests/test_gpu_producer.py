@@ -222,3 +222,50 @@ def test_attn_step_rejects_bad_arguments(cuda, oracle):
     with pytest.raises(gk.GkvError) as e:
         small.attn_step([t], 4, f(1, 8, 128), f(1, 2, 64), f(1, 2, 64), f(64), f(64), f(1, 16), f(1, 16))
     assert e.value.code == gk.GKV_ERR_UNSUPPORTED
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed,P,dh,G,n_rot", [(61, 16, 256, 4, 64), (62, 8, 128, 2, 128), (63, 32, 128, 4, 32)])
+def test_attn_step_random_mix(cuda, oracle, seed, P, dh, G, n_rot):
+    """gkv_attn_step interleaved with the operations that reshape the cache
+    -- plain appends, truncates into shared pages, clones, releases -- so
+    that steps meet fresh pages, page boundaries and copy-on-write tails
+    (the unfused route) in every combination; state and outputs checked
+    after every step against the oracle's producer + append + decode."""
+    from test_gpu_parity import dev_f16
+    sp = StepPair(cuda, oracle, kvh=2, dh=dh, P=P, num_pages=160, G=G, n_rot=n_rot, seed=seed)
+    pr, rng = sp.pr, np.random.default_rng(seed)
+    live = [pr.new_seq() for _ in range(3)]
+    pr.append(live, [int(x) for x in rng.integers(1, 3 * P, size=3)])
+    ops = ["step", "step", "step", "append", "truncate", "clone", "release", "new"]
+    for i in range(60):
+        op = ops[int(rng.integers(len(ops)))]
+        if op == "step":
+            ids = [int(x) for x in rng.choice(live, size=int(rng.integers(1, len(live) + 1)), replace=False)]
+            got, want = sp.step(ids)
+            assert_attn_close(got, want, f"step {i}")
+        elif op == "append":
+            ids = [int(x) for x in rng.choice(live, size=int(rng.integers(1, len(live) + 1)), replace=False)]
+            pr.append(ids, [int(x) for x in rng.integers(0, 2 * P, size=len(ids))])
+        elif op == "truncate":
+            ids = [int(x) for x in rng.choice(live, size=int(rng.integers(1, len(live) + 1)), replace=False)]
+            pr.truncate(ids, [int(rng.integers(1, pr.gpu.length(s) + 1)) if pr.gpu.length(s) else 0 for s in ids])
+        elif op == "clone" and len(live) < 8:
+            src = int(rng.choice(live))
+            c = pr.gpu.clone(src)
+            assert pr.orc.clone(src) == c
+            pr.seqs.append(c)
+            live.append(c)
+        elif op == "release" and len(live) > 2:
+            s = int(rng.choice(live))
+            pr.gpu.seq_release(s)
+            assert pr.orc.seq_release(s) == 0
+            live.remove(s)
+            pr.seqs.remove(s)
+        elif op == "new" and len(live) < 8:
+            live.append(pr.new_seq())
+        if i % 6 == 5:
+            sp.check_state()
+        else:
+            pr.check_state(pages=False)
+    sp.check_state()
