@@ -157,3 +157,39 @@ def test_random_operation_mix(cuda, oracle, seed, P, dh, num_pages, grow, kvh, G
     assert counts["decode"] > 10 and counts["truncate"] > 5 and counts["clone"] > 0, (counts, refused)
     if grow >= 10:
         assert refused > 0, "the small pool never ran out"
+
+
+def test_random_large_batches(cuda, oracle):
+    """Batches of 129-300 sequences -- past the 128 whose descriptors ride in
+    the kernel parameter block, so every call uploads its descriptor through
+    the pool's staging ring -- in a seeded mix of fused decode, fused verify,
+    appends, truncates and clones; state bit-exact, outputs in tolerance."""
+    torch = cuda
+    seed, P, dh, G, kvh = 5001, 16, 128, 2, 2
+    rng = np.random.default_rng(seed)
+    pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=9000, max_seqs=400, max_pps=2000, seed=seed)
+    live = [pr.new_seq() for _ in range(300)]
+    pr.append(live, [int(x) for x in rng.integers(1, 200, size=len(live))])
+    for step in range(20):
+        op = rng.choice(["decode", "fverify", "append", "truncate", "clone"], p=[0.35, 0.25, 0.15, 0.15, 0.10])
+        ids = [int(x) for x in rng.choice(live, size=int(rng.integers(129, len(live) + 1)), replace=False)]
+        if op in ("decode", "fverify"):
+            n_q = 1 if op == "decode" else int(rng.integers(2, 5))
+            k, v = pr.rows(len(ids) * n_q)
+            q = oracle.normal_f16(seed, step, (len(ids), n_q, kvh * G, dh))
+            got = pr.gpu.append_attend(ids, n_q, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+            assert pr.orc.append(ids, [n_q] * len(ids), k, v) == 0
+            want = pr.orc.attend_causal(ids, n_q, q, G, dh ** -0.5, n_threads=8)
+            assert_attn_close(got.cpu().numpy(), want, f"step {step} {op}")
+        elif op == "append":
+            pr.append(ids, [int(x) for x in rng.integers(0, 3 * P, size=len(ids))])
+        elif op == "truncate":
+            pr.truncate(ids, [int(rng.integers(1, pr.gpu.length(s) + 1)) for s in ids])
+        elif op == "clone":
+            for s in ids[:5]:
+                c = pr.gpu.clone(s)
+                assert pr.orc.clone(s) == c
+                pr.seqs.append(c)
+                live.append(c)
+        pr.check_state(pages=(step % 10 == 9))
+    pr.check_state(pages=True)
