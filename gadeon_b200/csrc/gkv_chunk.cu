@@ -45,6 +45,7 @@
 // the K/V bytes per FLOP.  The even CTA issues every MMA; its commits arrive
 // on both CTAs' barriers, the odd CTA's loads complete on the even CTA's
 // barriers, and the odd CTA's softmax warps arrive remotely on them.
+#include <atomic>
 #include <cuda_fp16.h>
 
 #include "gkv_kernels.cuh"
@@ -511,13 +512,13 @@ cudaError_t launch_chunk_t(const ChunkParams &p, const CUtensorMap *tk, const CU
                            cudaStream_t s) {
     auto kern = chunk_kernel<DH, PAIR>;
     constexpr int smem = ChunkCfg<DH, PAIR>::SMEM_ALLOC;
-    static bool configured[64] = {};
+    static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    if (dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        if (dev < 64) configured[dev].store(true, std::memory_order_release);
     }
     if constexpr (PAIR) {
         cudaLaunchConfig_t cfg = {};

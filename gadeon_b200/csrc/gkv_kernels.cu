@@ -33,6 +33,7 @@
 //     finish the item (atomic counter, no spinning) merges them with the
 //     same online-softmax rule as pagedFlashBatched's host merge
 //     (PagedAttention.swift:396-409).
+#include <atomic>
 #include <cuda_fp16.h>
 
 #include "gkv_kernels.cuh"
@@ -811,15 +812,15 @@ template <int DH, bool TMA, bool FUSED = false, bool PROD = false>
 cudaError_t launch_attend_t(const AttendParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                             int grid, cudaStream_t s, const InlineDesc *desc) {
     auto kern = attend_kernel<DH, TMA, FUSED, PROD>;
-    static bool configured[64] = {};
+    static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
     static const InlineDesc empty_desc{};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    if (dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Cfg<DH>::SMEM_ALLOC);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        if (dev < 64) configured[dev].store(true, std::memory_order_release);
     }
     // Programmatic stream serialization: the launch may begin while the
     // previous kernel of the stream drains; the kernel's grid_dep_wait()
