@@ -97,3 +97,37 @@ def test_zero_row_entries_in_a_batch(cuda, oracle):
     pr.check_state()
     got, want = pr.attend([ids[0], ids[1], ids[2], ids[3]], 1, 2)
     assert_attn_close(got, want, "after zero-row entries")
+
+
+def test_pools_driven_from_threads(cuda, oracle):
+    """Four host threads, each with its own pool, seeding, appending and
+    running fused decode steps at the same time (the library's host code
+    runs concurrently: ctypes releases the interpreter lock); every pool's
+    state and outputs match its own oracle."""
+    import threading
+    errors = []
+
+    def worker(t):
+        try:
+            pr = Pair(cuda, oracle, kvh=2, dh=128, P=16, num_pages=120, seed=300 + t)
+            ids = [pr.new_seq() for _ in range(4)]
+            for s, n in zip(ids, (17, 33, 64, 90)):
+                pr.seed(s, n)
+            for step in range(12):
+                k, v = pr.rows(len(ids))
+                q = oracle.normal_f16(300 + t, step, (len(ids), 1, 8, 128))
+                got = pr.gpu.append_attend(ids, 1, 4, dev_f16(cuda, k), dev_f16(cuda, v), dev_f16(cuda, q))
+                assert pr.orc.append(ids, [1] * len(ids), k, v) == 0
+                want = pr.orc.attend_causal(ids, 1, q, 4, 128 ** -0.5)
+                assert_attn_close(got.cpu().numpy(), want, f"thread {t} step {step}")
+            pr.check_state()
+        except BaseException as e:  # reported by the main thread
+            errors.append((t, e))
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(4)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not any(th.is_alive() for th in threads), "a worker did not finish"
+    assert not errors, errors
