@@ -370,6 +370,8 @@ def test_gpu_f16_unaligned_state_takes_the_elementwise_kernel(cuda, oracle):
 @pytest.mark.parametrize("H,DK,DV,C,CD,taps", [
     (32, 128, 128, 5, 8192, 3),   # Qwen3.5 GDN layer at the MTP verify width: one fused launch
     (16, 128, 128, 8, 1024, 4),   # wide verify, 4 taps: fused
+    (4, 128, 128, 5, 256, 1),     # 1 tap, a conv block a quarter full: fused
+    (4, 64, 64, 3, 136, 2),       # 2 taps, 17 channel groups: fused
     (4, 8, 12, 5, 64, 2),         # DV % 8 != 0: the two separate launches
     (4, 128, 128, 5, 20, 3),      # conv_dim % 8 != 0: the two separate launches
 ])
