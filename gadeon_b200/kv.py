@@ -474,6 +474,8 @@ class PagePool:
         """MetalKVPool.restore(_:) (:110-120): this sequence becomes a copy of
         the snapshot (shared full pages, its own tail copy), so the snapshot
         stays intact and may be restored again.  The sequence id changes."""
+        if snap.block_pool is not self.block_pool:
+            raise GkvError(GKV_ERR_INVALID, "restore: the snapshot belongs to another BlockPool")
         new_id = self.block_pool.clone(snap.seq_id, stream)
         self.block_pool.seq_release(self.seq_id)
         self.seq_id = new_id

@@ -228,6 +228,7 @@ public:
      * snap (shared full pages, its own tail copy); snap stays intact and may
      * be restored again.  The sequence id changes. */
     void restore(const PagePool &snap, cudaStream_t s = nullptr) {
+        if (snap.bp_ != bp_) throw Error(GKV_ERR_INVALID, "restore: the snapshot belongs to another BlockPool");
         int32_t dst = -1;
         check(gkv_clone_seq(bp_->handle(), snap.id_, &dst, s));
         gkv_seq_release(bp_->handle(), id_);
