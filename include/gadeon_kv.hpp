@@ -348,8 +348,10 @@ inline void hostFlashDecode(const void *q, const PagePool &pool, int G, float *o
     check(gkv_attend(pool.blockPool().handle(), 1, &id, 1, G, q, out, (float)std::pow((double)pool.dh(), -0.5), s));
 }
 
-/* The Swift's value-returning form: host q in, host [Float] out (stages
- * through device memory of the pool's device; waits for the result). */
+/* The Swift's value-returning form: host q in, host [Float] out.  A
+ * convenience: it allocates device staging on every call and waits for the
+ * result; a decode loop keeps its own device or page-locked buffers and
+ * calls the pointer form above. */
 inline std::vector<float> hostFlashDecode(const std::vector<uint16_t> &q, const PagePool &pool, int G) {
     const size_t nq = (size_t)pool.kvHeads() * (size_t)G * (size_t)pool.dh();
     if (G <= 0 || q.size() != nq) throw Error(GKV_ERR_INVALID, "hostFlashDecode: q must hold kvHeads*G*dh values");
