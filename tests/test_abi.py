@@ -72,3 +72,30 @@ def test_null_arguments(lib):
     assert lib.gkv_pool_create(None, None) == 1
     assert lib.gkv_seq_create(None, None) == 1
     assert lib.gkv_pool_destroy(None) == 0
+
+
+def test_binding_refuses_bad_arguments_before_any_device_work(lib):
+    """The Python layer's checks run before anything reaches the C ABI or a
+    device: wrong shapes or dtypes, an m array of the wrong length, and
+    pageable host tensors (a kernel could not reach them) are refused with
+    GKV_ERR_INVALID -- here on a machine without a GPU."""
+    import torch
+    import gadeon_b200 as gk
+    n, H, D, C = 2, 4, 8, 3
+    s0 = torch.zeros((n, H, D, D), dtype=torch.float16)
+    delta, k = torch.zeros((n, H, C, D)), torch.zeros((n, H, C, D))
+    gcum = torch.zeros((n, H, C))
+    proj, pre = torch.zeros((n, C, 16)), torch.zeros((n, 16, 3), dtype=torch.float16)
+    bad = [
+        lambda: gk.mtp_rollback([1, 2], s0, delta[:, :, :2], k, gcum),        # delta rows != C
+        lambda: gk.mtp_rollback([1, 2], s0, delta, k.double(), gcum),         # k not fp32
+        lambda: gk.mtp_rollback([1], s0, delta, k, gcum),                     # one m for two items
+        lambda: gk.mtp_rollback([1, 2], s0, delta, k, gcum),                  # pageable host memory
+        lambda: gk.gdn_rollback([1, 2], s0, delta, k, gcum, proj[:, :2], pre),  # proj rows != C
+        lambda: gk.gdn_rollback([1, 2], s0.float(), delta, k, gcum, proj, pre),  # fused call is fp16 only
+        lambda: gk.conv_rollback([1, 2], proj, pre.float().double()),         # pre of no storage type
+    ]
+    for i, call in enumerate(bad):
+        with pytest.raises(gk.GkvError) as e:
+            call()
+        assert e.value.code == gk.GKV_ERR_INVALID, i
