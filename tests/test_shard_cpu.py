@@ -113,3 +113,26 @@ def test_dead_rank_is_detected_by_the_collective():
     res = _run(2, fail_rank=1)
     assert res[1][0] == "error"
     assert res[0][0] == "error", res  # the gather fails instead of hanging
+
+
+def test_partition_properties():
+    """For random context lists: every sequence lands in exactly one part;
+    the capped partition gives every part exactly per_part sequences; the
+    LPT partition keeps the heaviest part within the list-scheduling bound
+    (mean load + the largest context)."""
+    hypothesis = pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    from gadeon_b200.workload import capped_partition, lpt_partition
+
+    @settings(max_examples=200, deadline=None)
+    @given(parts=st.integers(1, 8), per=st.integers(1, 12), data=st.data())
+    def check(parts, per, data):
+        tokens = data.draw(st.lists(st.integers(0, 131072), min_size=parts * per, max_size=parts * per))
+        for split in (capped_partition(tokens, parts, per), lpt_partition(tokens, parts)):
+            assert sorted(i for p in split for i in p) == list(range(len(tokens)))
+            assert len(split) == parts and all(p == sorted(p) for p in split)
+        assert all(len(p) == per for p in capped_partition(tokens, parts, per))
+        loads = [sum(tokens[i] for i in p) for p in lpt_partition(tokens, parts)]
+        assert max(loads) <= sum(tokens) / parts + max(tokens) + 1e-9
+
+    check()
