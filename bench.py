@@ -808,25 +808,19 @@ def run_config6(args, rank, world, local):
     ms_acc = rng.integers(1, Cw + 1, size=(W + K, n)).astype(np.int32)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
 
-    fused = not args.gdn_f32  # fp16 storage: state and conv tail in one launch (gkv_gdn_rollback_f16)
-
     def step(i, ti):
+        # the state and conv tail of every item in one launch
+        # (gkv_gdn_rollback_f16, or gkv_gdn_rollback with --gdn-f32)
         if ti is not None:
             ev[ti][0].record()
-        if fused:
-            gk.gdn_rollback(ms_acc[i], s0, delta, kk, gcum, proj, pre, out=out, conv_out=conv)
-        else:
-            gk.mtp_rollback(ms_acc[i], s0, delta, kk, gcum, out=out)
+        gk.gdn_rollback(ms_acc[i], s0, delta, kk, gcum, proj, pre, out=out, conv_out=conv)
         if ti is not None:
             ev[ti][1].record()
-        if not fused:
-            gk.conv_rollback(ms_acc[i], proj, pre, out=conv)
 
     ms, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
-    # bytes of the timed launch: the state rollback, plus the conv tail when fused
-    bpl = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)[: 2 if fused else 1]) for i in range(K))
     step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)) for i in range(K))
+    bpl = step_bytes  # one launch per step
     hbm, kind = peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -858,12 +852,11 @@ def run_config6(args, rank, world, local):
                                f"DK=DV={D}, C={Cw}, conv {CD}x{T} taps; m ~ U{{1..{Cw}}}",
                    "step_bytes": step_bytes, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": NCU_C6_TRAFFIC_PER_ALGO_BYTE * bpl if fused else None,
-                     "kernel": "gdn_rollback_f16_kernel (state + conv tail)" if fused
-                     else "mtp_rollback_fast_f32_kernel",
+                     "peak_kind": kind, "traffic": None if args.gdn_f32 else NCU_C6_TRAFFIC_PER_ALGO_BYTE * bpl,
+                     "kernel": "gdn_rollback_%s_kernel (state + conv tail)" % ("f32" if args.gdn_f32 else "f16"),
                      "bytes_per_launch": bpl, "launch_ms": launch_ms},
         "step_gbs": step_bytes / (ms * 1e-3) / 1e9,
-        "cpu_baseline": cpu, "e2e": None, "gpu_launches": K * (1 if fused else 2), "clocks": clk}), flush=True)
+        "cpu_baseline": cpu, "e2e": None, "gpu_launches": K, "clocks": clk}), flush=True)
 
 
 def run_config7(args, rank, world, local):
@@ -937,11 +930,7 @@ def run_config7(args, rank, world, local):
         lens = lens + m
         main.truncate(mids, lens)
         mm = np.repeat(m, g.layers).astype(np.int32)
-        if args.gdn_f32:
-            gk.mtp_rollback(mm, s0, gd, gk_, gc, out=s_out)
-            gk.conv_rollback(mm, proj, pre, out=conv)
-        else:  # fp16 storage: state and conv tail in one launch
-            gk.gdn_rollback(mm, s0, gd, gk_, gc, proj, pre, out=s_out, conv_out=conv)
+        gk.gdn_rollback(mm, s0, gd, gk_, gc, proj, pre, out=s_out, conv_out=conv)  # state + conv tail, one launch
         drafter.rewind_append(dids, base, m, k4[: int(m.sum())], k4[: int(m.sum())])
         dlens = base + m
 
@@ -971,7 +960,7 @@ def run_config7(args, rank, world, local):
                      "kernel": "attend_kernel<256,TMA> (3 drafter decodes + 1 verify per cycle, fused appends)",
                      "bytes_per_cycle": sum(att_bytes) / K, "attend_ms_per_cycle": att_ms / K},
         "cycle_gbs": cycle_bytes / (ms * 1e-3) / 1e9,
-        "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 1 + (2 if args.gdn_f32 else 1) + 1), "clocks": clk}), flush=True)
+        "cpu_baseline": None, "e2e": None, "gpu_launches": K * (n_draft + 1 + 1 + 1), "clocks": clk}), flush=True)
 
 
 def _json_only_stdout():

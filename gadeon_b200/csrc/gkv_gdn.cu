@@ -245,10 +245,10 @@ __device__ __forceinline__ void conv_slice(const ConvParams<T> &p, int item, int
     for (int v = 0; v < NW / 4; ++v) __stcs(dst + v, make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]));
 }
 
-template <typename T, int TAPS>
+template <typename T, int TAPS, int THREADS = kConvVecThreads>
 __device__ __forceinline__ void conv_vec_block(const ConvParams<T> &p, int item, int bx) {
     static_assert((8 * TAPS / Words<T>::PER) % 4 == 0, "whole 16-byte vectors");
-    const int c0 = (bx * kConvVecThreads + threadIdx.x) * 8;
+    const int c0 = (bx * THREADS + threadIdx.x) * 8;
     if (c0 >= p.CD) return;
     const int m = p.m[item];
     const int64_t tail = ((int64_t)item * p.CD + c0) * TAPS;
@@ -289,10 +289,9 @@ constexpr int kF16Threads = 128;
 constexpr int kF16NarrowC = 5;              // verify width of the MTP cycle (token + 4 drafts)
 
 // fp32 state: thread = one float4 column group (64 registers, 4 CTAs/SM).
-__global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_f32_kernel(const __grid_constant__ RollbackParams<float> p) {
+__device__ __forceinline__ void state_fast_f32_block(const RollbackParams<float> &p, int hs) {
     __shared__ float kw[kFastC][kFastDK];
     __shared__ float eM_s;
-    const int hs = blockIdx.x;
     const int m = p.m[hs / p.H];
     const int ncg = p.DV >> 2;
     const int rstride = kRollThreads / ncg;
@@ -352,6 +351,10 @@ __global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_f32_kernel(con
             if (i < p.DK) s[u] = __ldcs(s4 + (int64_t)i * ncg + cg);
         }
     }
+}
+
+__global__ void __launch_bounds__(kRollThreads) mtp_rollback_fast_f32_kernel(const __grid_constant__ RollbackParams<float> p) {
+    state_fast_f32_block(p, blockIdx.x);
 }
 
 // The stream loop of the fp16 kernel for a compile-time accepted length M:
@@ -465,20 +468,32 @@ __global__ void __launch_bounds__(THREADS) mtp_rollback_fast_kernel(const __grid
 // the rest one 1,024-channel slice of an item's conv tail each.  The two
 // parts touch disjoint memory, so the conv blocks, dispatched last, fill the
 // state stream's tail instead of running as a launch of their own.
+template <typename T>
 struct GdnParams {
-    RollbackParams<__half> s;
-    ConvParams<__half> c;
+    RollbackParams<T> s;
+    ConvParams<T> c;
     int32_t state_blocks, conv_bx;
 };
-static_assert(kConvVecThreads == kF16Threads, "one block size for both parts");
 
 template <int MAXC, int TAPS>
-__global__ void __launch_bounds__(kF16Threads) gdn_rollback_f16_kernel(const __grid_constant__ GdnParams p) {
+__global__ void __launch_bounds__(kF16Threads) gdn_rollback_f16_kernel(const __grid_constant__ GdnParams<__half> p) {
     if ((int)blockIdx.x < p.state_blocks) {
         state_fast_block<__half, kF16Cols, kF16Unroll, MAXC, kF16Threads>(p.s, blockIdx.x);
     } else {
         const int b = (int)blockIdx.x - p.state_blocks;
-        conv_vec_block<__half, TAPS>(p.c, b / p.conv_bx, b % p.conv_bx);
+        conv_vec_block<__half, TAPS, kF16Threads>(p.c, b / p.conv_bx, b % p.conv_bx);
+    }
+}
+
+// fp32 storage: 256-thread blocks, the fp32 state body, conv slices of 2,048
+// channels.
+template <int TAPS>
+__global__ void __launch_bounds__(kRollThreads) gdn_rollback_f32_kernel(const __grid_constant__ GdnParams<float> p) {
+    if ((int)blockIdx.x < p.state_blocks) {
+        state_fast_f32_block(p.s, blockIdx.x);
+    } else {
+        const int b = (int)blockIdx.x - p.state_blocks;
+        conv_vec_block<float, TAPS, kRollThreads>(p.c, b / p.conv_bx, b % p.conv_bx);
     }
 }
 
@@ -634,31 +649,34 @@ int conv_rollback_impl(int32_t n_items, const int32_t *m, int32_t conv_dim, int3
 
 // State and conv tail of every item in one launch when both take their
 // vector kernels; otherwise the two launches of the separate entry points.
-int gdn_rollback_f16_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
-                          const __half *s0, const float *delta, const float *k, const float *gcum, __half *s_out,
-                          int32_t conv_dim, int32_t taps, const float *proj, const __half *pre, __half *conv_out,
-                          void *stream) {
+template <typename T>
+int gdn_rollback_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C, const T *s0,
+                      const float *delta, const float *k, const float *gcum, T *s_out, int32_t conv_dim,
+                      int32_t taps, const float *proj, const T *pre, T *conv_out, void *stream) {
+    constexpr bool F16 = sizeof(T) == 2;
+    constexpr int THREADS = F16 ? kF16Threads : kRollThreads;  // the state kernel's block size
     bool svec = false, sfast = false, cvec = false;
-    if (const int rc = check_state_args<__half>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, &svec, &sfast))
+    if (const int rc = check_state_args<T>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, &svec, &sfast))
         return rc;
-    if (const int rc = check_conv_args<__half>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, &cvec)) return rc;
+    if (const int rc = check_conv_args<T>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, &cvec)) return rc;
     if (n_items == 0) return GKV_OK;
     if (!sfast || !cvec) {
-        if (const int rc = mtp_rollback_impl<__half>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, stream))
+        if (const int rc = mtp_rollback_impl<T>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, s_out, stream))
             return rc;
-        return conv_rollback_impl<__half>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, stream);
+        return conv_rollback_impl<T>(n_items, m, conv_dim, taps, C, proj, pre, conv_out, stream);
     }
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int32_t conv_bx = (conv_dim / 8 + kConvVecThreads - 1) / kConvVecThreads;
+    const int32_t conv_bx = (conv_dim / 8 + THREADS - 1) / THREADS;
     const bool narrow = C <= kF16NarrowC;
     for (int32_t first = 0; first < n_items; first += kMaxItemsPerLaunch) {
         const int32_t cnt = n_items - first < kMaxItemsPerLaunch ? n_items - first : kMaxItemsPerLaunch;
-        GdnParams p{};
-        fill_state_params<__half>(p.s, first, cnt, m, H, DK, DV, C, s0, delta, k, gcum, s_out);
-        fill_conv_params<__half>(p.c, first, cnt, m, conv_dim, taps, C, proj, pre, conv_out);
+        GdnParams<T> p{};
+        fill_state_params<T>(p.s, first, cnt, m, H, DK, DV, C, s0, delta, k, gcum, s_out);
+        fill_conv_params<T>(p.c, first, cnt, m, conv_dim, taps, C, proj, pre, conv_out);
         p.state_blocks = cnt * H;
         p.conv_bx = conv_bx;
         const unsigned blocks = (unsigned)((int64_t)cnt * H + (int64_t)cnt * conv_bx);
+        if constexpr (F16) {
 #define GKV_GDN_LAUNCH(MAXC)                                                                                \
     switch (taps) {                                                                                         \
         case 1: gdn_rollback_f16_kernel<MAXC, 1><<<blocks, kF16Threads, 0, st>>>(p); break;                 \
@@ -666,12 +684,20 @@ int gdn_rollback_f16_impl(int32_t n_items, const int32_t *m, int32_t H, int32_t 
         case 3: gdn_rollback_f16_kernel<MAXC, 3><<<blocks, kF16Threads, 0, st>>>(p); break;                 \
         default: gdn_rollback_f16_kernel<MAXC, 4><<<blocks, kF16Threads, 0, st>>>(p); break;                \
     }
-        if (narrow) {
-            GKV_GDN_LAUNCH(kF16NarrowC)
-        } else {
-            GKV_GDN_LAUNCH(kFastC)
-        }
+            if (narrow) {
+                GKV_GDN_LAUNCH(kF16NarrowC)
+            } else {
+                GKV_GDN_LAUNCH(kFastC)
+            }
 #undef GKV_GDN_LAUNCH
+        } else {
+            switch (taps) {
+                case 1: gdn_rollback_f32_kernel<1><<<blocks, kRollThreads, 0, st>>>(p); break;
+                case 2: gdn_rollback_f32_kernel<2><<<blocks, kRollThreads, 0, st>>>(p); break;
+                case 3: gdn_rollback_f32_kernel<3><<<blocks, kRollThreads, 0, st>>>(p); break;
+                default: gdn_rollback_f32_kernel<4><<<blocks, kRollThreads, 0, st>>>(p); break;
+            }
+        }
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return report_error(GKV_ERR_CUDA, "gdn_rollback launch: %s", cudaGetErrorString(e));
     }
@@ -698,9 +724,17 @@ extern "C" int gkv_gdn_rollback_f16(int32_t n_items, const int32_t *m, int32_t H
                                     int32_t C, const void *s0, const float *delta, const float *k,
                                     const float *gcum, void *state_out, int32_t conv_dim, int32_t taps,
                                     const float *proj, const void *pre, void *conv_out, void *stream) {
-    return gkv::gdn_rollback_f16_impl(n_items, m, H, DK, DV, C, static_cast<const __half *>(s0), delta, k, gcum,
-                                      static_cast<__half *>(state_out), conv_dim, taps, proj,
-                                      static_cast<const __half *>(pre), static_cast<__half *>(conv_out), stream);
+    return gkv::gdn_rollback_impl<__half>(n_items, m, H, DK, DV, C, static_cast<const __half *>(s0), delta, k,
+                                          gcum, static_cast<__half *>(state_out), conv_dim, taps, proj,
+                                          static_cast<const __half *>(pre), static_cast<__half *>(conv_out), stream);
+}
+
+extern "C" int gkv_gdn_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                                const float *s0, const float *delta, const float *k, const float *gcum,
+                                float *state_out, int32_t conv_dim, int32_t taps, const float *proj,
+                                const float *pre, float *conv_out, void *stream) {
+    return gkv::gdn_rollback_impl<float>(n_items, m, H, DK, DV, C, s0, delta, k, gcum, state_out, conv_dim, taps,
+                                         proj, pre, conv_out, stream);
 }
 
 extern "C" int gkv_conv_rollback(int32_t n_items, const int32_t *m, int32_t conv_dim, int32_t taps, int32_t C,

@@ -49,7 +49,7 @@ EXPORTED = (
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
     "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16", "gkv_check_bounded_wait",
-    "gkv_tile_at", "gkv_gdn_rollback_f16",
+    "gkv_tile_at", "gkv_gdn_rollback_f16", "gkv_gdn_rollback",
 )
 
 
@@ -120,6 +120,7 @@ def load_library(path: str = LIB_PATH):
         "gkv_check_bounded_wait": (C.c_int, [i32, i64, i32p]),
         "gkv_tile_at": (C.c_int, [P, i32, i64, i64, i32, P, P, P]),
         "gkv_gdn_rollback_f16": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, i32, i32, P, P, P, P]),
+        "gkv_gdn_rollback": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, i32, i32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -587,33 +588,35 @@ def conv_rollback(m, proj, pre, out=None, stream=None):
 
 
 def gdn_rollback(m, s0, delta, k, gcum, proj, pre, out=None, conv_out=None, stream=None):
-    """``gkv_gdn_rollback_f16``: Engine.rollbackGDN (Engine.swift:2678-2716)
-    for a batch in one launch -- :func:`mtp_rollback` of the fp16 state and
-    :func:`conv_rollback` of the fp16 conv tail, the same items and m.
+    """``gkv_gdn_rollback_f16`` / ``gkv_gdn_rollback``: Engine.rollbackGDN
+    (Engine.swift:2678-2716) for a batch in one launch -- :func:`mtp_rollback`
+    of the state and :func:`conv_rollback` of the conv tail, the same items and
+    m; fp16 storage (the reference's) or fp32, as s0 and pre are.
     Returns (state_out, conv_out)."""
     import torch
     L = load_library()
     n, H, DK, DV = (int(x) for x in s0.shape)
     Cw = int(gcum.shape[-1])
     CD, T = int(pre.shape[1]), int(pre.shape[2])
-    _check_shape("s0", s0, (n, H, DK, DV), ("float16",))
+    sd = ("float16",) if str(s0.dtype) == "torch.float16" else ("float32",)
+    _check_shape("s0", s0, (n, H, DK, DV), sd)
     _check_shape("delta", delta, (n, H, Cw, DV), ("float32",))
     _check_shape("k", k, (n, H, Cw, DK), ("float32",))
     _check_shape("gcum", gcum, (n, H, Cw), ("float32",))
     _check_shape("proj", proj, (n, Cw, CD), ("float32",))
-    _check_shape("pre", pre, (n, CD, T), ("float16",))
+    _check_shape("pre", pre, (n, CD, T), sd)
     if out is None:
         out = torch.empty_like(s0)
     if conv_out is None:
         conv_out = torch.empty_like(pre)
-    _check_shape("out", out, (n, H, DK, DV), ("float16",))
-    _check_shape("conv_out", conv_out, (n, CD, T), ("float16",))
+    _check_shape("out", out, (n, H, DK, DV), sd)
+    _check_shape("conv_out", conv_out, (n, CD, T), sd)
     mm = _i32(m)
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
-    _check(L.gkv_gdn_rollback_f16(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k),
-                                  _dev_ptr(gcum), _dev_ptr(out), CD, T, _dev_ptr(proj), _dev_ptr(pre),
-                                  _dev_ptr(conv_out), _stream_ptr(stream)))
+    fn = L.gkv_gdn_rollback_f16 if sd == ("float16",) else L.gkv_gdn_rollback
+    _check(fn(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k), _dev_ptr(gcum), _dev_ptr(out),
+              CD, T, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(conv_out), _stream_ptr(stream)))
     return out, conv_out
 
 

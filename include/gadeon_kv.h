@@ -286,6 +286,14 @@ int gkv_gdn_rollback_f16(int32_t n_items, const int32_t *m, int32_t H,
                          void *state_out, int32_t conv_dim, int32_t taps,
                          const float *proj, const void *pre, void *conv_out,
                          void *stream);
+/* The same with fp32 storage: gkv_mtp_rollback + gkv_conv_rollback in one
+ * launch (DV % 4 == 0 for the state's vector kernel). */
+int gkv_gdn_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK,
+                     int32_t DV, int32_t C, const float *s0,
+                     const float *delta, const float *k, const float *gcum,
+                     float *state_out, int32_t conv_dim, int32_t taps,
+                     const float *proj, const float *pre, float *conv_out,
+                     void *stream);
 
 /* Size of the library's static scratch array used by gkv_attend_noalloc
  * (held on every GPU that loads the library until the process exits), and

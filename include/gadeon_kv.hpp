@@ -396,6 +396,14 @@ inline void rollbackGDN(int32_t nItems, const int32_t *m, int32_t H, int32_t DK,
     check(gkv_gdn_rollback_f16(nItems, m, H, DK, DV, C, s0, delta, k, gcum, stateOut, convDim, taps, proj, pre,
                                convOut, s));
 }
+/* The same for an engine that keeps fp32 state and conv tail (gkv_gdn_rollback). */
+inline void rollbackGDN(int32_t nItems, const int32_t *m, int32_t H, int32_t DK, int32_t DV, int32_t C,
+                        const float *s0, const float *delta, const float *k, const float *gcum, float *stateOut,
+                        int32_t convDim, int32_t taps, const float *proj, const float *pre, float *convOut,
+                        cudaStream_t s = nullptr) {
+    check(gkv_gdn_rollback(nItems, m, H, DK, DV, C, s0, delta, k, gcum, stateOut, convDim, taps, proj, pre, convOut,
+                           s));
+}
 
 }  // namespace gadeon
 

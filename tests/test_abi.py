@@ -92,7 +92,7 @@ def test_binding_refuses_bad_arguments_before_any_device_work(lib):
         lambda: gk.mtp_rollback([1], s0, delta, k, gcum),                     # one m for two items
         lambda: gk.mtp_rollback([1, 2], s0, delta, k, gcum),                  # pageable host memory
         lambda: gk.gdn_rollback([1, 2], s0, delta, k, gcum, proj[:, :2], pre),  # proj rows != C
-        lambda: gk.gdn_rollback([1, 2], s0.float(), delta, k, gcum, proj, pre),  # fused call is fp16 only
+        lambda: gk.gdn_rollback([1, 2], s0.float(), delta, k, gcum, proj, pre),  # state fp32, conv tail fp16
         lambda: gk.conv_rollback([1, 2], proj, pre.float().double()),         # pre of no storage type
     ]
     for i, call in enumerate(bad):

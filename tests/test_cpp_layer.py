@@ -22,7 +22,10 @@ def test_header_compiles(std):
            '  void (*f)(int32_t, const int32_t *, int32_t, int32_t, int32_t, int32_t, const void *, const float *,\n'
            '            const float *, const float *, void *, int32_t, int32_t, const float *, const void *, void *,\n'
            '            cudaStream_t) = gadeon::rollbackGDN;\n'
-           '  return f ? 0 : 1; }\n')
+           '  void (*g)(int32_t, const int32_t *, int32_t, int32_t, int32_t, int32_t, const float *, const float *,\n'
+           '            const float *, const float *, float *, int32_t, int32_t, const float *, const float *, float *,\n'
+           '            cudaStream_t) = gadeon::rollbackGDN;\n'
+           '  return f && g ? 0 : 1; }\n')
     r = subprocess.run(["g++", f"-std={std}", *WARN, *INC, "-x", "c++", "-", "-fsyntax-only"],
                        input=src, text=True, capture_output=True)
     assert r.returncode == 0, r.stderr

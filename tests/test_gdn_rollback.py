@@ -422,3 +422,33 @@ def test_gpu_gdn_rollback_fused_across_launch_chunks(cuda):
     torch.cuda.synchronize()
     u16 = lambda t: t.cpu().numpy().view(np.uint16)
     assert np.array_equal(u16(got_s), u16(want_s)) and np.array_equal(u16(got_c), u16(want_c))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,DK,DV,C,CD,taps", [
+    (32, 128, 128, 5, 8192, 3),   # fp32 state at the MTP verify width: one fused launch
+    (8, 128, 128, 8, 2056, 1),    # wide verify, 1 tap, a conv block partly filled: fused
+    (4, 8, 6, 5, 64, 2),          # DV % 4 != 0: the two separate launches
+])
+def test_gpu_gdn_rollback_f32_fused_equals_two_calls(cuda, oracle, H, DK, DV, C, CD, taps):
+    """gkv_gdn_rollback (fp32 storage) equals gkv_mtp_rollback +
+    gkv_conv_rollback bit for bit; state within rtol 1e-5 of the oracle
+    (expf may differ by an ulp), conv tail bit-exact with it."""
+    import gadeon_b200 as gk
+    torch = cuda
+    n = 3 * C + 1
+    m = (np.arange(n) % C + 1).astype(np.int32)
+    m, s0, delta, k, gcum = random_batch(95 + C, n, H, DK, DV, C, m)
+    rng = np.random.default_rng(96)
+    proj = rng.standard_normal((n, C, CD)).astype(np.float32)
+    pre = rng.standard_normal((n, CD, taps)).astype(np.float32)
+    ds, dpre, dproj = _dev(torch, s0), _dev(torch, pre), _dev(torch, proj)
+    dev = [_dev(torch, x) for x in (delta, k, gcum)]
+    want_s, want_c = gk.mtp_rollback(m, ds, *dev), gk.conv_rollback(m, dproj, dpre)
+    got_s, got_c = gk.gdn_rollback(m, ds, *dev, dproj, dpre)
+    torch.cuda.synchronize()
+    assert got_s.dtype == torch.float32
+    u32 = lambda t: t.cpu().numpy().view(np.uint32)
+    assert np.array_equal(u32(got_s), u32(want_s)) and np.array_equal(u32(got_c), u32(want_c))
+    np.testing.assert_allclose(got_s.cpu().numpy(), oracle.mtp_rollback(m, s0, delta, k, gcum), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(got_c.cpu().numpy(), oracle.conv_rollback(m, proj, pre))
