@@ -25,7 +25,7 @@ def test_decode_bytes_closed_form():
     assert decode_bytes([8196], cfg3) == 8196 * 4 * 256 * 2 * 2 + 4 * 16 * 256 * 6 + 4 * 513
 
 
-def test_config2_step_bytes_near_the_survey_estimate():
+def test_config2_step_bytes_near_the_published_estimate():
     """Config 2 at its mean context (~17.5K) moves ~2.3 GB per layer: 6
     layers ~13.8 GB per step, the order of the per-step estimate (13.3 GB at
     a mean of 16,896)."""
