@@ -58,9 +58,10 @@ enum gkv_status {
     GKV_ERR_CAPACITY = 6     /* max_seqs or max_pages_per_seq exceeded */
 };
 
-/* Message for the calling thread's last failing call ("" if none). */
+/* Message for the calling thread's last failing call ("" if none).  No
+ * reference counterpart: the Swift's thrown errors carry their message. */
 const char *gkv_last_error(void);
-/* Library version string. */
+/* Library version string.  No reference counterpart. */
 const char *gkv_version(void);
 
 typedef struct gkv_pool_config {
@@ -80,9 +81,12 @@ typedef struct gkv_pool_config {
 int gkv_pool_create(const gkv_pool_config *cfg, gkv_pool **out);
 int gkv_pool_destroy(gkv_pool *pool);
 
-/* A new empty sequence; ids are the lowest unused id. */
+/* A new empty sequence (a new PagePool, PagedAttention.swift:40-42); ids
+ * are the lowest unused id. */
 int gkv_seq_create(gkv_pool *pool, int32_t *seq_id);
-/* Drop every page of the sequence (last page first) and retire its id. */
+/* Drop every page of the sequence (last page first) and retire its id: the
+ * end of a PagePool, whose pages Swift's ARC frees (PagedAttention.swift
+ * :25-26). */
 int gkv_seq_release(gkv_pool *pool, int32_t seq_id);
 /* PagePool.length / pageCount (PagedAttention.swift:27, :79). */
 int gkv_seq_length(const gkv_pool *pool, int32_t seq_id, int64_t *length);
@@ -122,7 +126,9 @@ int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                float scale, void *stream);
 
 /* One decode / verify / chunk step in one call: gkv_append of n_q rows per
- * sequence followed by gkv_attend of those n_q rows. */
+ * sequence followed by gkv_attend of those n_q rows (Engine.stepHidden's
+ * append + hostFlashDecode, Engine.swift:1921-1927; verifyAttn, :2620-2646;
+ * batchedAttn, :1797-1820). */
 int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                       int32_t n_q, int32_t group, const void *k,
                       const void *v, const void *q, float *out, float scale,
@@ -286,8 +292,9 @@ int gkv_gdn_rollback_f16(int32_t n_items, const int32_t *m, int32_t H,
                          void *state_out, int32_t conv_dim, int32_t taps,
                          const float *proj, const void *pre, void *conv_out,
                          void *stream);
-/* The same with fp32 storage: gkv_mtp_rollback + gkv_conv_rollback in one
- * launch (DV % 4 == 0 for the state's vector kernel). */
+/* The same with fp32 storage (Engine.swift:2678-2716 over fp32 arrays):
+ * gkv_mtp_rollback + gkv_conv_rollback in one launch (DV % 4 == 0 for the
+ * state's vector kernel). */
 int gkv_gdn_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK,
                      int32_t DV, int32_t C, const float *s0,
                      const float *delta, const float *k, const float *gcum,
@@ -325,17 +332,21 @@ int gkv_attend_noalloc(const void *k_pages, const void *v_pages,
 
 /* ---- state export, for parity checks and debugging (synchronous) ---- */
 
-/* The sequence's block table as held ON THE DEVICE (first `pages` entries;
+/* State export for parity checks (no reference counterpart: the reference
+ * keeps no block table or free list).
+ * The sequence's block table as held ON THE DEVICE (first `pages` entries;
  * waits for the device).  cap = room in `pages_out`. */
 int gkv_export_table(gkv_pool *pool, int32_t seq_id, int32_t *pages_out,
                      int32_t cap, int32_t *n_pages);
-/* The free list in pop order (head first). */
+/* The free list in pop order (head first); no reference counterpart. */
 int gkv_export_free_list(const gkv_pool *pool, int32_t *out, int32_t cap,
                          int32_t *n);
-/* Reference count of a physical page (0 = free). */
+/* Reference count of a physical page (0 = free); no reference counterpart
+ * (PagePool.clone shares pages by ARC, PagedAttention.swift:199-210). */
 int gkv_page_refcount(const gkv_pool *pool, int32_t page_id, int32_t *ref);
 /* Copy one physical page's K and V ([kv_heads, P, head_dim] fp16 each) to
- * host memory (waits for the device). */
+ * host memory (waits for the device): the bytes of PagePool.kPage(_:) /
+ * vPage(_:) (PagedAttention.swift:80-81) by physical id. */
 int gkv_export_page(gkv_pool *pool, int32_t page_id, void *k_host,
                     void *v_host);
 /* Waits for the device and returns the pool's device status word: 0, or

@@ -99,3 +99,31 @@ def test_binding_refuses_bad_arguments_before_any_device_work(lib):
         with pytest.raises(gk.GkvError) as e:
             call()
         assert e.value.code == gk.GKV_ERR_INVALID, i
+
+
+def test_every_entry_point_cites_what_it_replaces():
+    """Each block of declarations in the header carries the reference
+    interface it replaces (file:line) or says that it has no counterpart."""
+    assert not uncited_entry_points(open(HEADER).read())
+
+
+def uncited_entry_points(text):
+    """Declarations whose comment -- the one right above, or the previous
+    declaration's when a group shares one -- names no reference location."""
+    body = text[text.index("typedef struct gkv_pool gkv_pool;"):]
+    cite = re.compile(r"\.(swift|metal):\d+|:\d+(-\d+)?\)|:\d+-\d+|counterpart", re.I)
+    missing, comment, prev_end = [], "", 0
+    for m in re.finditer(r"^(?:int|const char \*)\s*(gkv_\w+)\s*\(", body, re.M):
+        between = body[prev_end:m.start()]
+        if "/*" in between:
+            comment = between[between.rindex("/*"):]
+        if not cite.search(comment):
+            missing.append(m.group(1))
+        prev_end = body.index(";", m.end()) + 1
+    return missing
+
+
+def test_citation_check_catches_a_removed_citation():
+    text = open(HEADER).read()
+    assert uncited_entry_points(text.replace("Library version string.  No reference counterpart.",
+                                             "Library version string.", 1)) == ["gkv_version"]
