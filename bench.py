@@ -72,6 +72,13 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=20251201)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--repeats", type=int, default=10,
+                    help="timed blocks of --steps steps each; the line reports the median block")
+    ap.add_argument("--c5-parts", type=int, default=8,
+                    help="--config 5: partition the job into this many shards (8: the per-GPU shard of the "
+                         "8-way partition; = --gpus: the whole job over the GPUs)")
+    ap.add_argument("--no-subconfigs", action="store_true",
+                    help="config 2 alone: skip the configs 3/4 records (1 GPU) and config 5 (4 and 8 GPUs)")
     # profiling knobs: shrink the workload (ncu captures of one launch);
     # a line measured with them is not the config-2 number
     ap.add_argument("--seqs", type=int, default=None, help="sequences per GPU (default: config 2's 64)")
@@ -220,11 +227,53 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def mean_decode_bytes(ctx, cfg, first: int, count: int, out_bytes: int = 4) -> float:
+    """Mean algorithmic bytes of `count` consecutive decode launches whose
+    contexts (after the append) are ctx + first + j, j = 0..count-1."""
+    c = np.asarray(ctx, dtype=np.int64)[None, :] + first + np.arange(count, dtype=np.int64)[:, None]
+    kv_row = cfg.kv_heads * cfg.head_dim * 2
+    per = (c * kv_row * 2 + cfg.n_q * cfg.n_heads * cfg.head_dim * (2 + out_bytes)
+           + 4 * ((c + cfg.page_tokens - 1) // cfg.page_tokens))
+    return float(per.sum(axis=1).mean())
+
+
+def subconfigs(args, rank, world, local):
+    """The records beside config 2 in the default line: configs 3 and 4 on
+    one GPU (their full per-GPU workloads), and config 5's whole job strong-
+    scaled over 4 or 8 GPUs (every rank checks its memory first; all ranks
+    skip together when one lacks room)."""
+    import torch
+    import torch.distributed as dist
+    out = {}
+    R = max(1, args.repeats)
+    if world == 1:
+        out["3"] = measure_config3(args, rank, world, local, max(args.warmup, 3), max(args.steps, 20), R)
+        out["4"] = measure_config4(args, rank, world, local, max(args.warmup, 3), 3, 1)
+    elif world in (4, 8):
+        from gadeon_b200.workload import lpt_partition
+        cfg = CONFIGS[5]
+        job = contexts(5, args.seed, cfg.seqs)
+        mine = job[lpt_partition(job, world)[rank]]
+        need = pool_pages(mine, cfg.page_tokens, 128, 1.02) * cfg.kv_heads * cfg.page_tokens * cfg.head_dim * 4
+        need = need * cfg.layers + (4 << 30)
+        free = torch.cuda.mem_get_info(local)[0]
+        room = torch.tensor([free - need], device=torch.device("cuda", local), dtype=torch.float64)
+        dist.all_reduce(room, op=dist.ReduceOp.MIN)
+        if room.item() < 0:
+            out["5"] = {"skipped": "a GPU lacks room for its share of the job (%.1f GB short)"
+                                   % (-room.item() / 1e9)}
+        else:
+            out["5"] = measure_config5(args, rank, world, local, max(args.warmup, 3), min(args.steps, 20), 3, world)
+    return out
+
+
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
 
     from gadeon_b200 import BlockPool
+    from gadeon_b200.shard import gather_outputs
+    from gadeon_b200.workload import capped_partition
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -232,9 +281,14 @@ def run_ours(args, rank, world, local):
     L, S, KVH, dh, P, G, nH = cfg.layers, cfg.seqs, cfg.kv_heads, cfg.head_dim, cfg.page_tokens, cfg.group, cfg.n_heads
     L = args.layers or L
     S = args.seqs or S
-    W, K = args.warmup, args.steps
+    W, K, R = args.warmup, args.steps, max(1, args.repeats)
     ctx = weak_rank_contexts(2, args.seed, S, world, rank)
-    steps_total = W + K + (0 if args.no_e2e else 2 * K) + 2  # e2e: zero-copy and staged legs
+    # the N-GPU job: S * world sequences; rank r holds shard r of the count-
+    # capped token-balanced partition, rows of its outputs in shard order
+    job_ctx = weak_job_contexts(2, args.seed, S, world)
+    shards = capped_partition(job_ctx, world, S) if world > 1 else [list(range(S))]
+    n_legs = 0 if args.no_e2e else 3  # e2e: page-locked in place, staged copies, pageable arrays
+    steps_total = W + R * K + n_legs * K + 2
     max_pps = int(math.ceil((int(ctx.max()) + steps_total) / P)) + 2
     n_pages = pool_pages(ctx, P, steps_total)
 
@@ -258,20 +312,19 @@ def run_ours(args, rank, world, local):
         pools.append(pool)
         ids.append(lids)
     del scratch
-    # per-step inputs for warm-up + timed steps
+    # per-step inputs for warm-up + timed steps (every timed block reuses steps W..W+K-1)
     NS = W + K
     q_all = torch.randn((NS, L, S, 1, nH, dh), generator=gen, device=dev, dtype=torch.float16)
     k_all = torch.randn((NS, L, S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     v_all = torch.randn((NS, L, S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
-    ones = [1] * S
     torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    def step(i, timed_idx=None):
+    def step(i, ti):
         # one public call per layer: append the step's K/V row of every
         # sequence and attend (the append rides inside the attend kernel).
         # No event between the launches: each launch's start-up overlaps the
@@ -280,30 +333,23 @@ def run_ours(args, rank, world, local):
             pools[layer].append_attend(ids[layer], 1, G, k_all[i, layer], v_all[i, layer], q_all[i, layer],
                                        out=outs[layer])
 
-    for i in range(W):
-        step(i)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]
-                              if os.environ.get("CUDA_VISIBLE_DEVICES") else local))
-    clocks.start()
-    time.sleep(0.3)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    barrier()
-    start.record()
-    for i in range(K):
-        step(W + i, i)
-    end.record()
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
-    ms = start.elapsed_time(end) / K
+    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, R)
     attend_avg_ms = ms / L  # back-to-back launches: gaps between them included
     # algorithmic bytes of each timed attend launch (contexts after its append)
-    bytes_per_launch = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K)) + append_bytes(S, cfg)
+    bytes_per_launch = mean_decode_bytes(ctx, cfg, W + 1, R * K) + append_bytes(S, cfg)
     hbm_peak, peak_kind = peaks()
     achieved = bytes_per_launch / (attend_avg_ms * 1e-3) / 1e9
+    job_bytes = bytes_per_launch * L
+    if world > 1:
+        t = torch.tensor([job_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        job_bytes = float(t.item())
+
+    def job_outputs():
+        # every layer's outputs of the step, gathered over the GPUs into job
+        # order (pad to the largest shard, one NCCL all-gather, reorder)
+        local_out = torch.stack([o.reshape(S, -1) for o in outs], dim=1).reshape(S, -1)
+        return gather_outputs(local_out, shards, rank)
 
     # ---- end to end through the public call with host buffers
     e2e = None
@@ -311,66 +357,100 @@ def run_ours(args, rank, world, local):
         qh = q_all[W:].cpu().pin_memory()
         kh = k_all[W:].cpu().pin_memory()
         vh = v_all[W:].cpu().pin_memory()
-        oh = torch.empty((K, L, S, 1, nH, dh), dtype=torch.float32).pin_memory()
+        qp, kp, vp = q_all[W:].cpu(), k_all[W:].cpu(), v_all[W:].cpu()  # plain (pageable) host arrays
+        n_job = S * world
+        if world == 1:
+            oh = torch.empty((K, L, S, 1, nH, dh), dtype=torch.float32).pin_memory()
+            op = torch.empty((K, L, S, 1, nH, dh), dtype=torch.float32)
+        else:  # rank 0 receives the job's outputs
+            oh = torch.empty((K, n_job, L * nH * dh), dtype=torch.float32).pin_memory()
+            op = torch.empty((K, n_job, L * nH * dh), dtype=torch.float32)
         qd, kd, vd = torch.empty_like(q_all[0, 0]), torch.empty_like(k_all[0, 0]), torch.empty_like(v_all[0, 0])
-        torch.cuda.synchronize()
-        barrier()
-        # (a) the public call given the host buffers themselves: the kernel
-        # reads q/k/v from and writes out to page-locked host memory over the
-        # host link, overlapped with its HBM stream (zero-copy)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(K):
+
+        def leg(body):
+            torch.cuda.synchronize()
+            barrier()
+            e0.record()
+            for i in range(K):
+                body(i)
+            e1.record()
+            torch.cuda.synchronize()
+            barrier()
+            return e0.elapsed_time(e1) / K
+
+        def zero_copy(i):
+            # the public call given page-locked host q/k/v (read in place by
+            # the kernel over the host link); one GPU: out written in place to
+            # host memory; N GPUs: out on the device, gathered in job order,
+            # rank 0 copies the job's outputs to host memory
             for layer in range(L):
                 pools[layer].append_attend(ids[layer], 1, G, kh[i, layer], vh[i, layer], qh[i, layer],
-                                           out=oh[i, layer])
-        e1.record()
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / K
-        # (b) explicit staging: copy-engine H2D of q/k/v, the call on device
-        # buffers, D2H of the output, per layer
-        torch.cuda.synchronize()
-        barrier()
-        e0.record()
-        for i in range(K):
+                                           out=oh[i, layer] if world == 1 else outs[layer])
+            if world > 1:
+                job = job_outputs()
+                if rank == 0:
+                    oh[i].copy_(job, non_blocking=True)
+
+        def staged(i):
+            # explicit copy-engine H2D of q/k/v per layer, the call on device
+            # buffers, D2H of the output (one GPU) or of the gathered job (N)
             for layer in range(L):
                 qd.copy_(qh[i, layer], non_blocking=True)
                 kd.copy_(kh[i, layer], non_blocking=True)
                 vd.copy_(vh[i, layer], non_blocking=True)
                 pools[layer].append_attend(ids[layer], 1, G, kd, vd, qd, out=outs[layer])
-                oh[i, layer].copy_(outs[layer], non_blocking=True)
-        e1.record()
-        torch.cuda.synchronize()
-        e2e_copy_ms = e0.elapsed_time(e1) / K
-        h2d = L * (qd.numel() + kd.numel() + vd.numel()) * 2
-        d2h = L * outs[0].numel() * 4
-        e2e = [e2e_ms, h2d, d2h, e2e_copy_ms]
+                if world == 1:
+                    oh[i, layer].copy_(outs[layer], non_blocking=True)
+            if world > 1:
+                job = job_outputs()
+                if rank == 0:
+                    oh[i].copy_(job, non_blocking=True)
 
-    # ---- NCCL output gather (not on the hot path; timed separately)
+        def pageable(i):
+            # plain host arrays through the public call: the library stages
+            # them (one cudaMemcpyAsync per buffer; the call returns with out
+            # in place)
+            for layer in range(L):
+                pools[layer].append_attend(ids[layer], 1, G, kp[i, layer], vp[i, layer], qp[i, layer],
+                                           out=op[i, layer] if world == 1 else outs[layer])
+            if world > 1:
+                job = job_outputs()
+                if rank == 0:
+                    op[i].copy_(job)
+
+        e2e_ms = leg(zero_copy)
+        e2e_copy_ms = leg(staged)
+        e2e_page_ms = leg(pageable)
+        h2d = L * (qd.numel() + kd.numel() + vd.numel()) * 2 * world
+        d2h = (L * outs[0].numel() * 4) * world
+        e2e = [e2e_ms, h2d, d2h, e2e_copy_ms, e2e_page_ms]
+
+    # ---- the output gather on its own (N GPUs), after the timed region
     gather_ms = None
     if world > 1:
-        flat = torch.cat([o.reshape(-1) for o in outs])
-        gathered = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
         for _ in range(3):
-            dist.all_gather_into_tensor(gathered, flat)
+            job_outputs()
         torch.cuda.synchronize()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
         for _ in range(K):
-            dist.all_gather_into_tensor(gathered, flat)
+            job_outputs()
         g1.record()
         torch.cuda.synchronize()
         gather_ms = g0.elapsed_time(g1) / K
 
     # ---- max over ranks
-    vals = torch.tensor([ms, e2e[0] if e2e else 0.0, gather_ms or 0.0, attend_avg_ms, e2e[3] if e2e else 0.0],
-                        device=dev, dtype=torch.float64)
+    vals = torch.tensor([ms, e2e[0] if e2e else 0.0, gather_ms or 0.0, attend_avg_ms, e2e[3] if e2e else 0.0,
+                         e2e[4] if e2e else 0.0], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, e2e_ms_max, gather_max, attend_max, e2e_copy_max = vals.tolist()
+    ms, e2e_ms_max, gather_max, attend_max, e2e_copy_max, e2e_page_max = vals.tolist()
     for p in pools:
         st = p.device_status()
         assert st == 0, f"device status {st}"
+    del pools, q_all, k_all, v_all, outs
+    torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -380,12 +460,19 @@ def run_ours(args, rank, world, local):
         cpu = {"value": S / cpu_step, "unit": UNIT, "cores": 1, "kind": "port",
                "sample": desc + f" ({cpu_s:.1f} s of CPU time)"}
 
+    sub = None
+    if not args.no_subconfigs and (args.seqs, args.layers) == (None, None):
+        sub = subconfigs(args, rank, world, local)
+
     if rank != 0:
         return
     tokens = S * world
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": W, "repeats": R, "ms_per_step": ms, "block_ms_per_step": blocks,
+        "timing": f"{R} blocks of exactly {K} steps, each between barrier + synchronize brackets and timed "
+                  "with CUDA events (max over ranks); ms_per_step is the median block's",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
         "config": {
             "workload": (f"config2 decode step: {S} seqs/GPU x {L} layers, append 1 + paged GQA decode attend"
@@ -404,18 +491,31 @@ def run_ours(args, rank, world, local):
                      "kernel": "attend_kernel<256,TMA,fused append>", "bytes_per_launch": bytes_per_launch,
                      "launch_ms": attend_avg_ms, "launch_ms_max_rank": attend_max,
                      "launch_timing": "CUDA-event step time / layers (launches back to back, gaps included)"},
+        "job_gb_per_step": job_bytes / 1e9, "job_gbs": job_bytes / (ms * 1e-3) / 1e9,
+        "job_gbs_per_gpu": job_bytes / (ms * 1e-3) / 1e9 / world,
         "cpu_baseline": cpu,
         "e2e": ({"value": tokens / (e2e_ms_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": e2e[1],
                  "d2h_bytes_per_step": e2e[2], "ms_per_step": e2e_ms_max,
-                 "transfer": "gkv_append_attend on page-locked host q/k/v/out (kernel reads/writes them in place)",
+                 "transfer": ("gkv_append_attend on page-locked host q/k/v/out (kernel reads/writes them in place)"
+                              if world == 1 else
+                              "gkv_append_attend reading page-locked host q/k/v in place, outputs gathered "
+                              "over NCCL into job order (shard.gather_outputs), rank 0 copies the job's "
+                              "outputs to page-locked host memory; all inside each timed step"),
                  "staged_copy_value": tokens / (e2e_copy_max * 1e-3),
-                 "staged_copy_note": "same step with cudaMemcpyAsync H2D/D2H around each call"}
+                 "staged_copy_note": "same step with cudaMemcpyAsync H2D/D2H around each call",
+                 "pageable_value": tokens / (e2e_page_max * 1e-3),
+                 "pageable_note": "same step given plain (pageable) host arrays, which the library stages "
+                                  "through pool-owned device memory (one cudaMemcpyAsync per buffer)"}
                 if e2e else None),
-        "gpu_launches": K * L,
+        "gpu_launches": K * L * R,
         "clocks": clk,
     }
     if gather_ms is not None:
         line["gather_ms_per_step"] = gather_max
+        line["gather_note"] = ("all layers' outputs of a step gathered into job order (NCCL all-gather + "
+                               "reorder), timed on its own after the timed region; inside every e2e step")
+    if sub:
+        line["configs"] = sub
     print(json.dumps(line), flush=True)
 
 
@@ -458,9 +558,13 @@ def make_pools(torch, cfg, ctx, L, rank, seed, growth, local, factor=1.25, disti
     return pools, ids, gen
 
 
-def timed_loop(torch, dist, world, W, K, step, local):
-    """W untimed steps, then K steps between barrier+synchronize brackets,
-    clocks sampled meanwhile; returns (ms per step max over ranks, clocks)."""
+def timed_loop(torch, dist, world, W, K, step, local, repeats=1):
+    """W untimed steps, then `repeats` blocks of exactly K steps, each block
+    between barrier + synchronize brackets and timed with CUDA events on the
+    launching stream; clocks sampled meanwhile.  step(i, ti) runs step i
+    (ti = its index in the timed block, None while warming up); every block
+    runs steps W..W+K-1.  Returns (the median block's ms per step, each
+    block max over ranks; the blocks' ms per step; clocks)."""
     for i in range(W):
         step(i, None)
     torch.cuda.synchronize()
@@ -470,22 +574,25 @@ def timed_loop(torch, dist, world, W, K, step, local):
     clocks.start()
     time.sleep(0.3)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    start.record()
-    for i in range(K):
-        step(W + i, i)
-    end.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    blocks = []
+    for _ in range(repeats):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start.record()
+        for i in range(K):
+            step(W + i, i)
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        blocks.append(start.elapsed_time(end) / K)
     clk = clocks.stop()
-    ms = start.elapsed_time(end) / K
-    t = torch.tensor([ms], device=torch.device("cuda", local), dtype=torch.float64)
+    t = torch.tensor(blocks, device=torch.device("cuda", local), dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item()), clk
+    blocks = t.tolist()
+    return statistics.median(blocks), blocks, clk
 
 
 def max_over_ranks(torch, dist, world, local, x):
@@ -495,21 +602,21 @@ def max_over_ranks(torch, dist, world, local, x):
     return float(t.item())
 
 
-def run_config3(args, rank, world, local):
+def measure_config3(args, rank, world, local, W, K, repeats):
     """Config 3: MTP verify + rollback.  128 sequences at context 8192 (per
     GPU), nH=16, KVH=4, dh=256, P=16, one layer.  A step appends 4 draft
     rows per sequence, attends them causally (16 query rows per kv head),
-    then truncates to len + accepted, accepted ~ U{0..4} from a seeded RNG."""
+    then truncates to len + accepted, accepted ~ U{0..4} from a seeded RNG.
+    Returns this config's record (rank 0's view; timings max over ranks)."""
     import torch
     import torch.distributed as dist
     cfg = CONFIGS[3]
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    S, L = args.seqs or cfg.seqs, args.layers or cfg.layers
+    S, L = args.seqs or cfg.seqs, cfg.layers
     KVH, dh, G, nH, nq = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads, cfg.n_q
-    W, K = max(args.warmup, 3), max(args.steps, 64)
     ctx = contexts(3, args.seed + 1000 * rank, S)
-    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, (W + K) * nq + 8, local)
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, (W + K * repeats) * nq + 8, local)
     rng = np.random.default_rng(args.seed + 17 * rank)
     acc = rng.integers(0, nq + 1, size=(W + K, S))
     q = torch.randn((S, nq, nH, dh), generator=gen, device=dev, dtype=torch.float16)
@@ -519,7 +626,6 @@ def run_config3(args, rank, world, local):
     lens = ctx.copy()
     lens_at = []
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
-    fours = [nq] * S
 
     def step(i, ti):
         # one public call per layer appends the drafts and verifies them (the
@@ -537,31 +643,39 @@ def run_config3(args, rank, world, local):
         for layer in range(L):
             pools[layer].truncate(ids[layer], lens)
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, repeats)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)  # the last block's launches
     launch_ms = max_over_ranks(torch, dist, world, local, launch_ms)
     bpl = statistics.mean(decode_bytes(la, cfg) for la in lens_at) + append_bytes(S * nq, cfg)
     hbm, kind = peaks()
     for p in pools:
         assert p.device_status() == 0
-    if rank != 0:
-        return
+    del pools
+    torch.cuda.empty_cache()
     achieved = bpl / (launch_ms * 1e-3) / 1e9
-    print(json.dumps({
+    return {
         "metric": "MTP verify+rollback: draft tokens verified/s (config 3)",
         "value": S * nq * world / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
+        "repeats": repeats, "ms_per_step": ms, "block_ms_per_step": blocks, "higher_is_better": True,
+        "scaling": "weak", "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
         "config": {"workload": f"config3: {S} seqs/GPU at ctx 8192, {L} layer, 4 drafts appended + causal "
                                "attend in one gkv_append_attend (16 rows/kv head, split-K mma.sync kernel, "
                                "append fused), truncate to len+U{0..4}",
                    "kv_heads": KVH, "n_heads": nH, "head_dim": dh, "page_tokens": cfg.page_tokens,
-                   "l2": "inputs larger than L2"},
+                   "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)" % (float(ctx.sum()) * KVH * dh * 4 / 1e9)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append> (n_q=4)",
-                     "bytes_per_launch": bpl, "launch_ms": launch_ms},
+                     "bytes_per_launch": bpl, "launch_ms": launch_ms,
+                     "launch_timing": "CUDA events around each launch (the last timed block)"},
         "accepted_draft_tok_per_s": float(acc[W:].sum() * world / (K * ms * 1e-3)),
-        "cpu_baseline": None, "e2e": None, "gpu_launches": K * L, "clocks": clk}), flush=True)
+        "gpu_launches": K * L * repeats, "clocks": clk}
+
+
+def run_config3(args, rank, world, local):
+    rec = measure_config3(args, rank, world, local, max(args.warmup, 3), max(args.steps, 64), args.repeats)
+    if rank == 0:
+        rec.update({"vs_baseline": None, "cpu_baseline": None, "e2e": None})
+        print(json.dumps(rec), flush=True)
 
 
 def chunk_flops(ctx_before, n_q, cfg):
@@ -574,20 +688,19 @@ def chunk_flops(ctx_before, n_q, cfg):
     return f
 
 
-def run_config4(args, rank, world, local):
+def measure_config4(args, rank, world, local, W, K, repeats, seqs=None):
     """Config 4: prefill-chunk ingest.  32 sequences (per GPU) with a seeded
     16384-token context each ingest a 4096-token chunk per layer (append +
     causal chunk attention on the tcgen05 kernel), 8 layers, nH=16, KVH=4,
     dh=256, P=16; the chunk is truncated away after each step so every step
-    has the same shape."""
+    has the same shape.  Returns this config's record."""
     import torch
     import torch.distributed as dist
     cfg = CONFIGS[4]
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    S, L = args.seqs or cfg.seqs, args.layers or cfg.layers
+    S, L = seqs or cfg.seqs, cfg.layers
     KVH, dh, G, nH, nq = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads, cfg.n_q
-    W, K = max(args.warmup, 3), min(args.steps, 5)
     ctx = contexts(4, args.seed + 1000 * rank, S)
     pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, nq + 16, local, distinct=False)
     q = torch.randn((S, nq, nH, dh), generator=gen, device=dev, dtype=torch.float16)
@@ -607,97 +720,119 @@ def run_config4(args, rank, world, local):
                 ev[ti * L + layer][1].record()
             pools[layer].truncate(ids[layer], ctx)
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, repeats)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
     fl = chunk_flops(ctx, nq, cfg)
     peak, kind = tensor_peak(sustained=True)
     for p in pools:
         assert p.device_status() == 0
-    if rank != 0:
-        return
+    del pools
+    torch.cuda.empty_cache()
     achieved = fl / (launch_ms * 1e-3) / 1e12
-    print(json.dumps({
+    return {
         "metric": "prefill chunk ingest tok/s (config 4)", "value": S * nq * world / (ms * 1e-3), "unit": "tok/s",
-        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 x fp16 -> fp32 (tcgen05 kind::f16)",
+        "n_gpus": world, "steps": K, "warmup": W, "repeats": repeats, "ms_per_step": ms, "block_ms_per_step": blocks,
+        "higher_is_better": True, "scaling": "weak",
+        "dtype": "fp16 x fp16 -> fp32 (tcgen05 kind::f16; P.V as P_hi.V + P_lo.V)",
         "data": "synthetic (seeded N(0,1) fp16)",
         "config": {"workload": f"config4: {S} seqs/GPU x {L} layers, 16384-token context + 4096-token chunk "
                                "(append + causal chunk attention)", "kv_heads": KVH, "n_heads": nH,
                    "head_dim": dh, "page_tokens": cfg.page_tokens, "l2": "inputs larger than L2"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
-                     "traffic": None, "kernel": "chunk_kernel<256>", "flops_per_launch": fl,
-                     "launch_ms": launch_ms},
-        "cpu_baseline": None, "e2e": None, "gpu_launches": K * L * 2, "clocks": clk}), flush=True)
+                     "traffic": None, "kernel": "chunk_kernel<256,pair>", "flops_per_launch": fl,
+                     "flops_note": "algorithmic Q.K^T + P.V flops; the tensor cores also run the P_lo.V "
+                                   "correction (1.5x these flops)",
+                     "issued_tflops": 1.5 * achieved, "launch_ms": launch_ms,
+                     "launch_timing": "CUDA events around each chunk launch (the last timed block)"},
+        "gpu_launches": K * L * 2 * repeats, "clocks": clk}
 
 
-def run_config5(args, rank, world, local):
+def run_config4(args, rank, world, local):
+    rec = measure_config4(args, rank, world, local, max(args.warmup, 3), min(args.steps, 5), 1, args.seqs)
+    if rank == 0:
+        rec.update({"vs_baseline": None, "cpu_baseline": None, "e2e": None})
+        print(json.dumps(rec), flush=True)
+
+
+def measure_config5(args, rank, world, local, W, K, repeats, parts):
     """Config 5: long-context sharded decode.  The job is 512 sequences with
     contexts log-uniform in [4096, 131072] (8 layers, nH=16, KVH=4, dh=256,
-    P=16, ~0.6 TB of KV).  Sequences are token-balanced over 8 shards (greedy
-    LPT); rank r runs shard r % 8 -- the whole job at 8 GPUs, the per-GPU
-    shard of the 8-way partition at 1/2/4 GPUs (weak scaling).  One step =
-    per layer append 1 + decode attend; no collective on the hot path."""
+    P=16, ~0.6 TB of KV).  Sequences are token-balanced over `parts` shards
+    (greedy LPT) and rank r runs shard r % parts: parts = world is the whole
+    job strong-scaled over the GPUs; parts = 8 at fewer GPUs is the per-GPU
+    shard of the 8-way partition (weak scaling).  One step = per layer
+    append 1 + decode attend; no collective on the hot path.  After the
+    timed region the outputs are gathered in job order (NCCL all-gather)
+    and that gather is timed on its own.  Returns this config's record."""
     import torch
     import torch.distributed as dist
+    from gadeon_b200.shard import gather_outputs
     from gadeon_b200.workload import lpt_partition
     cfg = CONFIGS[5]
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     L = args.layers or cfg.layers
     KVH, dh, G, nH = cfg.kv_heads, cfg.head_dim, cfg.group, cfg.n_heads
-    W, K = max(args.warmup, 3), min(args.steps, 50)
     job = contexts(5, args.seed, cfg.seqs)
-    shards = lpt_partition(job, 8)
-    mine = shards[rank % 8]
-    if args.seqs:
-        mine = mine[: args.seqs]
+    shards = lpt_partition(job, parts)
+    if args.seqs:  # a reduced case: the first --seqs sequences of every shard
+        shards = [sh[: args.seqs] for sh in shards]
+    mine = shards[rank % parts]
     ctx = job[mine]
-    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, W + K + 4, local, factor=1.02,
+    pools, ids, gen = make_pools(torch, cfg, ctx, L, rank, args.seed, W + K * repeats + 4, local, factor=1.02,
                                  distinct=False)
     S = len(ctx)
     q = torch.randn((S, 1, nH, dh), generator=gen, device=dev, dtype=torch.float16)
     kk = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     vv = torch.randn((S, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
+
     def step(i, ti):
         # one public call per layer: the append rides inside the attend kernel
         for layer in range(L):
             pools[layer].append_attend(ids[layer], 1, G, kk, vv, q, out=outs[layer])
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, repeats)
     launch_ms = ms / L  # back-to-back launches: gaps between them included
     bpl = statistics.mean(decode_bytes(ctx + W + i + 1, cfg) for i in range(K)) + append_bytes(S, cfg)
     hbm, kind = peaks()
     gather_ms = None
-    if world > 1:
-        flat = torch.cat([o.reshape(-1) for o in outs])
-        n_max = int(max_over_ranks(torch, dist, world, local, flat.numel()))
-        padded = torch.zeros(n_max, dtype=flat.dtype, device=dev)
-        padded[: flat.numel()] = flat
-        gathered = torch.empty(world * n_max, dtype=flat.dtype, device=dev)
-        dist.all_gather_into_tensor(gathered, padded)
+    full_job = parts == world  # every rank holds one shard of the job (reduced by --seqs if given)
+    if world > 1 and full_job:
+        # every layer's outputs of the step, gathered into job order
+        local_out = torch.stack([o.reshape(S, -1) for o in outs], dim=1).reshape(S, -1)
+        gather_outputs(local_out, shards, rank)
         torch.cuda.synchronize()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
         for _ in range(10):
-            dist.all_gather_into_tensor(gathered, padded)
+            gather_outputs(local_out, shards, rank)
         g1.record()
         torch.cuda.synchronize()
         gather_ms = max_over_ranks(torch, dist, world, local, g0.elapsed_time(g1) / 10)
     tok_sum = max_over_ranks(torch, dist, world, local, float(ctx.sum()))
+    job_bytes = bpl * L
+    if world > 1:
+        t = torch.tensor([job_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        job_bytes = float(t.item())
     for p in pools:
         assert p.device_status() == 0
-    if rank != 0:
-        return
+    del pools
+    torch.cuda.empty_cache()
     achieved = bpl / (launch_ms * 1e-3) / 1e9
-    loads = [int(job[s].sum()) for s in shards]
-    print(json.dumps({
-        "metric": "long-context sharded decode tok/s (config 5)", "value": S * world / (ms * 1e-3),
-        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak" if world < 8 else "strong (full job)", "vs_baseline": None,
+    loads = [int(job[s_].sum()) for s_ in shards]
+    n_job = sum(len(s_) for s_ in shards) if full_job else S * world
+    return {
+        "metric": "long-context sharded decode tok/s (config 5)", "value": n_job / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "repeats": repeats, "ms_per_step": ms,
+        "block_ms_per_step": blocks, "higher_is_better": True,
+        "scaling": (("strong (the whole 512-sequence job)" if not args.seqs else
+                     f"strong (REDUCED: {args.seqs} seqs of every shard)") if full_job
+                    else "weak (8-way shard per GPU)"),
         "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
-        "config": {"workload": f"config5: shard {rank % 8} of an 8-way LPT partition of 512 seqs "
+        "config": {"workload": f"config5: shard {rank % parts} of a {parts}-way LPT partition of 512 seqs "
                                f"(ctx log-U[4096,131072]); {S} seqs/GPU x {L} layers",
                    "kv_gb_per_gpu": float(ctx.sum()) * L * KVH * dh * 4 / 1e9,
                    "shard_tokens_max_over_mean": max(loads) / (sum(loads) / len(loads)),
@@ -706,8 +841,20 @@ def run_config5(args, rank, world, local):
                      "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append>",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms,
                      "launch_timing": "CUDA-event step time / layers (launches back to back, gaps included)"},
-        "gather_ms_per_step": gather_ms, "cpu_baseline": None, "e2e": None, "gpu_launches": K * L,
-        "clocks": clk}), flush=True)
+        "job_gb_per_step": job_bytes / 1e9, "job_gbs": job_bytes / (ms * 1e-3) / 1e9,
+        "job_gbs_per_gpu": job_bytes / (ms * 1e-3) / 1e9 / world,
+        "gather_ms_per_step": gather_ms,
+        "gather_note": ("all layers' outputs gathered into job order (shard.gather_outputs: NCCL "
+                        "all_gather_into_tensor + reorder), timed after the timed region") if gather_ms else None,
+        "gpu_launches": K * L * repeats, "clocks": clk}
+
+
+def run_config5(args, rank, world, local):
+    rec = measure_config5(args, rank, world, local, max(args.warmup, 3), min(args.steps, 50), args.repeats,
+                          args.c5_parts)
+    if rank == 0:
+        rec.update({"vs_baseline": None, "cpu_baseline": None, "e2e": None})
+        print(json.dumps(rec), flush=True)
 
 
 def run_config2_producer(args, rank, world, local):
@@ -746,7 +893,7 @@ def run_config2_producer(args, rank, world, local):
             pools[layer].attn_step(ids[layer], G, qg[layer], kr[layer], vr[layer], q_norm[layer], k_norm[layer],
                                    cos_t[i], sin_t[i], eps=1e-6, out=outs[layer])
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    ms, _, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = ms / L  # back-to-back launches: gaps between them included
     # algorithmic bytes: the decode bytes (K/V once, q as fp16, fp32 out,
     # table) with the fp16 q replaced by the fp32 q|gate row, plus the raw
@@ -817,7 +964,7 @@ def run_config6(args, rank, world, local):
         if ti is not None:
             ev[ti][1].record()
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    ms, _, clk = timed_loop(torch, dist, world, W, K, step, local)
     launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
     step_bytes = statistics.mean(sum(rollback_bytes(ms_acc[W + i], g, sb)) for i in range(K))
     bpl = step_bytes  # one launch per step
@@ -934,7 +1081,7 @@ def run_config7(args, rank, world, local):
         drafter.rewind_append(dids, base, m, k4[: int(m.sum())], k4[: int(m.sum())])
         dlens = base + m
 
-    ms, clk = timed_loop(torch, dist, world, W, K, step, local)
+    ms, _, clk = timed_loop(torch, dist, world, W, K, step, local)
     att_ms = sum(a.elapsed_time(b) for a, b in att_ev)
     committed = float(acc[W:].sum())
     hbm, kind = peaks()

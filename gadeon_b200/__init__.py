@@ -7,6 +7,8 @@ ABI of include/gadeon_kv.h); this package is its Python binding.
 """
 from .kv import (  # noqa: F401
     EXPORTED,
+    GKV_ATTEND_HEAD_MAJOR,
+    GKV_ATTEND_OUT_F16,
     GKV_ERR_BAD_SEQ,
     GKV_ERR_CAPACITY,
     GKV_ERR_CUDA,
@@ -25,8 +27,10 @@ from .kv import (  # noqa: F401
     load_library,
     deserialize,
     mtp_rollback,
+    paged_flash_batched,
     read_state_header,
     rope_table,
     serialize,
     state_header,
+    verify_attn,
 )

@@ -81,12 +81,16 @@ struct ChunkCfg {
     static constexpr int CB_V = kTile * 128;
     static constexpr int STAGE_BYTES = NCB * CB_K;
     static_assert(STAGE_BYTES == V_NCB * CB_V, "K and V parts fill the same stage");
-    static constexpr int P_BYTES = kChunkRows * kTile * 2;  // two 64-key atoms
+    // P as P_hi and P_lo (fp16 each, two 64-key atoms each): P.V runs as
+    // P_hi.V + P_lo.V so the weights keep ~22 significant bits
+    static constexpr int P_ONE = kChunkRows * kTile * 2;
+    static constexpr int P_BYTES = 2 * P_ONE;
     static constexpr int NS_FIT = (kSmemLimit - 2048 - P_BYTES) / STAGE_BYTES;
     static constexpr int NS = NS_FIT < 8 ? NS_FIT : 8;      // ring depth
     static_assert(NS >= 3, "the ring needs three stages");
     static constexpr int OFF_STAGE = 0;
-    static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
+    static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;  // P_hi
+    static constexpr int OFF_PL = OFF_P + P_ONE;                  // P_lo
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
     static constexpr int NBARS = 2 * NS + 5;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                         : p.n_qblocks - 1 - (int)blockIdx.x;
     const int kvh = blockIdx.y, b = blockIdx.z;
     const AttendEntry e = p.entries[b];
-    const int G = p.G, KVH = p.kvh, nH = KVH * G;
+    const int G = p.G, KVH = p.kvh;
     const int p0 = e.len - p.n_q;
     // t_hi < t_lo (no valid rows) for a pair's odd block past the chunk's end
     const int t_lo = qb * p.qtok, t_hi = min(p.n_q, t_lo + p.qtok);
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         const int t = tid / G, g = tid - t * G, tok = t_lo + t;
         const bool valid = t < p.qtok && tok < t_hi;
         const uint4 *src = reinterpret_cast<const uint4 *>(
-            p.q + (((int64_t)b * p.n_q + (valid ? tok : 0)) * nH + kvh * G + g) * DH);
+            p.q + qo_row(p.head_major, b, valid ? tok : 0, kvh, g, p.n_q, KVH, G) * DH);
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + C::Q_COL;
 #pragma unroll 1
         for (int c0 = 0; c0 < DH / 2; c0 += 32) {
@@ -307,18 +311,24 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 tc_fence_after();
                 const uint32_t sV = smem_u32(stage(vi));
                 const uint32_t sP = smem_u32(smem + C::OFF_P);
+                const uint32_t sPl = smem_u32(smem + C::OFF_PL);
 #pragma unroll
                 for (int kk = 0; kk < TT / 16; ++kk) {
                     // P atom kk/4 holds keys 64*(kk/4) .. +63; V is MN-major:
                     // 64-column blocks CB_V apart (LBO), 8-key groups 1024
                     // bytes apart (SBO), 16 keys = 2048 bytes per K step.
-                    const uint64_t a = umma_desc_sw128(sP + (kk >> 2) * M * 128 + (kk & 3) * 32, 16, 1024);
+                    const uint32_t patom = (kk >> 2) * M * 128 + (kk & 3) * 32;
+                    const uint64_t a = umma_desc_sw128(sP + patom, 16, 1024);
+                    const uint64_t al = umma_desc_sw128(sPl + patom, 16, 1024);
                     const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, C::CB_V, 1024);
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    if constexpr (PAIR)
-                        umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
-                    else
-                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
+                    if constexpr (PAIR) {
+                        umma_pair_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
+                        umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                    } else {
+                        umma_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
+                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                    }
                 }
                 commit(&empty[vi % C::NS]);
                 commit(p_free);
@@ -427,23 +437,25 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 }
             }
             uint8_t *sP = smem + C::OFF_P;
+            uint8_t *sPl = smem + C::OFF_PL;
             // packed fp32x2 FMA / add (each lane rounded as fmaf / + would)
             float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                              make_float2(0.f, 0.f)};
             const float2 sl2 = make_float2(sl, sl), nmu2 = make_float2(nmu, nmu);
 #pragma unroll
             for (int ch = 0; ch < TT / 8; ++ch) {  // 16-byte chunks of 8 keys
-                uint32_t w4[4];
+                uint32_t w4[4], w4l[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float2 x = __ffma2_rn(make_float2(s[ch * 8 + 2 * u], s[ch * 8 + 2 * u + 1]), sl2, nmu2);
                     const float a0 = fast_exp2(x.x), a1 = fast_exp2(x.y);
                     ps2[u] = __fadd2_rn(ps2[u], make_float2(a0, a1));
-                    w4[u] = pack_half2(a0, a1);
+                    split_half2(a0, a1, w4[u], w4l[u]);
                 }
                 // P atom (ch / 8) holds keys 64*(ch/8) .. +63 of all rows
-                *reinterpret_cast<uint4 *>(sP + (ch >> 3) * M * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) =
-                    make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                const int at = (ch >> 3) * M * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4 *>(sP + at) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                *reinterpret_cast<uint4 *>(sPl + at) = make_uint4(w4l[0], w4l[1], w4l[2], w4l[3]);
             }
             l = l * factor + (((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
                               ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y)));
@@ -474,18 +486,28 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         if (ok && wait(p_free, (nt - 1) & 1)) {
             tc_fence_after();
             const float inv = 1.f / l;
-            float *dst =
-                p.out + (((int64_t)b * p.n_q + (row_valid ? tok : 0)) * nH + kvh * G + (r - tr * G)) * DH;
+            const int64_t at = qo_row(p.head_major, b, row_valid ? tok : 0, kvh, r - tr * G, p.n_q, KVH, G) * DH;
 #pragma unroll 1
             for (int c0 = 0; c0 < DH; c0 += 32) {
                 float o[32];
                 tmem_ld32(tmem_row + C::O_COL + c0, o);
                 tmem_wait_ld();
                 if (row_valid) {
+                    if (p.out_f16) {  // each value rounded to nearest even
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + at + c0);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4 *>(dst + c0 + i) =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                        for (int i = 0; i < 32; i += 8)
+                            dst[i / 8] = make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv),
+                                                    pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                                                    pack_half2(o[i + 4] * inv, o[i + 5] * inv),
+                                                    pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+                    } else {
+                        float *dst = static_cast<float *>(p.out) + at + c0;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(dst + i) =
+                                make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                    }
                 }
             }
         }
@@ -548,14 +570,16 @@ bool chunk_supported(int dh, int P, int G) {
 }
 
 // CTA pairs when the chunk has two or more query blocks and dh splits into
-// two halves of whole 64-column blocks; one CTA per block otherwise.
+// two halves of whole 64-column blocks; one CTA per block otherwise.  At dh
+// 256 always pairs (a lone block's partner has no rows): one CTA's 64 KB
+// stages would leave room for only two beside P_hi and P_lo.
 cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int dh,
                          cudaStream_t s) {
     const bool pair = p.n_qblocks >= 2;
     switch (dh) {
         case 64: return launch_chunk_t<64, false>(p, tk, tv, s);
         case 128: return pair ? launch_chunk_t<128, true>(p, tk, tv, s) : launch_chunk_t<128, false>(p, tk, tv, s);
-        case 256: return pair ? launch_chunk_t<256, true>(p, tk, tv, s) : launch_chunk_t<256, false>(p, tk, tv, s);
+        case 256: return launch_chunk_t<256, true>(p, tk, tv, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -82,7 +82,8 @@ __global__ void __launch_bounds__(256)
         if (pos >= row_lo && pos < row_hi) {
             const int64_t r = pos - row_lo;
             const uint16_t *src = kv ? p.v_src : p.k_src;
-            const int64_t off = p.head_major ? ((int64_t)h * e.n_new + r) * dh
+            // head-major: entry e's block [KVH, n_new, dh] starts at row src_row0 * KVH
+            const int64_t off = p.head_major ? ((int64_t)e.src_row0 * KVH + (int64_t)h * e.n_new + r) * dh
                                              : (((int64_t)e.src_row0 + r) * KVH + h) * dh;
             val = reinterpret_cast<const uint4 *>(src + off)[c];
         } else if (tp.src_pid >= 0) {
@@ -147,8 +148,9 @@ struct Cfg {
     static constexpr bool Q_REGS = DH <= 128;              // keep Q fragments in registers
     static constexpr int TKP = TK + 8;                     // padded P row (halves)
     static constexpr int OFF_Q = NSTAGE * 2 * TILE_BYTES;
-    static constexpr int OFF_P = OFF_Q + kRows * DH * 2;
-    static constexpr int OFF_RED = OFF_P + kRows * TKP * 2;
+    static constexpr int OFF_P = OFF_Q + kRows * DH * 2;      // P_hi [16][TKP] fp16
+    static constexpr int OFF_PL = OFF_P + kRows * TKP * 2;    // P_lo [16][TKP] fp16
+    static constexpr int OFF_RED = OFF_PL + kRows * TKP * 2;
     static constexpr int OFF_BAR = OFF_RED + 2 * kConsumerWarps * kRows * 4;
     static constexpr int OFF_FLAG = OFF_BAR + (2 * NSTAGE + 1) * 8;  // full, empty, rows_done
     static constexpr int SMEM = OFF_FLAG + 16;
@@ -179,6 +181,10 @@ __device__ __forceinline__ uint32_t q_off(int row, int c16) {
 // n_rot elements with the token's cos/sin row (Kernels.swift:66-84: pair
 // (i, i + n_rot/2) -> (a c - b s, a s + b c)).  Products and sums are rounded
 // one at a time, as the reference writes them (no fused multiply-add).
+// The sum of squares runs in the reference's order, element 0 first, one
+// rounded add after another (rmsnormRows, Kernels.swift:31): the running sum
+// visits the lanes in turn, each adding its E squares.  So a K row stored in
+// a page matches the reference bit for bit, and so does every fp16 q row.
 template <int DH>
 __device__ __forceinline__ void produce_row(const float *x, const float *w, float eps, const float *cs,
                                             const float *sn, int n_rot, int lane, float (&v)[DH / 32]) {
@@ -203,11 +209,18 @@ __device__ __forceinline__ void produce_row(const float *x, const float *w, floa
         cv[i] = (lo || hi) ? __ldg(cs + ti + i) : 1.f;
         sv[i] = (lo || hi) ? __ldg(sn + ti + i) : 0.f;
     }
+    float sq[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) sq[i] = __fmul_rn(v[i], v[i]);
     float ss = 0.f;
+#pragma unroll 1
+    for (int l = 0; l < 32; ++l) {
+        if (lane == l) {
 #pragma unroll
-    for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+            for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, sq[i]);
+        }
+        ss = __shfl_sync(0xffffffffu, ss, l);
+    }
     const float inv = 1.f / sqrtf(ss / (float)DH + eps);
 #pragma unroll
     for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
@@ -419,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
     const int tid = threadIdx.x;  // 0..127
     uint8_t *sQ = smem + C::OFF_Q;
     __half *sP = reinterpret_cast<__half *>(smem + C::OFF_P);
+    __half *sPl = reinterpret_cast<__half *>(smem + C::OFF_PL);
     float *red_max = reinterpret_cast<float *>(smem + C::OFF_RED);
     float *red_sum = red_max + kConsumerWarps * kRows;
     const int G = p.G, R = p.n_q * p.G, nH = KVH * p.G;
@@ -435,6 +449,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
     // Causal limits of this thread's two fragment rows: key t is visible to
     // row r iff t <= len - n_q + r / G (padding rows use the last real row).
     const int rq0 = min(lr, R - 1) / G, rq1 = min(lr + 8, R - 1) / G;
+    // Up to 8 query rows (decode: G rows): P_lo of row r rides in the unused
+    // row r + 8 of the same MMA, so P_hi.V and P_lo.V cost one MMA; rows
+    // r and r + 8 of O are added at the end.  16 rows (MTP verify) run a
+    // second MMA over a P_lo tile.
+    const bool stack = R <= 8;
 
     if constexpr (FUSED) {
         // Fused append, while the producer's first loads are in flight: for
@@ -482,7 +501,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                     } else {
                         for (int i = tid; i < (r_hi - r_lo) * C::CH; i += 128) {
                             const int pos = r_lo + i / C::CH, c = i % C::CH;
-                            const int64_t src = (((int64_t)a.b * p.n_q + (pos - p0)) * KVH + a.kvh) * C::CH + c;
+                            const int64_t src =
+                                (p.head_major ? ((int64_t)a.b * KVH + a.kvh) * p.n_q + (pos - p0)
+                                              : ((int64_t)a.b * p.n_q + (pos - p0)) * KVH + a.kvh) * C::CH + c;
                             kd[(pos - pg) * C::CH + c] = reinterpret_cast<const uint4 *>(p.k_new)[src];
                             vd[(pos - pg) * C::CH + c] = reinterpret_cast<const uint4 *>(p.v_new)[src];
                         }
@@ -541,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                     if (row < R) {
                         const int s = row / G, g = row - s * G;
                         const uint16_t *src =
-                            p.q + (((int64_t)b * p.n_q + s) * nH + kvh * G + g) * DH + c16 * 8;
+                            p.q + qo_row(p.head_major, b, s, kvh, g, p.n_q, KVH, G) * DH + c16 * 8;
                         val = *reinterpret_cast<const uint4 *>(src);
                     }
                     *reinterpret_cast<uint4 *>(sQ + q_off(row, c16)) = val;
@@ -662,28 +683,39 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
             ps0 += p0 + p1;
             ps1 += p2 + p3;
             const int kb = warp * C::KPW + n * 8 + lc;
-            *reinterpret_cast<uint32_t *>(sP + lr * C::TKP + kb) = pack_half2(p0, p1);
-            *reinterpret_cast<uint32_t *>(sP + (lr + 8) * C::TKP + kb) = pack_half2(p2, p3);
+            uint32_t h01, l01, h23, l23;
+            split_half2(p0, p1, h01, l01);
+            *reinterpret_cast<uint32_t *>(sP + lr * C::TKP + kb) = h01;
+            if (stack) {
+                *reinterpret_cast<uint32_t *>(sP + (lr + 8) * C::TKP + kb) = l01;
+            } else {
+                split_half2(p2, p3, h23, l23);
+                *reinterpret_cast<uint32_t *>(sP + (lr + 8) * C::TKP + kb) = h23;
+                *reinterpret_cast<uint32_t *>(sPl + lr * C::TKP + kb) = l01;
+                *reinterpret_cast<uint32_t *>(sPl + (lr + 8) * C::TKP + kb) = l23;
+            }
         }
         l0 = l0 * c0 + ps0;
         l1 = l1 * c1 + ps1;
+        const float c1o = stack ? c0 : c1;  // stacked: rows r + 8 hold row r's P_lo.V
 #pragma unroll
         for (int n = 0; n < C::NT_PV; ++n) {
             o[n][0] *= c0;
             o[n][1] *= c0;
-            o[n][2] *= c1;
-            o[n][3] *= c1;
+            o[n][2] *= c1o;
+            o[n][3] *= c1o;
         }
         consumer_sync();
 
-        // ---- O += P V for this warp's DPW head-dim columns
+        // ---- O += P V for this warp's DPW head-dim columns, as P_lo.V + P_hi.V
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
-            uint32_t a0, a1, a2, a3;
+            uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
             {
                 const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int key = kk * 16 + (lane >> 4) * 8;
                 ldsm_x4(smem_u32(sP + row * C::TKP + key), a0, a1, a2, a3);
+                if (!stack) ldsm_x4(smem_u32(sPl + row * C::TKP + key), c0, c1, c2, c3);
             }
             const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
@@ -691,6 +723,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                 const int c16 = (warp * C::DPW) / 8 + jp * 2 + (lane >> 4);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(smem_u32(sV) + tile_off(key, c16, lbh, C::NCB), b0, b1, b2, b3);
+                if (!stack) {
+                    mma16816(o[2 * jp], c0, c1, c2, c3, b0, b1);
+                    mma16816(o[2 * jp + 1], c0, c1, c2, c3, b2, b3);
+                }
                 mma16816(o[2 * jp], a0, a1, a2, a3, b0, b1);
                 mma16816(o[2 * jp + 1], a0, a1, a2, a3, b2, b3);
             }
@@ -706,6 +742,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
         // ---- item end: final output, or a partial for the merge
         const bool last_of_item = (j == w.e.ntiles - 1) || (u == u_end - 1);
         if (last_of_item) {
+            if (stack) {  // row r's O = its P_hi.V (row r) + its P_lo.V (row r + 8)
+#pragma unroll
+                for (int n = 0; n < C::NT_PV; ++n) {
+                    o[n][0] += o[n][2];
+                    o[n][1] += o[n][3];
+                }
+            }
             float ls0 = l0, ls1 = l1;
             ls0 += __shfl_xor_sync(0xffffffffu, ls0, 1);
             ls0 += __shfl_xor_sync(0xffffffffu, ls0, 2);
@@ -732,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                     const int row = lr + half * 8;
                     if (row < R) {
                         const int s_ = row / G, g = row - s_ * G;
-                        float *dst = p.out + (((int64_t)b * p.n_q + s_) * nH + kvh * G + g) * DH;
+                        const int64_t orow = qo_row(p.head_major, b, s_, kvh, g, p.n_q, KVH, G);
                         const float inv = half ? i1 : i0;
 #pragma unroll
                         for (int n = 0; n < C::NT_PV; ++n) {
@@ -743,7 +786,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                                 r2.x *= sigmoid_gate(__ldg(gt + col0 + n * 8));
                                 r2.y *= sigmoid_gate(__ldg(gt + col0 + n * 8 + 1));
                             }
-                            *reinterpret_cast<float2 *>(dst + col0 + n * 8) = r2;
+                            const int64_t at = orow * DH + col0 + n * 8;
+                            if (p.out_f16)
+                                *reinterpret_cast<uint32_t *>(static_cast<uint16_t *>(p.out) + at) =
+                                    pack_half2(r2.x, r2.y);
+                            else
+                                *reinterpret_cast<float2 *>(static_cast<float *>(p.out) + at) = r2;
                         }
                     }
                 }
@@ -795,10 +843,16 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
                             Os += __ldcg(pk + 32 + (int64_t)row * DH + d) * wk;
                         }
                         const int s_ = row / G, g = row - s_ * G;
-                        const int64_t orow = ((int64_t)b * p.n_q + s_) * nH + kvh * G + g;
                         float res = Os / Ls;
-                        if constexpr (PROD) res *= sigmoid_gate(__ldg(p.prod.q_gate + orow * (2 * DH) + DH + d));
-                        p.out[orow * DH + d] = res;
+                        if constexpr (PROD) {
+                            const int64_t grow = ((int64_t)b * p.n_q + s_) * nH + kvh * G + g;
+                            res *= sigmoid_gate(__ldg(p.prod.q_gate + grow * (2 * DH) + DH + d));
+                        }
+                        const int64_t at = qo_row(p.head_major, b, s_, kvh, g, p.n_q, KVH, G) * DH + d;
+                        if (p.out_f16)
+                            static_cast<__half *>(p.out)[at] = __float2half_rn(res);
+                        else
+                            static_cast<float *>(p.out)[at] = res;
                     }
                 }
             }

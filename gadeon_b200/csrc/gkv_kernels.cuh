@@ -51,9 +51,9 @@ struct AppendParams {
     const AppendEntry *entries;  // null: AppendInline::entries
     const TouchedPage *pages;    // null: AppendInline::pages
     int32_t n_pages;
-    const uint16_t *k_src;  // token-major [rows, KVH, dh] or head-major [KVH, rows, dh]
+    const uint16_t *k_src;  // token-major [rows, KVH, dh], or head-major: per entry [KVH, n_new, dh]
     const uint16_t *v_src;
-    int32_t head_major;     // 1: seed layout [KVH, n_new, dh]
+    int32_t head_major;     // 1: head-major (seed; the reference's verify k / v [KVH, S, dh])
     uint16_t *k_pool;       // [num_pages, KVH, P, dh]
     uint16_t *v_pool;
     int32_t *table;         // [max_seqs, table_stride]
@@ -62,6 +62,16 @@ struct AppendParams {
 };
 
 // ---------------------------------------------------------------- attend
+// Row (query token s of sequence b, query head kvh*G + g) of q and out, in
+// units of head_dim: token-major [n, n_q, KVH*G] (the default), or the
+// reference's verify / batched-flash layout [n, KVH, n_q, G] -- per sequence
+// [KVH, S, G, dh] (Engine.verifyAttn, Engine.swift:2618-2646;
+// pagedFlashBatched, PagedAttention.swift:370-376).
+__host__ __device__ inline int64_t qo_row(bool head_major, int64_t b, int s, int kvh, int g, int n_q, int KVH,
+                                          int G) {
+    return head_major ? ((b * KVH + kvh) * n_q + s) * G + g : (b * n_q + s) * (int64_t)(KVH * G) + kvh * G + g;
+}
+
 struct AttendEntry {
     int32_t seq_id;
     int32_t len;        // keys in the sequence (query rows are the last n_q)
@@ -108,8 +118,9 @@ struct AttendParams {
     const AttendEntry *entries;  // null: InlineDesc::entries
     int32_t n_seqs;
     int32_t total_units;
-    // fused append (fused = 1): k_new/v_new [n_seqs * n_q, KVH, dh] fp16, the
-    // n_q new rows of every sequence, written into the pool before the key
+    // fused append (fused = 1): k_new/v_new [n_seqs * n_q, KVH, dh] fp16
+    // ([n_seqs, KVH, n_q, dh] when head_major), the n_q new rows of every
+    // sequence, written into the pool before the key
     // tiles holding them are loaded; tails (null: InlineDesc::tails) say where
     int32_t fused;
     const FusedTail *tails;
@@ -120,8 +131,10 @@ struct AttendParams {
     int32_t table_stride;
     const uint16_t *k_pool;  // used by the cp.async loader (P < 8)
     const uint16_t *v_pool;
-    const uint16_t *q;       // [n_seqs, n_q, KVH*G, dh]
-    float *out;              // [n_seqs, n_q, KVH*G, dh]
+    const uint16_t *q;       // [n_seqs, n_q, KVH*G, dh], head_major: [n_seqs, KVH, n_q, G, dh]
+    void *out;               // q's layout; fp32, or fp16 when out_f16
+    int32_t head_major;      // q / out (and the fused append's k_new / v_new) head-major
+    int32_t out_f16;         // out values rounded to fp16 (nearest even)
     float *partials;         // [n_items + grid, 32 + 16*dh]
     int32_t *counters;       // [n_items], zero between launches
     int32_t *status;         // device status word
@@ -167,8 +180,10 @@ struct ChunkParams {
     int32_t n_seqs;
     const int32_t *table;
     int32_t table_stride;
-    const uint16_t *q;  // [n_seqs, n_q, KVH*G, dh]
-    float *out;         // [n_seqs, n_q, KVH*G, dh]
+    const uint16_t *q;  // [n_seqs, n_q, KVH*G, dh], head_major: [n_seqs, KVH, n_q, G, dh]
+    void *out;          // q's layout; fp32, or fp16 when out_f16
+    int32_t head_major;
+    int32_t out_f16;
     int32_t *status;
     int32_t n_q, G, kvh, P, num_pages;
     int32_t qtok;       // query tokens per CTA

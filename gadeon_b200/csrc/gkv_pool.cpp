@@ -169,6 +169,8 @@ struct gkv_pool {
     float *d_partials = nullptr;
     int32_t *d_counters = nullptr;
     uint16_t *d_prod = nullptr;  // [2][max_seqs * KVH * dh] fp16 K/V rows of gkv_attn_step's unfused route
+    uint8_t *d_host_stage = nullptr;  // device copies of a call's pageable host buffers
+    size_t host_stage_bytes = 0;
     CUtensorMap tmk{}, tmv{};  // chunk kernel: boxes of min(P, 64) rows
     CUtensorMap tak{}, tav{};  // attend kernel: boxes of min(P, tile_keys) rows
     std::vector<int32_t> stack;  // free list; back() is the head
@@ -235,6 +237,85 @@ int check_buffers(const gkv_pool *pool, std::initializer_list<std::pair<const vo
     }
     return GKV_OK;
 }
+
+// Pageable host buffers (plain host arrays: malloc, a Swift [Float], numpy).
+// A kernel cannot reach them, so a call given one stages it through device
+// memory the pool owns: one cudaMemcpyAsync per pageable input on the call's
+// stream before the launch, one per pageable output after it.  A copy into
+// pageable memory returns only once it is done, so such a call returns with
+// its output in place (it waits for the device); the input copies return
+// once the runtime holds the bytes, so inputs may be reused at once.  The
+// staging memory grows (cudaMalloc) when a call needs more than it holds and
+// is reused by the next call in stream order.
+bool is_pageable(const void *ptr) {
+    if (!ptr) return false;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return false;  // check_buffers reports it
+    }
+    return a.type == cudaMemoryTypeUnregistered;
+}
+
+class HostStage {
+public:
+    explicit HostStage(gkv_pool *pool) : pool_(pool) {}
+    // Registers a caller buffer of `bytes`; when it is pageable host memory,
+    // reserve() points *ptr at the pool's staging memory.
+    void in(const void **ptr, size_t bytes) { add(const_cast<void **>(ptr), bytes, false); }
+    void out(void **ptr, size_t bytes) { add(ptr, bytes, true); }
+    bool any() const { return !items_.empty(); }
+    // Makes room (the one step that may allocate: call it with the pool's
+    // device current and before any bookkeeping changes) and re-points the
+    // registered pageable buffers.
+    int reserve() {
+        size_t total = 0;
+        for (Item &it : items_) {
+            it.off = total;
+            total += (it.bytes + 255) & ~size_t(255);
+        }
+        if (total > pool_->host_stage_bytes) {
+            cudaFree(pool_->d_host_stage);  // waits for work that may still read it
+            pool_->d_host_stage = nullptr;
+            pool_->host_stage_bytes = 0;
+            size_t cap = size_t(1) << 20;
+            while (cap < total) cap *= 2;
+            const cudaError_t e = cudaMalloc(&pool_->d_host_stage, cap);
+            if (e != cudaSuccess) return cuda_fail(e, "staging memory for pageable host buffers");
+            pool_->host_stage_bytes = cap;
+        }
+        for (Item &it : items_) *it.slot = pool_->d_host_stage + it.off;
+        return GKV_OK;
+    }
+    int copy_in(cudaStream_t st) const {
+        for (const Item &it : items_)
+            if (!it.out)
+                GKV_CUDA(cudaMemcpyAsync(*it.slot, it.host, it.bytes, cudaMemcpyHostToDevice, st),
+                         "pageable input copy");
+        return GKV_OK;
+    }
+    int copy_out(cudaStream_t st) const {
+        for (const Item &it : items_)
+            if (it.out)
+                GKV_CUDA(cudaMemcpyAsync(it.host, *it.slot, it.bytes, cudaMemcpyDeviceToHost, st),
+                         "pageable output copy");
+        return GKV_OK;
+    }
+
+private:
+    struct Item {
+        void **slot;
+        void *host;
+        size_t bytes;
+        bool out;
+        size_t off;
+    };
+    void add(void **ptr, size_t bytes, bool out) {
+        if (bytes > 0 && is_pageable(*ptr)) items_.push_back({ptr, *ptr, bytes, out, 0});
+    }
+    gkv_pool *pool_;
+    std::vector<Item> items_;
+};
 
 // Host half of an append/seed: validates, mutates the bookkeeping, and fills
 // the descriptor (entries + touched pages).  Nothing is mutated on failure.
@@ -375,7 +456,7 @@ int enqueue_append(gkv_pool *pool, const std::vector<gkv::AppendEntry> &entries,
 
 // Validation shared by gkv_attend / gkv_append_attend (after the append).
 int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
-                 const void *q, const float *out) {
+                 const void *q, const void *out) {
     if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
     if ((int64_t)n_q * group > 16 &&
         !gkv::chunk_supported(pool->cfg.head_dim, pool->cfg.page_tokens, group))
@@ -395,9 +476,11 @@ int check_attend(const gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_
 // tails != null: single-token decode with the append fused into the attend
 // kernel (k_new / v_new hold each sequence's new row).
 int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, int32_t group,
-                   const void *q, float *out, float scale, cudaStream_t st,
+                   const void *q, void *out, float scale, uint32_t flags, cudaStream_t st,
                    const gkv::FusedTail *tails = nullptr, const void *k_new = nullptr,
                    const void *v_new = nullptr, const gkv::ProducerArgs *prod = nullptr) {
+    const int32_t head_major = (flags & GKV_ATTEND_HEAD_MAJOR) ? 1 : 0;
+    const int32_t out_f16 = (flags & GKV_ATTEND_OUT_F16) ? 1 : 0;
     if (n == 0) return GKV_OK;
     const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
     const bool chunk = (int64_t)n_q * group > 16;  // many rows per kv head: tcgen05 chunk kernel
@@ -438,6 +521,8 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         c.table_stride = pool->cfg.max_pages_per_seq;
         c.q = static_cast<const uint16_t *>(q);
         c.out = out;
+        c.head_major = head_major;
+        c.out_f16 = out_f16;
         c.status = pool->d_status;
         c.n_q = n_q;
         c.G = group;
@@ -473,6 +558,8 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
     p.v_pool = pool->d_v;
     p.q = static_cast<const uint16_t *>(q);
     p.out = out;
+    p.head_major = head_major;
+    p.out_f16 = out_f16;
     p.partials = pool->d_partials;
     p.counters = pool->d_counters;
     p.status = pool->d_status;
@@ -500,6 +587,9 @@ void free_device(gkv_pool *p) {
     cudaFree(p->d_counters);
     cudaFree(p->d_prod);
     p->d_prod = nullptr;
+    cudaFree(p->d_host_stage);
+    p->d_host_stage = nullptr;
+    p->host_stage_bytes = 0;
     p->d_k = p->d_v = nullptr;
     p->d_table = p->d_status = p->d_counters = nullptr;
     p->d_partials = nullptr;
@@ -780,14 +870,21 @@ int gkv_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int
     int64_t rows = 0;
     for (int32_t i = 0; i < n_seqs; ++i) rows += std::max(n_new[i], 0);
     if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t kb = (size_t)rows * pool->cfg.kv_heads * pool->cfg.head_dim * 2;
+    hs.in(&k, kb);
+    hs.in(&v, kb);
+    if ((rc = hs.reserve())) return rc;
     if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
     if (rows > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}}))) return rc;
-    DeviceGuard guard(pool->cfg.device);
     std::vector<gkv::AppendEntry> entries;
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new, entries, pages);
     if (rc) return rc;
-    return enqueue_append(pool, entries, pages, k, v, 0, static_cast<cudaStream_t>(stream));
+    if ((rc = hs.copy_in(st))) return rc;
+    return enqueue_append(pool, entries, pages, k, v, 0, st);
 }
 
 int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64_t count,
@@ -799,38 +896,60 @@ int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64
                                  seq_id, (long long)s->len);
     if (count < 0 || count > INT32_MAX) return fail(GKV_ERR_INVALID, "count=%lld", (long long)count);
     if (count > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
-    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
-    if (count > 0) {
-        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
-        if (rc) return rc;
-    }
     DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t kb = (size_t)count * pool->cfg.kv_heads * pool->cfg.head_dim * 2;
+    hs.in(&K, kb);
+    hs.in(&V, kb);
+    int rc = hs.reserve();
+    if (rc) return rc;
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    if (count > 0 && (rc = check_buffers(pool, {{K, "K"}, {V, "V"}}))) return rc;
     const int32_t n = (int32_t)count;
     std::vector<gkv::AppendEntry> entries;
     std::vector<gkv::TouchedPage> pages;
-    int rc = plan_append(pool, 1, &seq_id, &n, entries, pages);
+    rc = plan_append(pool, 1, &seq_id, &n, entries, pages);
     if (rc) return rc;
-    return enqueue_append(pool, entries, pages, K, V, 1, static_cast<cudaStream_t>(stream));
+    if ((rc = hs.copy_in(st))) return rc;
+    return enqueue_append(pool, entries, pages, K, V, 1, st);
 }
 
-int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q,
-               int32_t group, const void *q, float *out, float scale, void *stream) {
+int gkv_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
+                  const void *q, void *out, float scale, uint32_t flags, void *stream) {
     if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16))
+        return fail(GKV_ERR_INVALID, "unknown flags 0x%x", flags);
     int rc = check_batch(pool, n_seqs, seq_ids);
     if (rc) return rc;
+    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
+    if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t nqo = (size_t)n_seqs * n_q * pool->cfg.kv_heads * group * pool->cfg.head_dim;
+    hs.in(&q, nqo * 2);
+    hs.out(&out, nqo * ((flags & GKV_ATTEND_OUT_F16) ? 2 : 4));
+    if ((rc = hs.reserve())) return rc;
     rc = check_attend(pool, n_seqs, seq_ids, n_q, group, q, out);
     if (rc) return rc;
-    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
     if (n_seqs > 0 && (rc = check_buffers(pool, {{q, "q"}, {out, "out"}}))) return rc;
-    DeviceGuard guard(pool->cfg.device);
-    return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale,
-                          static_cast<cudaStream_t>(stream));
+    if ((rc = hs.copy_in(st))) return rc;
+    rc = enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, flags, st);
+    return rc ? rc : hs.copy_out(st);
 }
 
-int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q,
-                      int32_t group, const void *k, const void *v, const void *q, float *out,
-                      float scale, void *stream) {
+int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
+               const void *q, float *out, float scale, void *stream) {
+    return gkv_attend_ex(pool, n_seqs, seq_ids, n_q, group, q, out, scale, 0u, stream);
+}
+
+int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
+                         const void *k, const void *v, const void *q, void *out, float scale, uint32_t flags,
+                         void *stream) {
     if (!pool) return fail(GKV_ERR_INVALID, "null pool");
+    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16))
+        return fail(GKV_ERR_INVALID, "unknown flags 0x%x", flags);
     int rc = check_batch(pool, n_seqs, seq_ids);
     if (rc) return rc;
     if (n_q < 1 || group < 1) return fail(GKV_ERR_INVALID, "n_q=%d group=%d", n_q, group);
@@ -841,27 +960,44 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, in
                     "page_tokens >= 8)",
                     (long long)n_q * group);
     if (n_seqs > 0 && (!k || !v || !q || !out)) return fail(GKV_ERR_INVALID, "null k/v/q/out");
+    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t nkv = (size_t)n_seqs * n_q * pool->cfg.kv_heads * pool->cfg.head_dim;
+    const size_t nqo = nkv * group;
+    hs.in(&k, nkv * 2);
+    hs.in(&v, nkv * 2);
+    hs.in(&q, nqo * 2);
+    hs.out(&out, nqo * ((flags & GKV_ATTEND_OUT_F16) ? 2 : 4));
+    if ((rc = hs.reserve())) return rc;
     if (!aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(out))
         return fail(GKV_ERR_INVALID, "k/v/q/out not 16-byte aligned");
-    if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
     if (n_seqs > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}, {q, "q"}, {out, "out"}}))) return rc;
-    DeviceGuard guard(pool->cfg.device);
     std::vector<int32_t> n_new(n_seqs, n_q);
     std::vector<gkv::AppendEntry> entries;
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = hs.copy_in(st))) return rc;
     // Decode and verify steps of the split-K kernel (n_q*group <= 16, n_q <=
     // P) with TMA-staged pages and no shared tail page: the append rides
     // inside the attend kernel (one launch per layer).
     std::vector<gkv::FusedTail> tails;
     const bool fuse = (int64_t)n_q * group <= 16 && n_q <= pool->cfg.page_tokens && pool->cfg.page_tokens >= 8 &&
                       (pool->cfg.head_dim == 128 || pool->cfg.head_dim == 256) && fused_tails(pages, n_seqs, tails);
-    if (fuse) return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st, tails.data(), k, v);
-    rc = enqueue_append(pool, entries, pages, k, v, 0, st);
-    if (rc) return rc;
-    return enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, st);
+    if (fuse) {
+        rc = enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, flags, st, tails.data(), k, v);
+    } else {
+        rc = enqueue_append(pool, entries, pages, k, v, (flags & GKV_ATTEND_HEAD_MAJOR) ? 1 : 0, st);
+        if (!rc) rc = enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, flags, st);
+    }
+    return rc ? rc : hs.copy_out(st);
+}
+
+int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
+                      const void *k, const void *v, const void *q, float *out, float scale, void *stream) {
+    return gkv_append_attend_ex(pool, n_seqs, seq_ids, n_q, group, k, v, q, out, scale, 0u, stream);
 }
 
 int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t group, const float *q_gate,
@@ -880,6 +1016,31 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     if (!(std::isfinite(scale) && scale != 0.f)) return fail(GKV_ERR_INVALID, "scale must be finite and non-zero");
     if (n_seqs > 0 && (!q_gate || !k_raw || !v_raw || !q_norm || !k_norm || !rope_cos || !rope_sin || !out))
         return fail(GKV_ERR_INVALID, "null argument");
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the staging slots: they outlive every use of hs below
+    const void *in[7] = {q_gate, k_raw, v_raw, q_norm, k_norm, rope_cos, rope_sin};
+    void *o = out;
+    HostStage hs(pool);
+    {
+        const size_t n = (size_t)n_seqs, KVH = (size_t)pool->cfg.kv_heads, D = (size_t)dh;
+        const size_t nH = KVH * (size_t)group, hr = (size_t)(n_rot / 2);
+        const size_t in_bytes[7] = {n * nH * 2 * D * 4, n * KVH * D * 4, n * KVH * D * 4, D * 4, D * 4,
+                                    n * hr * 4, n * hr * 4};
+        if (n_seqs > 0) {
+            for (int i = 0; i < 7; ++i) hs.in(&in[i], in_bytes[i]);
+            hs.out(&o, n * nH * D * 4);
+            if ((rc = hs.reserve())) return rc;
+        }
+        q_gate = static_cast<const float *>(in[0]);
+        k_raw = static_cast<const float *>(in[1]);
+        v_raw = static_cast<const float *>(in[2]);
+        q_norm = static_cast<const float *>(in[3]);
+        k_norm = static_cast<const float *>(in[4]);
+        rope_cos = static_cast<const float *>(in[5]);
+        rope_sin = static_cast<const float *>(in[6]);
+        out = static_cast<float *>(o);
+    }
     if (!aligned16(q_gate) || !aligned16(k_raw) || !aligned16(v_raw) || !aligned16(out) ||
         ((reinterpret_cast<uintptr_t>(q_norm) | reinterpret_cast<uintptr_t>(k_norm) |
           reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 3))
@@ -888,20 +1049,20 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
                                                  {q_norm, "q_norm"}, {k_norm, "k_norm"}, {rope_cos, "rope_cos"},
                                                  {rope_sin, "rope_sin"}, {out, "out"}})))
         return rc;
-    DeviceGuard guard(pool->cfg.device);
     std::vector<int32_t> n_new(n_seqs, 1);
     std::vector<gkv::AppendEntry> entries;
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = hs.copy_in(st))) return rc;
     gkv::ProducerArgs prod{q_gate, k_raw, v_raw, q_norm, k_norm, rope_cos, rope_sin, n_rot, eps};
     // Same fusion rule as gkv_append_attend: TMA-staged pages and no shared
     // tail page -> the attend kernel's prologue builds and writes the rows.
     std::vector<gkv::FusedTail> tails;
     if (pool->cfg.page_tokens >= 8 && fused_tails(pages, n_seqs, tails)) {
-        return enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, st, tails.data(), nullptr,
-                              nullptr, &prod);
+        rc = enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, 0u, st, tails.data(), nullptr,
+                            nullptr, &prod);
+        return rc ? rc : hs.copy_out(st);
     }
     // Otherwise the rows are built by a small kernel, appended (copy-on-write
     // of a shared tail included), then attended.
@@ -910,7 +1071,9 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     GKV_CUDA(gkv::launch_produce_kv(pp, dh, st), "producer kernel launch");
     rc = enqueue_append(pool, entries, pages, pp.k_out, pp.v_out, 0, st);
     if (rc) return rc;
-    return enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, st, nullptr, nullptr, nullptr, &prod);
+    rc = enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, 0u, st, nullptr, nullptr, nullptr,
+                        &prod);
+    return rc ? rc : hs.copy_out(st);
 }
 
 int gkv_rope_table(int32_t n_rot, float base, int32_t n, const int64_t *positions, float *cos_out,
@@ -969,9 +1132,15 @@ int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, co
         rows += n_new[i];
     }
     if (rows > 0 && (!k || !v)) return fail(GKV_ERR_INVALID, "null k/v");
+    DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t kb = (size_t)rows * pool->cfg.kv_heads * pool->cfg.head_dim * 2;
+    hs.in(&k, kb);
+    hs.in(&v, kb);
+    if ((rc = hs.reserve())) return rc;
     if (!aligned16(k) || !aligned16(v)) return fail(GKV_ERR_INVALID, "k/v not 16-byte aligned");
     if (rows > 0 && (rc = check_buffers(pool, {{k, "k"}, {v, "v"}}))) return rc;
-    DeviceGuard guard(pool->cfg.device);
     // truncate (PagePool.truncate: pages pushed last-first), keeping an undo
     // log so that an append refused for lack of pages leaves no trace
     struct Undo {
@@ -1011,7 +1180,8 @@ int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, co
         }
         return rc;
     }
-    return enqueue_append(pool, entries, pages, k, v, 0, static_cast<cudaStream_t>(stream));
+    if ((rc = hs.copy_in(st))) return rc;
+    return enqueue_append(pool, entries, pages, k, v, 0, st);
 }
 
 int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream) {
@@ -1056,12 +1226,16 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stre
     const Seq *s = pool->seq(seq_id);
     if (!s) return fail(GKV_ERR_BAD_SEQ, "unknown sequence id %d", seq_id);
     if (s->len > 0 && (!K || !V)) return fail(GKV_ERR_INVALID, "null K/V");
-    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
-    if (s->len > 0) {
-        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
-        if (rc) return rc;
-    }
     DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t kb = (size_t)pool->cfg.kv_heads * s->len * pool->cfg.head_dim * 2;
+    hs.out(&K, kb);
+    hs.out(&V, kb);
+    int rc = hs.reserve();
+    if (rc) return rc;
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    if (s->len > 0 && (rc = check_buffers(pool, {{K, "K"}, {V, "V"}}))) return rc;
     gkv::CompactParams p{};
     p.table = pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq;
     p.k_pool = pool->d_k;
@@ -1073,8 +1247,8 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stre
     p.kvh = pool->cfg.kv_heads;
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
-    GKV_CUDA(gkv::launch_compact(p, static_cast<cudaStream_t>(stream)), "compact kernel launch");
-    return GKV_OK;
+    GKV_CUDA(gkv::launch_compact(p, st), "compact kernel launch");
+    return hs.copy_out(st);
 }
 
 int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, int32_t tile_p, void *K, void *V,
@@ -1089,10 +1263,16 @@ int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, in
         return fail(GKV_ERR_BAD_SEQ, "window [%lld, %lld) outside sequence %d of length %lld", (long long)start,
                     (long long)(start + count), seq_id, (long long)s->len);
     if (!K || !V) return fail(GKV_ERR_INVALID, "null K/V");
-    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
-    const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
-    if (rc) return rc;
     DeviceGuard guard(pool->cfg.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HostStage hs(pool);
+    const size_t kb = (size_t)pool->cfg.kv_heads * tile_p * pool->cfg.head_dim * 2;
+    hs.out(&K, kb);
+    hs.out(&V, kb);
+    int rc = hs.reserve();
+    if (rc) return rc;
+    if (!aligned16(K) || !aligned16(V)) return fail(GKV_ERR_INVALID, "K/V not 16-byte aligned");
+    if ((rc = check_buffers(pool, {{K, "K"}, {V, "V"}}))) return rc;
     gkv::CompactParams p{};
     p.table = pool->d_table + (size_t)seq_id * pool->cfg.max_pages_per_seq;
     p.k_pool = pool->d_k;
@@ -1105,8 +1285,8 @@ int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, in
     p.kvh = pool->cfg.kv_heads;
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
-    GKV_CUDA(gkv::launch_compact(p, static_cast<cudaStream_t>(stream)), "tile kernel launch");
-    return GKV_OK;
+    GKV_CUDA(gkv::launch_compact(p, st), "tile kernel launch");
+    return hs.copy_out(st);
 }
 
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V, int64_t length,
@@ -1115,8 +1295,11 @@ int gkv_from_compact(gkv_pool *pool, const void *K, const void *V, int64_t lengt
     if (length < 0) return fail(GKV_ERR_INVALID, "length=%lld", (long long)length);
     if (length > 0) {  // before a sequence is made, so a refused buffer leaves nothing behind
         if (!K || !V) return fail(GKV_ERR_INVALID, "null K/V");
-        const int rc = check_buffers(pool, {{K, "K"}, {V, "V"}});
-        if (rc) return rc;
+        for (const void *b : {K, V})  // pageable host memory: staged by gkv_seed below
+            if (!is_pageable(b)) {
+                const int rc = check_buffers(pool, {{b, b == K ? "K" : "V"}});
+                if (rc) return rc;
+            }
     }
     if (pool->pages_for(length) > (int64_t)pool->stack.size())
         return fail(GKV_ERR_NO_PAGES, "fromCompact needs %lld pages",

@@ -152,6 +152,18 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// A pair of softmax weights as two fp16 pairs whose sum carries them to
+// ~22 significant bits: hi = fp16(a), lo = fp16(a - hi) (a - hi is exact in
+// fp32).  P.V then runs as P_hi.V + P_lo.V on the tensor cores, so the
+// weights lose ~2^-22 of their value instead of fp16's ~2^-12.
+__device__ __forceinline__ void split_half2(float a0, float a1, uint32_t &hi, uint32_t &lo) {
+    __half2 h = __floats2half2_rn(a0, a1);
+    const float2 b = __half22float2(h);
+    __half2 l = __floats2half2_rn(a0 - b.x, a1 - b.y);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    lo = *reinterpret_cast<uint32_t *>(&l);
+}
+
 // Named barrier over the consumer warps only (the producer never joins).
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, 128;" ::: "memory");

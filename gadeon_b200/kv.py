@@ -39,6 +39,10 @@ GKV_ERR_BAD_SEQ = 4
 GKV_ERR_UNSUPPORTED = 5
 GKV_ERR_CAPACITY = 6
 
+# gkv_attend_ex / gkv_append_attend_ex flags
+GKV_ATTEND_HEAD_MAJOR = 1  # q / out [n, kv_heads, n_q, group, head_dim]; k / v [n, kv_heads, n_q, head_dim]
+GKV_ATTEND_OUT_F16 = 2     # out fp16, rounded to nearest even
+
 # Every entry point include/gadeon_kv.h declares.
 EXPORTED = (
     "gkv_last_error", "gkv_version", "gkv_pool_create", "gkv_pool_destroy", "gkv_seq_create",
@@ -49,7 +53,8 @@ EXPORTED = (
     "gkv_attend_noalloc", "gkv_mtp_rollback", "gkv_conv_rollback", "gkv_attn_step",
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
     "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16", "gkv_check_bounded_wait",
-    "gkv_tile_at", "gkv_gdn_rollback_f16", "gkv_gdn_rollback",
+    "gkv_tile_at", "gkv_gdn_rollback_f16", "gkv_gdn_rollback", "gkv_noalloc_status",
+    "gkv_attend_ex", "gkv_append_attend_ex",
 )
 
 
@@ -95,6 +100,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_seed": (C.c_int, [P, i32, P, P, i64, P]),
         "gkv_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, P]),
         "gkv_append_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, P]),
+        "gkv_attend_ex": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, C.c_uint32, P]),
+        "gkv_append_attend_ex": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, C.c_uint32, P]),
         "gkv_truncate": (C.c_int, [P, i32, i32p, i64p]),
         "gkv_rewind_append": (C.c_int, [P, i32, i32p, i64p, i32p, P, P, P]),
         "gkv_clone_seq": (C.c_int, [P, i32, i32p, P]),
@@ -107,6 +114,7 @@ def load_library(path: str = LIB_PATH):
         "gkv_device_status": (C.c_int, [P, i32p]),
         "gkv_attend_noalloc": (C.c_int, [P, P, i32, i32, i32, i32, P, i32, i32, i32p, i32, i32, P, P,
                                          f32, P]),
+        "gkv_noalloc_status": (C.c_int, [P, i32p]),
         "gkv_mtp_rollback": (C.c_int, [i32, i32p, i32, i32, i32, i32, P, P, P, P, P, P]),
         "gkv_attn_step": (C.c_int, [P, i32, i32p, i32, P, P, P, P, P, f32, P, P, i32, f32, P, P]),
         "gkv_rope_table": (C.c_int, [i32, f32, i32, i64p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
@@ -152,28 +160,40 @@ def _p64(a: np.ndarray):
 
 
 def _dev_ptr(t) -> Optional[int]:
-    """Address of a contiguous torch tensor a kernel can reach (or None): a
-    CUDA tensor, or a page-locked CPU tensor (``pin_memory()``), which the
-    kernels read and write in place over the host link.  The library checks
-    each address again and refuses host memory where an argument must be
-    device memory.  A host buffer must stay referenced and unchanged until
-    the stream has finished with it: torch's pinned-memory cache can hand a
-    freed block to the next pin_memory() at once."""
+    """Address of a contiguous torch tensor (or None): a CUDA tensor, a
+    page-locked CPU tensor (``pin_memory()``), which the kernels read and
+    write in place over the host link, or a plain CPU tensor, which the
+    library stages through device memory (the call returns with its output
+    in place).  The library checks each address again and refuses host
+    memory where an argument must be device memory.  A page-locked buffer
+    must stay referenced and unchanged until the stream has finished with
+    it: torch's pinned-memory cache can hand a freed block to the next
+    pin_memory() at once."""
     if t is None:
         return None
-    if not t.is_cuda and not (t.device.type == "cpu" and t.is_pinned()):
-        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU or in page-locked host memory")
+    if not t.is_cuda and t.device.type != "cpu":
+        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU or in host memory")
     if not t.is_contiguous():
         raise GkvError(GKV_ERR_INVALID, "tensor must be contiguous")
     return t.data_ptr()
 
 
+def _gpu_ptr(t) -> Optional[int]:
+    """Address of a contiguous CUDA tensor, for the entry points that take
+    device memory only (the GDN rollback)."""
+    if t is not None and not t.is_cuda:
+        raise GkvError(GKV_ERR_INVALID, "tensor must live on the GPU (this call takes device memory only)")
+    return _dev_ptr(t)
+
+
 def _empty_f32(shape, like):
-    """fp32 output beside `like`: on its GPU, or page-locked host memory."""
+    """fp32 output beside `like`: on its GPU, or in host memory of its kind
+    (page-locked or plain)."""
     import torch
     if like.is_cuda:
         return torch.empty(shape, dtype=torch.float32, device=like.device)
-    return torch.empty(shape, dtype=torch.float32).pin_memory()
+    out = torch.empty(shape, dtype=torch.float32)
+    return out.pin_memory() if like.is_pinned() else out
 
 
 def _check_shape(name, t, shape, dtypes):
@@ -270,40 +290,59 @@ class BlockPool:
             _check_shape(name, t, (self.kv_heads, count, self.head_dim), _F16)
         _check(_lib.gkv_seed(self._h, seq, _dev_ptr(K), _dev_ptr(V), count, _stream_ptr(stream)))
 
-    def attend(self, seq_ids: Sequence[int], n_q: int, group: int, q, out=None,
-               scale: Optional[float] = None, stream=None):
-        """q: [n, n_q, kv_heads*group, head_dim] fp16; returns fp32 of the same shape.
-        Row r of a sequence sees keys [0, length - n_q + r]."""
+    def _qo_shape(self, n: int, n_q: int, group: int, head_major: bool):
+        if head_major:
+            return (n, self.kv_heads, n_q, group, self.head_dim)
+        return (n, n_q, self.kv_heads * group, self.head_dim)
+
+    def _out(self, out, shape, q, out_f16: bool):
         import torch
-        ids = _i32(seq_ids)
-        qshape = (len(ids), n_q, self.kv_heads * group, self.head_dim)
-        _check_shape("q", q, qshape, _F16)
+        dt = torch.float16 if out_f16 else torch.float32
         if out is None:
-            out = _empty_f32(qshape, q)
-        _check_shape("out", out, qshape, ("float32",))
+            out = torch.empty(shape, dtype=dt, device=q.device)
+            if not q.is_cuda and q.is_pinned():
+                out = out.pin_memory()
+        _check_shape("out", out, shape, ("float16",) if out_f16 else ("float32",))
+        return out
+
+    def attend(self, seq_ids: Sequence[int], n_q: int, group: int, q, out=None,
+               scale: Optional[float] = None, stream=None, head_major: bool = False,
+               out_f16: bool = False):
+        """q: [n, n_q, kv_heads*group, head_dim] fp16 (head_major: the
+        reference's [n, kv_heads, n_q, group, head_dim]); returns the result
+        in q's layout, fp32 (out_f16: fp16).  Row r of a sequence sees keys
+        [0, length - n_q + r]."""
+        ids = _i32(seq_ids)
+        qshape = self._qo_shape(len(ids), n_q, group, head_major)
+        _check_shape("q", q, qshape, _F16)
+        out = self._out(out, qshape, q, out_f16)
         if scale is None:
             scale = self.head_dim ** -0.5
-        _check(_lib.gkv_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(q),
-                               _dev_ptr(out), float(scale), _stream_ptr(stream)))
+        flags = (GKV_ATTEND_HEAD_MAJOR if head_major else 0) | (GKV_ATTEND_OUT_F16 if out_f16 else 0)
+        _check(_lib.gkv_attend_ex(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(q),
+                                  _dev_ptr(out), float(scale), flags, _stream_ptr(stream)))
         return out
 
     def append_attend(self, seq_ids: Sequence[int], n_q: int, group: int, k, v, q, out=None,
-                      scale: Optional[float] = None, stream=None):
-        """Append n_q rows per sequence, then attend those n_q query rows."""
-        import torch
+                      scale: Optional[float] = None, stream=None, head_major: bool = False,
+                      out_f16: bool = False):
+        """Append n_q rows per sequence, then attend those n_q query rows.
+        k, v: [n * n_q, kv_heads, head_dim] (head_major: [n, kv_heads, n_q,
+        head_dim]); q / out as for :meth:`attend`."""
         ids = _i32(seq_ids)
-        qshape = (len(ids), n_q, self.kv_heads * group, self.head_dim)
+        n = len(ids)
+        qshape = self._qo_shape(n, n_q, group, head_major)
         _check_shape("q", q, qshape, _F16)
+        kshape = (n, self.kv_heads, n_q, self.head_dim) if head_major else (n * n_q, self.kv_heads, self.head_dim)
         for name, t in (("k", k), ("v", v)):
-            _check_shape(name, t, (len(ids) * n_q, self.kv_heads, self.head_dim), _F16)
-        if out is None:
-            out = _empty_f32(qshape, q)
-        _check_shape("out", out, qshape, ("float32",))
+            _check_shape(name, t, kshape, _F16)
+        out = self._out(out, qshape, q, out_f16)
         if scale is None:
             scale = self.head_dim ** -0.5
-        _check(_lib.gkv_append_attend(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(k),
-                                      _dev_ptr(v), _dev_ptr(q), _dev_ptr(out), float(scale),
-                                      _stream_ptr(stream)))
+        flags = (GKV_ATTEND_HEAD_MAJOR if head_major else 0) | (GKV_ATTEND_OUT_F16 if out_f16 else 0)
+        _check(_lib.gkv_append_attend_ex(self._h, n, _p32(ids), n_q, group, _dev_ptr(k),
+                                         _dev_ptr(v), _dev_ptr(q), _dev_ptr(out), float(scale), flags,
+                                         _stream_ptr(stream)))
         return out
 
     def attn_step(self, seq_ids: Sequence[int], group: int, q_gate, k_raw, v_raw, q_norm, k_norm,
@@ -536,6 +575,47 @@ def host_flash_decode(q, pool: PagePool, G: int, stream=None):
     return out.reshape(-1)
 
 
+def paged_flash_batched(q, pool: PagePool, s0_global_pos: int, s_count: int, G: int, out=None,
+                        stream=None):
+    """``pagedFlashBatched(q:pool:tile:s0GlobalPos:sCount:G:)``
+    (PagedAttention.swift:376-416) on the GPU: the S = s_count query rows
+    q [kv_heads, S, G, head_dim] fp16 at global positions s0_global_pos + s,
+    each seeing keys [0, s0_global_pos + s] of the pool (the band mask of
+    :512-529), scale = head_dim^-0.5.  Returns the normalized
+    [kv_heads, S, G, head_dim] fp32 result (the Swift returns it flat).  The
+    rows must be the pool's last S positions (the chunk appended first, as
+    Engine.batchedAttn does, Engine.swift:1797-1820)."""
+    bp = pool.block_pool
+    if s0_global_pos + s_count != pool.length:
+        raise GkvError(GKV_ERR_INVALID, f"rows {s0_global_pos}..{s0_global_pos + s_count - 1} are not the "
+                       f"last {s_count} positions of a pool of length {pool.length}")
+    qq = q.reshape(1, bp.kv_heads, s_count, G, bp.head_dim)
+    if out is not None:
+        out = out.reshape(1, bp.kv_heads, s_count, G, bp.head_dim)
+    res = bp.attend([pool.seq_id], s_count, G, qq, out=out, scale=bp.head_dim ** -0.5, stream=stream,
+                    head_major=True)
+    return res.reshape(bp.kv_heads, s_count, G, bp.head_dim)
+
+
+def verify_attn(pool: PagePool, k, v, q, G: int, out=None, stream=None):
+    """``Engine.verifyAttn`` (LLM/src/CoreML/Engine.swift:2620-2646) on the
+    GPU: append the L rows k, v [kv_heads, L, head_dim] fp16 to the pool and
+    attend query row s of q [kv_heads, L, G, head_dim] over the pool so far
+    (causal among the rows), scale = head_dim^-0.5, in one launch.  Returns
+    attn_out [kv_heads, L, G, head_dim] fp16 (each value rounded to nearest
+    even, as the Swift stores Float16)."""
+    bp = pool.block_pool
+    L = int(k.shape[1])
+    kk = k.reshape(1, bp.kv_heads, L, bp.head_dim)
+    vv = v.reshape(1, bp.kv_heads, L, bp.head_dim)
+    qq = q.reshape(1, bp.kv_heads, L, G, bp.head_dim)
+    if out is not None:
+        out = out.reshape(1, bp.kv_heads, L, G, bp.head_dim)
+    res = bp.append_attend([pool.seq_id], L, G, kk, vv, qq, out=out, scale=bp.head_dim ** -0.5,
+                           stream=stream, head_major=True, out_f16=True)
+    return res.reshape(bp.kv_heads, L, G, bp.head_dim)
+
+
 def mtp_rollback(m, s0, delta, k, gcum, out=None, stream=None):
     """``MtpRollback.stateAfter`` (LLM/src/CoreML/MtpRollback.swift:47-60) on the
     GPU for a batch of items (sequence x GDN layer): s0 [n, H, DK, DV],
@@ -559,8 +639,8 @@ def mtp_rollback(m, s0, delta, k, gcum, out=None, stream=None):
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
     fn = L.gkv_mtp_rollback_f16 if f16 else L.gkv_mtp_rollback
-    _check(fn(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k),
-              _dev_ptr(gcum), _dev_ptr(out), _stream_ptr(stream)))
+    _check(fn(n, _p32(mm), H, DK, DV, Cw, _gpu_ptr(s0), _gpu_ptr(delta), _gpu_ptr(k),
+              _gpu_ptr(gcum), _gpu_ptr(out), _stream_ptr(stream)))
     return out
 
 
@@ -583,7 +663,7 @@ def conv_rollback(m, proj, pre, out=None, stream=None):
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
     fn = L.gkv_conv_rollback_f16 if f16 else L.gkv_conv_rollback
-    _check(fn(n, _p32(mm), CD, taps, Cw, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(out), _stream_ptr(stream)))
+    _check(fn(n, _p32(mm), CD, taps, Cw, _gpu_ptr(proj), _gpu_ptr(pre), _gpu_ptr(out), _stream_ptr(stream)))
     return out
 
 
@@ -615,8 +695,8 @@ def gdn_rollback(m, s0, delta, k, gcum, proj, pre, out=None, conv_out=None, stre
     if len(mm) != n:
         raise GkvError(GKV_ERR_INVALID, f"m has {len(mm)} entries for {n} items")
     fn = L.gkv_gdn_rollback_f16 if sd == ("float16",) else L.gkv_gdn_rollback
-    _check(fn(n, _p32(mm), H, DK, DV, Cw, _dev_ptr(s0), _dev_ptr(delta), _dev_ptr(k), _dev_ptr(gcum), _dev_ptr(out),
-              CD, T, _dev_ptr(proj), _dev_ptr(pre), _dev_ptr(conv_out), _stream_ptr(stream)))
+    _check(fn(n, _p32(mm), H, DK, DV, Cw, _gpu_ptr(s0), _gpu_ptr(delta), _gpu_ptr(k), _gpu_ptr(gcum), _gpu_ptr(out),
+              CD, T, _gpu_ptr(proj), _gpu_ptr(pre), _gpu_ptr(conv_out), _stream_ptr(stream)))
     return out, conv_out
 
 

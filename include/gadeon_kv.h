@@ -18,23 +18,27 @@
  *     calling thread's message for its last failure.  A failing call leaves
  *     the pool unchanged (validation happens before any mutation).
  *   - K/V/Q and outputs of the pool calls are device memory of the pool's
- *     GPU, managed memory, or page-locked host memory mapped at the same
- *     address (cudaHostAlloc / cudaMallocHost / cudaHostRegister): the
- *     kernels read and write such host buffers in place over the host link,
- *     so a caller holding host arrays needs no copies of its own.  Pageable
- *     host memory cannot be reached by a kernel and is refused with
- *     GKV_ERR_INVALID before anything is enqueued.  A host buffer must stay
- *     valid and unchanged until the stream has finished the call.  The GDN
- *     rollback and gkv_attend_noalloc take device memory only.  Id and
- *     length arrays are HOST pointers.  `stream` is a cudaStream_t (NULL =
- *     the legacy default stream).  Work is enqueued asynchronously.
+ *     GPU, managed memory, page-locked host memory mapped at the same
+ *     address (cudaHostAlloc / cudaMallocHost / cudaHostRegister), or plain
+ *     pageable host memory.  The kernels read and write page-locked host
+ *     buffers in place over the host link; such a buffer must stay valid
+ *     and unchanged until the stream has finished the call.  A kernel cannot
+ *     reach pageable memory, so the call stages it through device memory
+ *     the pool owns (grown with cudaMalloc when a call needs more): one
+ *     cudaMemcpyAsync per pageable input before the launch, one per pageable
+ *     output after it.  A call with a pageable output returns once that
+ *     output is in place (it waits for the device); pageable inputs may be
+ *     reused as soon as the call returns.  The GDN rollback and
+ *     gkv_attend_noalloc take device memory only.  Id and length arrays are
+ *     HOST pointers.  `stream` is a cudaStream_t (NULL = the legacy default
+ *     stream).  Work is enqueued asynchronously.
  *   - Host bookkeeping (lengths, block tables, free list) is updated when the
  *     call returns; the device copy of the tables is updated in stream order.
  *   - A pool is not thread-safe: serialise calls on one pool (the reference
  *     serialises them inside one Swift actor, Engine.swift:41) and issue all
  *     of its work on one stream, or order the streams yourself.
  *   - fp16 values are IEEE binary16 bit patterns; attention accumulates in
- *     fp32 and writes fp32.
+ *     fp32 and writes fp32 (or fp16, GKV_ATTEND_OUT_F16).
  */
 #ifndef GADEON_KV_H
 #define GADEON_KV_H
@@ -133,6 +137,38 @@ int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                       int32_t n_q, int32_t group, const void *k,
                       const void *v, const void *q, float *out, float scale,
                       void *stream);
+
+/* Layout and output options of gkv_attend_ex / gkv_append_attend_ex. */
+enum gkv_attend_flags {
+    /* q and out [n_seqs, kv_heads, n_q, group, head_dim] -- per sequence
+     * the reference's [KVH, S, G, dh] (verifyAttn's q and attn_out,
+     * Engine.swift:2618-2646; pagedFlashBatched's q and result,
+     * PagedAttention.swift:370-376) -- and gkv_append_attend_ex's k and v
+     * [n_seqs, kv_heads, n_q, head_dim] (verifyAttn's k/v rows, [KVH, S, dh]
+     * per sequence, Engine.swift:2051-2072) */
+    GKV_ATTEND_HEAD_MAJOR = 1,
+    /* out holds fp16: each fp32 result rounded to nearest even (verifyAttn
+     * stores Float16(flat[...]), Engine.swift:2637) */
+    GKV_ATTEND_OUT_F16 = 2
+};
+
+/* gkv_attend with `flags` (gkv_attend_flags) choosing the layout of q and
+ * out and the type of out; written by the kernels directly, with no extra
+ * pass (pagedFlashBatched, PagedAttention.swift:376-416, with flags =
+ * GKV_ATTEND_HEAD_MAJOR).  flags == 0 is gkv_attend. */
+int gkv_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                  int32_t n_q, int32_t group, const void *q, void *out,
+                  float scale, uint32_t flags, void *stream);
+
+/* gkv_append_attend with `flags`: Engine.verifyAttn (Engine.swift:2620-2646)
+ * as one call with flags = GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16 --
+ * k, v [n_seqs, KVH, S, dh], q [n_seqs, KVH, S, G, dh], out fp16
+ * [n_seqs, KVH, S, G, dh].  flags == 0 is gkv_append_attend. */
+int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs,
+                         const int32_t *seq_ids, int32_t n_q, int32_t group,
+                         const void *k, const void *v, const void *q,
+                         void *out, float scale, uint32_t flags,
+                         void *stream);
 
 /* One decode token of a Qwen3.5 full-attention layer from its raw
  * projections, with the producer and the output gate fused into the append
@@ -304,9 +340,12 @@ int gkv_gdn_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK,
 
 /* Size of the library's static scratch array used by gkv_attend_noalloc
  * (held on every GPU that loads the library until the process exits), and
- * the largest batch that entry point takes. */
+ * the largest batch and kv-head count that entry point takes.  With at most
+ * GKV_NOALLOC_MAX_KV_HEADS kv heads every head_dim fits the array: a larger
+ * batch simply runs as more launches. */
 #define GKV_NOALLOC_SCRATCH_BYTES 8388608u
 #define GKV_NOALLOC_MAX_SEQS 1024
+#define GKV_NOALLOC_MAX_KV_HEADS 64
 
 /* Paged GQA decode / verify attention that allocates nothing.  No
  * counterpart in the reference.  For callers that own all device memory
@@ -316,19 +355,31 @@ int gkv_gdn_rollback(int32_t n_items, const int32_t *m, int32_t H, int32_t DK,
  * block table (device int32, row i = batch entry i, table_stride entries)
  * and q/out are the caller's; seq_lens is a HOST array of the n_seqs
  * lengths.  q, out, n_q, group and scale mean what they mean for
- * gkv_attend, and the results match it.  The kernel's scratch lives in one
- * static __device__ array of GKV_NOALLOC_SCRATCH_BYTES; a call that needs
- * more (too many sequences x kv heads for head_dim) or has more than
- * GKV_NOALLOC_MAX_SEQS sequences fails with GKV_ERR_CAPACITY.  The first
- * call on each device looks up that array's device address (set-up), so
- * make that first call before any stream capture.  Calls share the array:
- * calls that overlap on the GPU (other streams, other threads) race. */
+ * gkv_attend, and the results match it.  The kernel's scratch (merge
+ * counters, split-K partials, a status word) lives in one static __device__
+ * array of GKV_NOALLOC_SCRATCH_BYTES; nothing is copied from the host (the
+ * work descriptor rides in the kernel's parameter block, a batch of more
+ * than 128 sequences runs as several launches on `stream`).  More than
+ * GKV_NOALLOC_MAX_SEQS sequences or GKV_NOALLOC_MAX_KV_HEADS kv heads fail
+ * with GKV_ERR_CAPACITY.  A block-table entry outside [0, num_pages) is
+ * read as page 0 and recorded in the status word, which gkv_noalloc_status
+ * reports.  The first call on each device looks up that array's device
+ * address (set-up), so make that first call before any stream capture.
+ * Calls share the array: calls that overlap on the GPU (other streams,
+ * other threads) race. */
 int gkv_attend_noalloc(const void *k_pages, const void *v_pages,
                        int32_t num_pages, int32_t kv_heads, int32_t head_dim,
                        int32_t page_tokens, const int32_t *block_table,
                        int32_t table_stride, int32_t n_seqs,
                        const int32_t *seq_lens, int32_t n_q, int32_t group,
                        const void *q, float *out, float scale, void *stream);
+
+/* The device status bits gkv_attend_noalloc calls on the CURRENT device
+ * left since the last read (bit 1 = a bounded wait ran out, bit 2 = a
+ * block-table entry was outside the pages), then cleared.  Waits for
+ * `stream`.  No counterpart in the reference (its device errors surface
+ * through Metal command buffers, MetalGolden.swift:384). */
+int gkv_noalloc_status(void *stream, int32_t *status);
 
 /* ---- state export, for parity checks and debugging (synchronous) ---- */
 

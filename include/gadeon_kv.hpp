@@ -33,8 +33,9 @@
  * Buffers: fp16 values are passed as uint16_t bit patterns, like the
  * Swift's [UInt16] (compact / fromCompact).  Pointer arguments of append,
  * seed, hostFlashDecode and the batched BlockPool calls follow the C ABI:
- * device memory or page-locked host memory of the pool's device; pageable
- * host memory is refused.  compact() / fromCompact() and the
+ * device memory or page-locked host memory of the pool's device (read and
+ * written in place), or plain host memory, which the library stages through
+ * the pool's device memory.  compact() / fromCompact() and the
  * std::vector overload of hostFlashDecode take ordinary host memory.
  * Streams are cudaStream_t (nullptr = the legacy default stream).
  */
@@ -253,7 +254,7 @@ public:
         return {std::move(k), std::move(v)};
     }
     /* tileAt(_:_:_:) -- positions [start, start + count) into head-major
-     * [kvHeads, tileP, dh] fp16 tiles K and V (device or page-locked),
+     * [kvHeads, tileP, dh] fp16 tiles K and V (device or host memory),
      * rows count..tileP-1 zero. */
     void tileAt(int64_t start, int64_t count, int tileP, void *K, void *V, cudaStream_t s = nullptr) const {
         check(gkv_tile_at(bp_->handle(), id_, start, count, tileP, K, V, s));
@@ -336,50 +337,35 @@ private:
 
 /* hostFlashDecode(q:pool:G:) -- the newest query, q [kvHeads, G, dh] fp16,
  * attending every one of the pool's length() keys with scale dh^-0.5;
- * out [kvHeads*G*dh] fp32 (head h = kvh*G + g).  q and out: device or
- * page-locked memory.  An empty pool gives zeros, as the Swift (:323). */
+ * out [kvHeads*G*dh] fp32 (head h = kvh*G + g).  q and out: device,
+ * page-locked or plain host memory (plain host memory is staged by the
+ * library, and the call then waits for the result).  An empty pool gives
+ * zeros, as the Swift (:323). */
 inline void hostFlashDecode(const void *q, const PagePool &pool, int G, float *out, cudaStream_t s = nullptr) {
     if (G <= 0) throw Error(GKV_ERR_INVALID, "hostFlashDecode: G must be positive");
     if (pool.length() == 0) {
-        check_cuda(cudaMemsetAsync(out, 0, sizeof(float) * pool.kvHeads() * G * pool.dh(), s), "zero output");
+        const size_t bytes = sizeof(float) * pool.kvHeads() * G * pool.dh();
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, out) == cudaSuccess && a.type == cudaMemoryTypeUnregistered) {
+            std::memset(out, 0, bytes);
+        } else {
+            cudaGetLastError();
+            check_cuda(cudaMemsetAsync(out, 0, bytes, s), "zero output");
+        }
         return;
     }
     const int32_t id = pool.seqId();
     check(gkv_attend(pool.blockPool().handle(), 1, &id, 1, G, q, out, (float)std::pow((double)pool.dh(), -0.5), s));
 }
 
-/* The Swift's value-returning form: host q in, host [Float] out.  A
- * convenience: it allocates device staging on every call and waits for the
- * result; a decode loop keeps its own device or page-locked buffers and
- * calls the pointer form above. */
+/* The Swift's value-returning form: host q in, host [Float] out.  The
+ * vectors are plain (pageable) host memory, which the library stages
+ * through the pool's device memory; the call waits for the result. */
 inline std::vector<float> hostFlashDecode(const std::vector<uint16_t> &q, const PagePool &pool, int G) {
     const size_t nq = (size_t)pool.kvHeads() * (size_t)G * (size_t)pool.dh();
     if (G <= 0 || q.size() != nq) throw Error(GKV_ERR_INVALID, "hostFlashDecode: q must hold kvHeads*G*dh values");
-    int prev = 0;
-    check_cuda(cudaGetDevice(&prev), "get device");
-    check_cuda(cudaSetDevice(pool.blockPool().device()), "set device");
-    void *dq = nullptr;
-    float *dout = nullptr;
-    std::vector<float> out(nq);
-    cudaError_t e = cudaMalloc(&dq, nq * 2);
-    if (e == cudaSuccess) e = cudaMalloc((void **)&dout, nq * sizeof(float));
-    if (e == cudaSuccess) e = cudaMemcpy(dq, q.data(), nq * 2, cudaMemcpyHostToDevice);
-    int rc = GKV_OK;
-    std::string msg;
-    if (e == cudaSuccess) {
-        try {
-            hostFlashDecode(dq, pool, G, dout, nullptr);
-        } catch (const Error &err) {
-            rc = err.code;
-            msg = err.what();
-        }
-    }
-    if (e == cudaSuccess && rc == GKV_OK) e = cudaMemcpy(out.data(), dout, nq * sizeof(float), cudaMemcpyDeviceToHost);
-    cudaFree(dq);
-    cudaFree(dout);
-    cudaSetDevice(prev);
-    if (rc != GKV_OK) throw Error(rc, msg);
-    check_cuda(e, "hostFlashDecode staging");
+    std::vector<float> out(nq);  // zeros: an empty pool's result (PagedAttention.swift:323)
+    if (pool.length() > 0) hostFlashDecode(q.data(), pool, G, out.data(), nullptr);
     return out;
 }
 

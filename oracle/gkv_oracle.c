@@ -608,6 +608,8 @@ typedef struct {
     OrcPool *p;
     int n, n_q, G;
     const int32_t *ids;
+    const int32_t *rows; /* NULL: every row 0..n_q-1; else the n_rows chosen rows */
+    int n_rows;
     const uint16_t *q;
     float scale;
     float *out;
@@ -625,11 +627,12 @@ static void *causal_worker(void *arg) {
         pthread_mutex_lock(&J->mu);
         int64_t job = J->next++;
         pthread_mutex_unlock(&J->mu);
-        if (job >= (int64_t)J->n * J->n_q) break;
-        int b = (int)(job / J->n_q), r = (int)(job % J->n_q);
+        if (job >= (int64_t)J->n * J->n_rows) break;
+        int b = (int)(job / J->n_rows), i = (int)(job % J->n_rows);
+        int r = J->rows ? J->rows[i] : i;
         OrcSeq *s = get_seq(p, J->ids[b]);
         int64_t nk = s->len - J->n_q + r + 1;
-        int64_t row = (int64_t)b * J->n_q + r;
+        int64_t row = (int64_t)b * J->n_rows + i;
         flash_decode_one(p, s, J->q + row * H * p->dh, J->G, J->scale, nk,
                          J->out + row * H * p->dh, work);
     }
@@ -637,9 +640,9 @@ static void *causal_worker(void *arg) {
     return NULL;
 }
 
-int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
-                      const uint16_t *q, int G, float scale, float *out,
-                      int n_threads) {
+static int attend_jobs(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
+                       const int32_t *rows, int n_rows, const uint16_t *q, int G,
+                       float scale, float *out, int n_threads) {
     int64_t max_len = 1;
     if (p->dh > 1024) return ORC_ERR_INVALID;
     for (int b = 0; b < n; b++) {
@@ -647,12 +650,14 @@ int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
         if (!s || s->len < n_q || n_q < 1) return ORC_ERR_BAD_SEQ;
         if (s->len > max_len) max_len = s->len;
     }
+    for (int i = 0; rows && i < n_rows; i++)
+        if (rows[i] < 0 || rows[i] >= n_q) return ORC_ERR_INVALID;
     /* the mirror grows once per sequence before the rows fan out */
     for (int b = 0; b < n; b++) {
         OrcSeq *s = get_seq(p, seq_ids[b]);
         grow_mirror(p, s, s->len);
     }
-    CausalJob J = {p, n, n_q, G, seq_ids, q, scale, out, 0,
+    CausalJob J = {p, n, n_q, G, seq_ids, rows, n_rows, q, scale, out, 0,
                    PTHREAD_MUTEX_INITIALIZER, max_len};
     if (n_threads < 1) n_threads = 1;
     if (n_threads == 1) {
@@ -663,6 +668,37 @@ int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
     for (int i = 0; i < n_threads; i++) pthread_create(&th[i], NULL, causal_worker, &J);
     for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
     free(th);
+    return ORC_OK;
+}
+
+int orc_attend_causal(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
+                      const uint16_t *q, int G, float scale, float *out,
+                      int n_threads) {
+    return attend_jobs(p, n, seq_ids, n_q, NULL, n_q, q, G, scale, out, n_threads);
+}
+
+/* The same causal attend for chosen query rows only (test helper, for
+ * full-size chunks whose every row would take the CPU too long): for each
+ * sequence b and each i < n_rows, query row rows[i] of b's last n_q
+ * positions sees keys [0, len_b - n_q + rows[i]].  q holds those rows only,
+ * [n, n_rows, KVH*G, dh] fp16; out the same shape, fp32. */
+int orc_attend_rows(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
+                    const int32_t *rows, int n_rows, const uint16_t *q, int G,
+                    float scale, float *out, int n_threads) {
+    if (!rows || n_rows < 1) return ORC_ERR_INVALID;
+    return attend_jobs(p, n, seq_ids, n_q, rows, n_rows, q, G, scale, out, n_threads);
+}
+
+/* Frees a sequence's fp32 mirror (test helper: bounds the host memory of
+ * full-size checks over many long sequences); the next attend widens its
+ * rows again, so results do not change. */
+int orc_seq_drop_mirror(OrcPool *p, int seq) {
+    OrcSeq *s = get_seq(p, seq);
+    if (!s) return ORC_ERR_BAD_SEQ;
+    free(s->kf);
+    free(s->vf);
+    s->kf = s->vf = NULL;
+    s->mcap = s->f32len = 0;
     return ORC_OK;
 }
 

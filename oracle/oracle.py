@@ -74,6 +74,9 @@ def lib():
         "orc_flash_decode": (C.c_int, [P, C.c_int, u16p, C.c_int, C.c_float, f32p]),
         "orc_attend_causal": (
             C.c_int, [P, C.c_int, i32p, C.c_int, u16p, C.c_int, C.c_float, f32p, C.c_int]),
+        "orc_attend_rows": (
+            C.c_int, [P, C.c_int, i32p, C.c_int, i32p, C.c_int, u16p, C.c_int, C.c_float, f32p, C.c_int]),
+        "orc_seq_drop_mirror": (C.c_int, [P, C.c_int]),
         "orc_mtp_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p,
                                     f32p, f32p]),
         "orc_conv_rollback": (None, [C.c_int, i32p, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p]),
@@ -240,6 +243,27 @@ class OraclePool:
         if rc:
             raise ValueError(f"orc_attend_causal rc={rc}")
         return out
+
+
+    def attend_rows(self, seq_ids, n_q: int, rows, q: np.ndarray, G: int, scale: float,
+                    n_threads: int = 1) -> np.ndarray:
+        """attend_causal for chosen rows of each sequence's last n_q
+        positions: q [n, len(rows), KVH*G, dh] fp16 bits (those rows only)
+        -> same shape fp32; row rows[i] sees keys [0, len - n_q + rows[i]]."""
+        ids = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        rr = np.ascontiguousarray(rows, dtype=np.int32)
+        q = np.ascontiguousarray(q, dtype=np.uint16)
+        out = np.zeros(q.shape, dtype=np.float32)
+        rc = lib().orc_attend_rows(self._h, len(ids), _ptr(ids, C.c_int32), n_q, _ptr(rr, C.c_int32), len(rr),
+                                   _ptr(q, C.c_uint16), G, scale, _ptr(out, C.c_float), n_threads)
+        if rc:
+            raise ValueError(f"orc_attend_rows rc={rc}")
+        return out
+
+    def drop_mirror(self, seq: int):
+        """Free the sequence's fp32 mirror (host memory); results unchanged."""
+        if lib().orc_seq_drop_mirror(self._h, seq):
+            raise ValueError(f"unknown sequence {seq}")
 
 
 def mtp_rollback(m, s0, delta, k, gcum) -> np.ndarray:

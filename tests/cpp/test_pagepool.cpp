@@ -81,20 +81,19 @@ struct Dev {
     }
 };
 
-// The attention tolerance of the path (fp16 storage, fp32 accumulation):
-// max-abs 2e-3 and L2-relative 1e-2 against the oracle.
+// The attention tolerance of the path (fp16 storage, fp32 accumulation),
+// element-wise against the oracle: |got - want| <= 2e-3 everywhere, and
+// <= 1e-2 * |want| wherever |want| >= 2e-3.
 void check_attn(const std::vector<float> &got, const std::vector<float> &want, const char *what) {
-    double max_abs = 0, num = 0, den = 0;
+    double max_abs = 0, max_rel = 0;
     bool finite = true;
     for (size_t i = 0; i < want.size(); ++i) {
         if (!std::isfinite(got[i])) finite = false;
-        const double d = (double)got[i] - want[i];
-        max_abs = std::fmax(max_abs, std::fabs(d));
-        num += d * d;
-        den += (double)want[i] * want[i];
+        const double d = std::fabs((double)got[i] - want[i]);
+        max_abs = std::fmax(max_abs, d);
+        if (std::fabs(want[i]) >= 2e-3) max_rel = std::fmax(max_rel, d / std::fabs((double)want[i]));
     }
-    const double rel = den > 0 ? std::sqrt(num / den) : std::sqrt(num);
-    CHECK(finite && max_abs <= 2e-3 && rel <= 1e-2, "%s: max-abs %.3e rel %.3e", what, max_abs, rel);
+    CHECK(finite && max_abs <= 2e-3 && max_rel <= 1e-2, "%s: max-abs %.3e max-rel %.3e", what, max_abs, max_rel);
 }
 
 std::vector<int32_t> gpu_table(const gadeon::PagePool &s) {
@@ -299,11 +298,6 @@ void run() {
         CHECK(thrown_code([&] { a.seed(dK.p, dV.p, prefill); }) == GKV_ERR_BAD_SEQ, "seed of a non-empty sequence");
     }
     {
-        std::vector<uint16_t> pageable((size_t)KVH * DH, 0);
-        CHECK(thrown_code([&] { a.append(pageable.data(), pageable.data()); }) == GKV_ERR_INVALID,
-              "append from pageable host memory");
-    }
-    {
         const int64_t too_long = (int64_t)(PAGES + 1) * P;
         std::vector<uint16_t> big((size_t)KVH * too_long * DH, 0);
         CHECK(thrown_code([&] { gadeon::PagePool::fromCompact(bp, big, big, too_long); }) == GKV_ERR_NO_PAGES,
@@ -311,6 +305,17 @@ void run() {
     }
     CHECK(bp.freePageCount() == free_before, "a refused call changed the free list");
     check_state(a, o, oa, "after refused calls");
+
+    // plain (pageable) host arrays: the library stages them through device
+    // memory, and the append lands as from device buffers
+    {
+        std::vector<uint16_t> kp = normal(901, (size_t)KVH * DH), vp = normal(902, (size_t)KVH * DH);
+        a.append(kp.data(), vp.data());
+        int32_t id = oa, one = 1;
+        CHECK(orc_append(o, 1, &id, &one, kp.data(), vp.data()) == 0, "oracle append");
+        check_state(a, o, oa, "after an append from pageable host memory");
+        check_decode(a, o, oa, 903, "decode after an append from pageable host memory");
+    }
 
     // release (destructors, last page first) returns every page
     {

@@ -1,13 +1,13 @@
-"""Host buffers at the C ABI: page-locked memory in place, pageable memory refused.
+"""Host buffers at the C ABI: page-locked memory in place, pageable memory staged.
 
 The reference's callers hand the cache host arrays (hostFlashDecode takes q
 and returns a [Float], LLM/src/CoreML/PagedAttention.swift:317-366).  Here q,
 k, v and out of the hot-path calls may be page-locked host memory mapped into
 the GPU's address space: the kernels read and write them in place over the
 host link.  Results must equal those of the same calls with device buffers
-bit for bit (same kernel, same arithmetic), and pageable host memory -- which
-a kernel cannot reach -- must be refused before anything is launched or the
-pool changes.
+bit for bit (same kernel, same arithmetic).  Pageable host memory -- which a
+kernel cannot reach -- is staged by the library through the pool's device
+memory, with the same results.
 """
 import ctypes as C
 
@@ -76,51 +76,87 @@ def test_pinned_host_buffers_match_device_buffers(cuda, oracle):
     host.check_state()
 
 
-def test_pageable_host_memory_refused(cuda, oracle):
-    """Pointers into plain (pageable) host memory are refused with
-    GKV_ERR_INVALID by the C ABI itself, before any launch: lengths, tables,
-    free list and pages stay as they were."""
+def test_pageable_host_buffers_staged(cuda, oracle):
+    """Plain (pageable) host arrays -- what a Swift [Float] or a numpy array
+    is -- are staged by the library through device memory of the pool: the
+    call copies them in and the output back (one cudaMemcpyAsync each) and
+    returns with the result in place.  Every hot-path call gives the same
+    bits as with device buffers, and the cache state stays bit-exact."""
     import gadeon_b200 as gk
-    from gadeon_b200 import GKV_ERR_INVALID, GkvError
     torch = cuda
-    G, dh, kvh = 4, 128, 2
-    pr = Pair(cuda, oracle, kvh=kvh, dh=dh, P=16, num_pages=40, seed=3)
-    s = pr.new_seq()
-    pr.append([s], [20])
-    torch.cuda.synchronize()
+    G, dh, P, kvh = 4, 128, 16, 2
+    nH = kvh * G
+    dev = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=300, seed=5)
+    host = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=300, seed=5)
+    ids = [dev.new_seq() for _ in range(4)]
+    assert [host.new_seq() for _ in range(4)] == ids
     lib = gk.load_library()
-    ids = np.array([s], dtype=np.int32)
-    pid = ids.ctypes.data_as(C.POINTER(C.c_int32))
-    # 16-byte aligned pageable buffers
-    q = np.zeros(kvh * G * dh + 64, dtype=np.float16)
-    kv = np.zeros(kvh * dh + 64, dtype=np.float16)
-    out = np.zeros(kvh * G * dh + 64, dtype=np.float32)
+    idarr = np.array(ids, dtype=np.int32)
+    pid = idarr.ctypes.data_as(C.POINTER(C.c_int32))
+    scale = C.c_float(dh ** -0.5)
 
-    def aligned(a):
-        p = a.ctypes.data
-        return p + (-p) % 16
+    def pageable(a):  # a fresh, plain numpy copy (malloc'd memory)
+        return np.array(a, copy=True, order="C")
 
-    qd = dev_f16(torch, oracle.normal_f16(1, 1, (1, 1, kvh * G, dh)))
-    outd = torch.empty((1, 1, kvh * G, dh), dtype=torch.float32, device="cuda")
-    one = np.array([1], dtype=np.int32)
-    calls = [
-        lambda: lib.gkv_attend(pr.gpu._h, 1, pid, 1, G, aligned(q), outd.data_ptr(), C.c_float(0.1), None),
-        lambda: lib.gkv_attend(pr.gpu._h, 1, pid, 1, G, qd.data_ptr(), aligned(out), C.c_float(0.1), None),
-        lambda: lib.gkv_append_attend(pr.gpu._h, 1, pid, 1, G, aligned(kv), aligned(kv), qd.data_ptr(),
-                                      outd.data_ptr(), C.c_float(0.1), None),
-        lambda: lib.gkv_append(pr.gpu._h, 1, pid, one.ctypes.data_as(C.POINTER(C.c_int32)), aligned(kv),
-                               aligned(kv), None),
-    ]
-    for call in calls:
-        assert call() == GKV_ERR_INVALID
-        assert "pageable" in lib.gkv_last_error().decode()
-    # the Python layer refuses an unpinned CPU tensor too
-    with pytest.raises(GkvError) as ei:
-        pr.gpu.attend([s], 1, G, torch.zeros((1, 1, kvh * G, dh), dtype=torch.float16))
-    assert ei.value.code == GKV_ERR_INVALID
+    # gkv_append from pageable k/v (the C ABI, numpy pointers)
+    ctx = np.array([5, 17, 300, 40], dtype=np.int32)
+    k, v = dev.rows(int(ctx.sum()))
+    dev.gpu.append(ids, ctx, dev_f16(torch, k), dev_f16(torch, v))
+    kp, vp = pageable(k), pageable(v)
+    assert lib.gkv_append(host.gpu._h, 4, pid, ctx.ctypes.data_as(C.POINTER(C.c_int32)), kp.ctypes.data,
+                          vp.ctypes.data, None) == 0, lib.gkv_last_error()
+    for pr in (dev, host):
+        assert pr.orc.append(ids, ctx, k, v) == 0
+    # decode steps and an MTP verify through gkv_append_attend with pageable
+    # k/v/q/out: out holds the result when the call returns
+    for step, n_q in enumerate([1, 1, 4, 1, 40]):
+        k, v = dev.rows(4 * n_q)
+        q = oracle.normal_f16(71, step, (4, n_q, nH, dh))
+        want = dev.gpu.append_attend(ids, n_q, G, dev_f16(torch, k), dev_f16(torch, v), dev_f16(torch, q))
+        kp, vp, qp = pageable(k), pageable(v), pageable(q)
+        outp = np.full((4, n_q, nH, dh), np.nan, dtype=np.float32)
+        rc = lib.gkv_append_attend(host.gpu._h, 4, pid, n_q, G, kp.ctypes.data, vp.ctypes.data, qp.ctypes.data,
+                                   outp.ctypes.data, scale, None)
+        assert rc == 0, lib.gkv_last_error()
+        assert np.array_equal(outp, want.cpu().numpy()), f"step {step}"
+        for pr in (dev, host):
+            assert pr.orc.append(ids, [n_q] * 4, k, v) == 0
+    # gkv_attend: pageable q, device out; then device q, pageable out
+    q = oracle.normal_f16(72, 0, (4, 1, nH, dh))
+    want = dev.gpu.attend(ids, 1, G, dev_f16(torch, q)).cpu().numpy()
+    outd = torch.empty((4, 1, nH, dh), dtype=torch.float32, device="cuda")
+    qp = pageable(q)
+    assert lib.gkv_attend(host.gpu._h, 4, pid, 1, G, qp.ctypes.data, outd.data_ptr(), scale, None) == 0
+    assert np.array_equal(outd.cpu().numpy(), want)
+    outp = np.zeros((4, 1, nH, dh), dtype=np.float32)
+    assert lib.gkv_attend(host.gpu._h, 4, pid, 1, G, dev_f16(torch, q).data_ptr(), outp.ctypes.data, scale,
+                          None) == 0
+    assert np.array_equal(outp, want)
+    # compact and tileAt into pageable buffers, fromCompact from them
+    n = host.gpu.length(ids[2])
+    Kp = np.zeros((kvh, n, dh), dtype=np.uint16)
+    Vp = np.zeros_like(Kp)
+    assert lib.gkv_compact_seq(host.gpu._h, ids[2], Kp.ctypes.data, Vp.ctypes.data, None) == 0
+    oK, oV = host.orc.compact(ids[2])
+    assert np.array_equal(Kp, oK) and np.array_equal(Vp, oV)
+    Tk = np.full((kvh, 32, dh), 7, dtype=np.uint16)
+    Tv = np.full_like(Tk, 7)
+    assert lib.gkv_tile_at(host.gpu._h, ids[2], 16, 20, 32, Tk.ctypes.data, Tv.ctypes.data, None) == 0
+    wk, wv = host.orc.tile_at(ids[2], 16, 20, 32)
+    assert np.array_equal(Tk, wk) and np.array_equal(Tv, wv)
+    new = C.c_int32(-1)
+    assert lib.gkv_from_compact(host.gpu._h, Kp.ctypes.data, Vp.ctypes.data, n, C.byref(new), None) == 0
+    assert host.orc.from_compact(oK, oV, n) == new.value
+    host.seqs.append(new.value)
+    # the Python layer passes plain CPU tensors through: the result comes back
+    # as a plain CPU tensor
+    q = oracle.normal_f16(73, 0, (4, 1, nH, dh))
+    got = host.gpu.attend(ids, 1, G, torch.from_numpy(q.view(np.int16)).view(torch.float16))
+    assert not got.is_cuda and not got.is_pinned()
+    assert np.array_equal(got.numpy(), dev.gpu.attend(ids, 1, G, dev_f16(torch, q)).cpu().numpy())
     torch.cuda.synchronize()
-    assert pr.gpu.length(s) == 20
-    pr.check_state()
+    dev.check_state()
+    host.check_state()
 
 
 def test_gdn_rollback_refuses_host_memory(cuda, oracle):

@@ -5,10 +5,9 @@ q|gate split, q/k RMSNorm (Kernels.swift:26-37), partial NEOX RoPE
 (Attention.swift:133-135) -- against the oracle's restatement of each step
 followed by its append and hostFlashDecode.
 
-Outputs within the attention tolerance.  Block tables and the free list are
-bit-exact; page bytes are bit-exact except the appended K rows, which the GPU
-normalises with a tree-ordered sum of squares: they may differ from the
-oracle's sequential sum by one fp16 unit in the last place."""
+Outputs within the attention tolerance.  Block tables, the free list and
+page bytes are bit-exact, the producer-built K rows included: the GPU forms
+RMSNorm's sum of squares in the reference's sequential order."""
 import numpy as np
 import pytest
 
@@ -116,8 +115,9 @@ class StepPair:
         return got, want
 
     def check_state(self):
-        """Tables, free list, lengths, refcounts bit-exact; page bytes exact
-        up to one fp16 ulp in the producer-built K rows."""
+        """Tables, free list, lengths, refcounts and page bytes bit-exact --
+        the producer-built K rows included (RMSNorm's sum of squares in the
+        reference's sequential order, every product and sum rounded)."""
         pr = self.pr
         pr.check_state(pages=False)
         for s in pr.seqs:
@@ -126,8 +126,7 @@ class StepPair:
                 ok, ov = pr.orc.page_bytes(int(pid))
                 assert np.array_equal(gv, ov), f"V page {pid}"
                 d = np.abs(gk.astype(np.int32) - ok.astype(np.int32))
-                assert d.max() <= 1, f"K page {pid}: {d.max()} ulp"
-                assert (d > 0).mean() < 0.02, f"K page {pid}: {(d > 0).mean():.3f} of the bytes differ"
+                assert np.array_equal(gk, ok), f"K page {pid}: {(d > 0).sum()} values differ, max {d.max()} ulp"
 
 
 @pytest.mark.gpu
