@@ -624,29 +624,42 @@ def measure_config3(args, rank, world, local, W, K, repeats):
     vv = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     out = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
     lens = ctx.copy()
-    lens_at = []
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+    # per timed block: the contexts each launch attends over, and an event
+    # pair around each launch
+    lens_at = [[] for _ in range(repeats)]
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+          for _ in range(repeats)]
+    timed = 0
 
     def step(i, ti):
         # one public call per layer appends the drafts and verifies them (the
         # append rides in the attend launch); the event bracket times it
-        nonlocal lens
+        nonlocal lens, timed
+        blk = timed // K
         for layer in range(L):
             if ti is not None:
-                ev[ti * L + layer][0].record()
+                ev[blk][ti * L + layer][0].record()
             pools[layer].append_attend(ids[layer], nq, G, kk, vv, q, out=out)
             if ti is not None:
-                ev[ti * L + layer][1].record()
+                ev[blk][ti * L + layer][1].record()
         if ti is not None:
-            lens_at.append(lens + nq)
+            lens_at[blk].append(lens + nq)
+            timed += 1
         lens = lens + acc[i]
         for layer in range(L):
             pools[layer].truncate(ids[layer], lens)
 
     ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, repeats)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)  # the last block's launches
-    launch_ms = max_over_ranks(torch, dist, world, local, launch_ms)
-    bpl = statistics.mean(decode_bytes(la, cfg) for la in lens_at) + append_bytes(S * nq, cfg)
+    # each block's mean launch time (max over ranks) and algorithmic bytes;
+    # the roofline is the median block's
+    blk_ms = torch.tensor([statistics.mean(a.elapsed_time(b) for a, b in e) for e in ev],
+                          device=torch.device("cuda", local), dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(blk_ms, op=dist.ReduceOp.MAX)
+    blk_bytes = [statistics.mean(decode_bytes(la, cfg) for la in b) + append_bytes(S * nq, cfg) for b in lens_at]
+    blk_gbs = [by / (t * 1e-3) / 1e9 for by, t in zip(blk_bytes, blk_ms.tolist())]
+    mid = sorted(range(repeats), key=lambda r: blk_gbs[r])[repeats // 2]
+    launch_ms, bpl = blk_ms.tolist()[mid], blk_bytes[mid]
     hbm, kind = peaks()
     for p in pools:
         assert p.device_status() == 0
@@ -666,7 +679,8 @@ def measure_config3(args, rank, world, local, W, K, repeats):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append> (n_q=4)",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms,
-                     "launch_timing": "CUDA events around each launch (the last timed block)"},
+                     "block_gbs": blk_gbs,
+                     "launch_timing": "CUDA events around each launch; the block with the median GB/s"},
         "accepted_draft_tok_per_s": float(acc[W:].sum() * world / (K * ms * 1e-3)),
         "gpu_launches": K * L * repeats, "clocks": clk}
 
