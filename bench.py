@@ -524,15 +524,17 @@ def run_ours(args, rank, world, local):
 def make_pools(torch, cfg, ctx, L, rank, seed, growth, local, factor=1.25, distinct=True):
     """One BlockPool per layer (its own seeded page permutation); sequence i
     seeded with ctx[i] rows of N(0,1) fp16 from torch's seeded device RNG.
-    distinct=False draws one random buffer per layer and seeds every
-    sequence from its prefix (values do not change the memory traffic)."""
+    distinct=False fills every sequence by appends of one 4,096-row block
+    drawn per layer (it stays in L2, so filling costs only the page writes;
+    values do not change the memory traffic of the timed steps)."""
     from gadeon_b200 import BlockPool
     KVH, dh, P = cfg.kv_heads, cfg.head_dim, cfg.page_tokens
     dev = torch.device("cuda", local)
     cmax = int(max(ctx))
     max_pps = int(math.ceil((cmax + growth) / P)) + 2
     n_pages = pool_pages(ctx, P, growth, factor)
-    scratch = torch.empty(2 * KVH * cmax * dh, dtype=torch.float16, device=dev)
+    block = 4096
+    scratch = torch.empty(2 * KVH * (cmax if distinct else block) * dh, dtype=torch.float16, device=dev)
     gen = torch.Generator(device=dev)
     pools, ids = [], []
     for layer in range(L):
@@ -541,15 +543,20 @@ def make_pools(torch, cfg, ctx, L, rank, seed, growth, local, factor=1.25, disti
         gen.manual_seed(seed * 7919 + rank * 131 + layer)
         if not distinct:
             torch.randn(scratch.shape, generator=gen, device=dev, dtype=torch.float16, out=scratch)
+            rows = scratch.view(2, block, KVH, dh)  # token-major K and V rows
         lids = []
         for c in ctx:
             c = int(c)
             sid = pool.seq_create()
-            buf = scratch[: 2 * KVH * c * dh]
             if distinct:
+                buf = scratch[: 2 * KVH * c * dh]
                 torch.randn(buf.shape, generator=gen, device=dev, dtype=torch.float16, out=buf)
-            kv = buf.view(2, KVH, c, dh)
-            pool.seed(sid, kv[0], kv[1], c)
+                kv = buf.view(2, KVH, c, dh)
+                pool.seed(sid, kv[0], kv[1], c)
+            else:
+                for t0 in range(0, c, block):
+                    n = min(block, c - t0)
+                    pool.append([sid], [n], rows[0, :n], rows[1, :n])
             lids.append(sid)
         pools.append(pool)
         ids.append(lids)
