@@ -55,8 +55,16 @@ UNIT = "tok/s"
 
 # DRAM bytes (read + write) per algorithmic byte of the config-2 attend
 # launch, from `ncu --set full` of one launch of the same per-layer workload
-# (64 sequences, 1 layer): 2.2970 GB measured / 2.2898 GB algorithmic.
-NCU_C2_TRAFFIC_PER_ALGO_BYTE = 2.2970 / 2.2898
+# (64 sequences, 1 layer): 2.2913 GB read + 4.6 MB written / 2.2899 GB
+# algorithmic.
+NCU_C2_TRAFFIC_PER_ALGO_BYTE = (2.291264e9 + 4.597504e6) / 2289898428.0
+# The same for the config-3 verify launch (32 of the 128 sequences, one
+# launch): 1.0811 GB read + 6.9 MB written / 1.0876 GB algorithmic.
+NCU_C3_TRAFFIC_PER_ALGO_BYTE = (1.0811e9 + 6.90688e6) / 1087551873.375
+# DRAM bytes per sequence of one config-4 chunk launch, from `ncu --set full`
+# of the 2-sequence case (245.2 MB read + 103.4 MB written): every sequence
+# streams its own K/V, so a full launch moves about 32 x this.
+NCU_C4_DRAM_PER_SEQ = (245.167104e6 + 103.359744e6) / 2
 # The same for the fused fp16 GDN rollback launch of config 6 (full-size
 # workload, launches 6-8): 2.5335 GB measured / 2.6911 GB algorithmic; the
 # shortfall is written state still dirty in L2 when the launch ends.
@@ -504,8 +512,8 @@ def run_ours(args, rank, world, local):
                  "staged_copy_value": tokens / (e2e_copy_max * 1e-3),
                  "staged_copy_note": "same step with cudaMemcpyAsync H2D/D2H around each call",
                  "pageable_value": tokens / (e2e_page_max * 1e-3),
-                 "pageable_note": "same step given plain (pageable) host arrays, which the library stages "
-                                  "through pool-owned device memory (one cudaMemcpyAsync per buffer)"}
+                 "pageable_note": "same step given plain (pageable) host arrays, which the library copies "
+                                  "through a pool-owned page-locked bounce buffer read and written in place"}
                 if e2e else None),
         "gpu_launches": K * L * R,
         "clocks": clk,
@@ -684,7 +692,10 @@ def measure_config3(args, rank, world, local, W, K, repeats):
                    "kv_heads": KVH, "n_heads": nH, "head_dim": dh, "page_tokens": cfg.page_tokens,
                    "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)" % (float(ctx.sum()) * KVH * dh * 4 / 1e9)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None, "kernel": "attend_kernel<256,TMA,fused append> (n_q=4)",
+                     "peak_kind": kind, "traffic": NCU_C3_TRAFFIC_PER_ALGO_BYTE * bpl,
+                     "traffic_source": "ncu dram__bytes_read+write of one verify launch over 32 of the sequences, "
+                                       "scaled by algorithmic bytes",
+                     "kernel": "attend_kernel<256,TMA,fused append> (n_q=4)",
                      "bytes_per_launch": bpl, "launch_ms": launch_ms,
                      "block_gbs": blk_gbs,
                      "launch_timing": "CUDA events around each launch; the block with the median GB/s"},
@@ -761,7 +772,10 @@ def measure_config4(args, rank, world, local, W, K, repeats, seqs=None):
                    "head_dim": dh, "page_tokens": cfg.page_tokens, "l2": "inputs larger than L2"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
-                     "traffic": None, "kernel": "chunk_kernel<256,pair>", "flops_per_launch": fl,
+                     "traffic": NCU_C4_DRAM_PER_SEQ * S,
+                     "traffic_source": "ncu dram__bytes_read+write of one launch of the 2-sequence case, scaled by "
+                                       "sequences",
+                     "kernel": "chunk_kernel<256,pair>", "flops_per_launch": fl,
                      "flops_note": "algorithmic Q.K^T + P.V flops; the tensor cores also run the P_lo.V "
                                    "correction (1.5x these flops)",
                      "issued_tflops": 1.5 * achieved, "launch_ms": launch_ms,

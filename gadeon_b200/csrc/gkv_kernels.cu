@@ -679,7 +679,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<DH>::CTAS)
 #pragma unroll
         for (int n = 0; n < C::NT_QK; ++n) {
             const float p0 = fast_exp2(s[n][0] - mu0), p1 = fast_exp2(s[n][1] - mu0);
-            const float p2 = fast_exp2(s[n][2] - mu1), p3 = fast_exp2(s[n][3] - mu1);
+            // stacked: rows r + 8 are padding, their P slots take row r's P_lo
+            const float p2 = stack ? 0.f : fast_exp2(s[n][2] - mu1);
+            const float p3 = stack ? 0.f : fast_exp2(s[n][3] - mu1);
             ps0 += p0 + p1;
             ps1 += p2 + p3;
             const int kb = warp * C::KPW + n * 8 + lc;

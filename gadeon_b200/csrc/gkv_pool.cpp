@@ -169,8 +169,10 @@ struct gkv_pool {
     float *d_partials = nullptr;
     int32_t *d_counters = nullptr;
     uint16_t *d_prod = nullptr;  // [2][max_seqs * KVH * dh] fp16 K/V rows of gkv_attn_step's unfused route
-    uint8_t *d_host_stage = nullptr;  // device copies of a call's pageable host buffers
-    size_t host_stage_bytes = 0;
+    uint8_t *h_bounce = nullptr;  // page-locked copies of a call's pageable host buffers
+    size_t bounce_bytes = 0;
+    cudaEvent_t bounce_ev = nullptr;  // recorded behind the last launch that used h_bounce
+    bool bounce_pending = false;
     CUtensorMap tmk{}, tmv{};  // chunk kernel: boxes of min(P, 64) rows
     CUtensorMap tak{}, tav{};  // attend kernel: boxes of min(P, tile_keys) rows
     std::vector<int32_t> stack;  // free list; back() is the head
@@ -239,14 +241,15 @@ int check_buffers(const gkv_pool *pool, std::initializer_list<std::pair<const vo
 }
 
 // Pageable host buffers (plain host arrays: malloc, a Swift [Float], numpy).
-// A kernel cannot reach them, so a call given one stages it through device
-// memory the pool owns: one cudaMemcpyAsync per pageable input on the call's
-// stream before the launch, one per pageable output after it.  A copy into
-// pageable memory returns only once it is done, so such a call returns with
-// its output in place (it waits for the device); the input copies return
-// once the runtime holds the bytes, so inputs may be reused at once.  The
-// staging memory grows (cudaMalloc) when a call needs more than it holds and
-// is reused by the next call in stream order.
+// A kernel cannot reach them, so a call given one copies it, on the CPU, into
+// a page-locked bounce buffer the pool owns, which the kernels read and write
+// in place over the host link as they do a caller's own page-locked buffers.
+// After the launch the call records an event; when it has pageable outputs it
+// waits for that event and copies them out of the bounce buffer, so it
+// returns with its outputs in place.  Pageable inputs may be reused as soon
+// as the call returns.  The next call that stages waits for the event before
+// it writes the bounce buffer again, and the buffer grows (cudaHostAlloc)
+// when a call needs more than it holds.
 bool is_pageable(const void *ptr) {
     if (!ptr) return false;
     cudaPointerAttributes a{};
@@ -261,44 +264,59 @@ class HostStage {
 public:
     explicit HostStage(gkv_pool *pool) : pool_(pool) {}
     // Registers a caller buffer of `bytes`; when it is pageable host memory,
-    // reserve() points *ptr at the pool's staging memory.
+    // reserve() points *ptr at the pool's bounce buffer.
     void in(const void **ptr, size_t bytes) { add(const_cast<void **>(ptr), bytes, false); }
     void out(void **ptr, size_t bytes) { add(ptr, bytes, true); }
-    bool any() const { return !items_.empty(); }
-    // Makes room (the one step that may allocate: call it with the pool's
+    // Waits until the previous staged launch is done with the bounce buffer,
+    // makes room (the one step that may allocate: call it with the pool's
     // device current and before any bookkeeping changes) and re-points the
     // registered pageable buffers.
     int reserve() {
+        if (items_.empty()) return GKV_OK;
+        if (pool_->bounce_pending) {
+            GKV_CUDA(cudaEventSynchronize(pool_->bounce_ev), "waiting for the previous staged call");
+            pool_->bounce_pending = false;
+        }
         size_t total = 0;
         for (Item &it : items_) {
             it.off = total;
             total += (it.bytes + 255) & ~size_t(255);
         }
-        if (total > pool_->host_stage_bytes) {
-            cudaFree(pool_->d_host_stage);  // waits for work that may still read it
-            pool_->d_host_stage = nullptr;
-            pool_->host_stage_bytes = 0;
+        if (total > pool_->bounce_bytes) {
+            if (pool_->h_bounce) cudaFreeHost(pool_->h_bounce);
+            pool_->h_bounce = nullptr;
+            pool_->bounce_bytes = 0;
             size_t cap = size_t(1) << 20;
             while (cap < total) cap *= 2;
-            const cudaError_t e = cudaMalloc(&pool_->d_host_stage, cap);
-            if (e != cudaSuccess) return cuda_fail(e, "staging memory for pageable host buffers");
-            pool_->host_stage_bytes = cap;
+            void *h = nullptr;
+            const cudaError_t e = cudaHostAlloc(&h, cap, cudaHostAllocDefault);
+            if (e != cudaSuccess) return cuda_fail(e, "bounce buffer for pageable host buffers");
+            pool_->h_bounce = static_cast<uint8_t *>(h);
+            pool_->bounce_bytes = cap;
         }
-        for (Item &it : items_) *it.slot = pool_->d_host_stage + it.off;
+        if (!pool_->bounce_ev)
+            GKV_CUDA(cudaEventCreateWithFlags(&pool_->bounce_ev, cudaEventDisableTiming), "bounce event");
+        for (Item &it : items_) *it.slot = pool_->h_bounce + it.off;
         return GKV_OK;
     }
-    int copy_in(cudaStream_t st) const {
+    // The pageable inputs into the bounce buffer (before the launch).
+    void copy_in() const {
         for (const Item &it : items_)
-            if (!it.out)
-                GKV_CUDA(cudaMemcpyAsync(*it.slot, it.host, it.bytes, cudaMemcpyHostToDevice, st),
-                         "pageable input copy");
-        return GKV_OK;
+            if (!it.out) std::memcpy(*it.slot, it.host, it.bytes);
     }
-    int copy_out(cudaStream_t st) const {
+    // After the launches: guards the bounce buffer with an event and, when
+    // there are pageable outputs, waits for them and copies them out.
+    int finish(cudaStream_t st) const {
+        if (items_.empty()) return GKV_OK;
+        GKV_CUDA(cudaEventRecord(pool_->bounce_ev, st), "bounce event record");
+        pool_->bounce_pending = true;
+        bool outs = false;
+        for (const Item &it : items_) outs |= it.out;
+        if (!outs) return GKV_OK;
+        GKV_CUDA(cudaEventSynchronize(pool_->bounce_ev), "waiting for the staged outputs");
+        pool_->bounce_pending = false;
         for (const Item &it : items_)
-            if (it.out)
-                GKV_CUDA(cudaMemcpyAsync(it.host, *it.slot, it.bytes, cudaMemcpyDeviceToHost, st),
-                         "pageable output copy");
+            if (it.out) std::memcpy(it.host, *it.slot, it.bytes);
         return GKV_OK;
     }
 
@@ -587,9 +605,12 @@ void free_device(gkv_pool *p) {
     cudaFree(p->d_counters);
     cudaFree(p->d_prod);
     p->d_prod = nullptr;
-    cudaFree(p->d_host_stage);
-    p->d_host_stage = nullptr;
-    p->host_stage_bytes = 0;
+    if (p->h_bounce) cudaFreeHost(p->h_bounce);
+    if (p->bounce_ev) cudaEventDestroy(p->bounce_ev);
+    p->h_bounce = nullptr;
+    p->bounce_bytes = 0;
+    p->bounce_ev = nullptr;
+    p->bounce_pending = false;
     p->d_k = p->d_v = nullptr;
     p->d_table = p->d_status = p->d_counters = nullptr;
     p->d_partials = nullptr;
@@ -883,8 +904,9 @@ int gkv_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, const int
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new, entries, pages);
     if (rc) return rc;
-    if ((rc = hs.copy_in(st))) return rc;
-    return enqueue_append(pool, entries, pages, k, v, 0, st);
+    hs.copy_in();
+    rc = enqueue_append(pool, entries, pages, k, v, 0, st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64_t count,
@@ -911,8 +933,9 @@ int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, 1, &seq_id, &n, entries, pages);
     if (rc) return rc;
-    if ((rc = hs.copy_in(st))) return rc;
-    return enqueue_append(pool, entries, pages, K, V, 1, st);
+    hs.copy_in();
+    rc = enqueue_append(pool, entries, pages, K, V, 1, st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
@@ -934,9 +957,9 @@ int gkv_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     rc = check_attend(pool, n_seqs, seq_ids, n_q, group, q, out);
     if (rc) return rc;
     if (n_seqs > 0 && (rc = check_buffers(pool, {{q, "q"}, {out, "out"}}))) return rc;
-    if ((rc = hs.copy_in(st))) return rc;
+    hs.copy_in();
     rc = enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, flags, st);
-    return rc ? rc : hs.copy_out(st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
@@ -979,7 +1002,7 @@ int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
-    if ((rc = hs.copy_in(st))) return rc;
+    hs.copy_in();
     // Decode and verify steps of the split-K kernel (n_q*group <= 16, n_q <=
     // P) with TMA-staged pages and no shared tail page: the append rides
     // inside the attend kernel (one launch per layer).
@@ -992,7 +1015,7 @@ int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
         rc = enqueue_append(pool, entries, pages, k, v, (flags & GKV_ATTEND_HEAD_MAJOR) ? 1 : 0, st);
         if (!rc) rc = enqueue_attend(pool, n_seqs, seq_ids, n_q, group, q, out, scale, flags, st);
     }
-    return rc ? rc : hs.copy_out(st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_append_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
@@ -1054,7 +1077,7 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     std::vector<gkv::TouchedPage> pages;
     rc = plan_append(pool, n_seqs, seq_ids, n_new.data(), entries, pages);
     if (rc) return rc;
-    if ((rc = hs.copy_in(st))) return rc;
+    hs.copy_in();
     gkv::ProducerArgs prod{q_gate, k_raw, v_raw, q_norm, k_norm, rope_cos, rope_sin, n_rot, eps};
     // Same fusion rule as gkv_append_attend: TMA-staged pages and no shared
     // tail page -> the attend kernel's prologue builds and writes the rows.
@@ -1062,7 +1085,7 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     if (pool->cfg.page_tokens >= 8 && fused_tails(pages, n_seqs, tails)) {
         rc = enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, 0u, st, tails.data(), nullptr,
                             nullptr, &prod);
-        return rc ? rc : hs.copy_out(st);
+        return rc ? rc : hs.finish(st);
     }
     // Otherwise the rows are built by a small kernel, appended (copy-on-write
     // of a shared tail included), then attended.
@@ -1073,7 +1096,7 @@ int gkv_attn_step(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_
     if (rc) return rc;
     rc = enqueue_attend(pool, n_seqs, seq_ids, 1, group, nullptr, out, scale, 0u, st, nullptr, nullptr, nullptr,
                         &prod);
-    return rc ? rc : hs.copy_out(st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_rope_table(int32_t n_rot, float base, int32_t n, const int64_t *positions, float *cos_out,
@@ -1180,8 +1203,9 @@ int gkv_rewind_append(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, co
         }
         return rc;
     }
-    if ((rc = hs.copy_in(st))) return rc;
-    return enqueue_append(pool, entries, pages, k, v, 0, st);
+    hs.copy_in();
+    rc = enqueue_append(pool, entries, pages, k, v, 0, st);
+    return rc ? rc : hs.finish(st);
 }
 
 int gkv_clone_seq(gkv_pool *pool, int32_t src, int32_t *dst, void *stream) {
@@ -1248,7 +1272,7 @@ int gkv_compact_seq(gkv_pool *pool, int32_t seq_id, void *K, void *V, void *stre
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
     GKV_CUDA(gkv::launch_compact(p, st), "compact kernel launch");
-    return hs.copy_out(st);
+    return hs.finish(st);
 }
 
 int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, int32_t tile_p, void *K, void *V,
@@ -1286,7 +1310,7 @@ int gkv_tile_at(gkv_pool *pool, int32_t seq_id, int64_t start, int64_t count, in
     p.dh = pool->cfg.head_dim;
     p.P = pool->cfg.page_tokens;
     GKV_CUDA(gkv::launch_compact(p, st), "tile kernel launch");
-    return hs.copy_out(st);
+    return hs.finish(st);
 }
 
 int gkv_from_compact(gkv_pool *pool, const void *K, const void *V, int64_t length,

@@ -23,10 +23,11 @@
  *     pageable host memory.  The kernels read and write page-locked host
  *     buffers in place over the host link; such a buffer must stay valid
  *     and unchanged until the stream has finished the call.  A kernel cannot
- *     reach pageable memory, so the call stages it through device memory
- *     the pool owns (grown with cudaMalloc when a call needs more): one
- *     cudaMemcpyAsync per pageable input before the launch, one per pageable
- *     output after it.  A call with a pageable output returns once that
+ *     reach pageable memory, so the call stages it through a page-locked
+ *     bounce buffer the pool owns (grown with cudaHostAlloc when a call needs
+ *     more), which the kernels read and write in place: pageable inputs are
+ *     copied into it before the launch, pageable outputs out of it after the
+ *     launch has finished.  A call with a pageable output returns once that
  *     output is in place (it waits for the device); pageable inputs may be
  *     reused as soon as the call returns.  The GDN rollback and
  *     gkv_attend_noalloc take device memory only.  Id and length arrays are
