@@ -254,9 +254,20 @@ def subconfigs(args, rank, world, local):
     import torch.distributed as dist
     out = {}
     R = max(1, args.repeats)
+
+    def guarded(fn):
+        # a failing record is reported in the line instead of losing the
+        # config-2 measurement before it
+        try:
+            return fn()
+        except Exception as e:  # noqa: BLE001
+            torch.cuda.empty_cache()
+            return {"error": f"{type(e).__name__}: {e}"[:400]}
+
     if world == 1:
-        out["3"] = measure_config3(args, rank, world, local, max(args.warmup, 3), max(args.steps, 20), R)
-        out["4"] = measure_config4(args, rank, world, local, max(args.warmup, 3), 3, 1)
+        out["3"] = guarded(lambda: measure_config3(args, rank, world, local, max(args.warmup, 3),
+                                                   max(args.steps, 20), R))
+        out["4"] = guarded(lambda: measure_config4(args, rank, world, local, max(args.warmup, 3), 3, 1))
     elif world in (4, 8):
         from gadeon_b200.workload import lpt_partition
         cfg = CONFIGS[5]
@@ -271,7 +282,8 @@ def subconfigs(args, rank, world, local):
             out["5"] = {"skipped": "a GPU lacks room for its share of the job (%.1f GB short)"
                                    % (-room.item() / 1e9)}
         else:
-            out["5"] = measure_config5(args, rank, world, local, max(args.warmup, 3), min(args.steps, 20), 3, world)
+            out["5"] = guarded(lambda: measure_config5(args, rank, world, local, max(args.warmup, 3),
+                                                       min(args.steps, 20), 3, world))
     return out
 
 
