@@ -41,7 +41,13 @@ def gather_outputs(local, shards: List[List[int]], rank: int, group=None):
     world = len(shards)
     n_max = max(len(s) for s in shards)
     row_shape = tuple(local.shape[1:])
-    assert local.shape[0] == len(shards[rank]), (local.shape, len(shards[rank]))
+    if local.shape[0] != len(shards[rank]):
+        raise ValueError(f"rank {rank} holds {local.shape[0]} rows for a shard of {len(shards[rank])}")
+    # the shards must partition 0..n_job-1 (checked here, before an index
+    # ever reaches a device kernel)
+    n_all = sum(len(s) for s in shards)
+    if sorted(i for s in shards for i in s) != list(range(n_all)):
+        raise ValueError("shards do not partition the job's sequence indices 0..n-1")
     padded = torch.zeros((n_max,) + row_shape, dtype=local.dtype, device=local.device)
     padded[: local.shape[0]] = local
     if dist.get_backend(group) == "nccl":
