@@ -136,3 +136,17 @@ def test_partition_properties():
         assert max(loads) <= sum(tokens) / parts + max(tokens) + 1e-9
 
     check()
+
+
+def test_gather_outputs_refuses_shards_that_do_not_partition_the_job():
+    """Row indices that fall outside 0..n-1 (or repeat) are refused on the
+    host, before any collective or index kernel runs."""
+    import pytest
+    import torch
+    from gadeon_b200.shard import gather_outputs
+    local = torch.zeros((2, 3))
+    for shards in ([[0, 5], [1, 2]], [[0, 1], [1, 2]], [[0, 2], [2]]):
+        with pytest.raises(ValueError, match="partition"):
+            gather_outputs(local, shards, 0)
+    with pytest.raises(ValueError, match="rows"):  # the rank's rows do not match its shard
+        gather_outputs(torch.zeros((3, 3)), [[0, 1], [2, 3]], 0)
