@@ -19,11 +19,13 @@ sequence and run paged decode attention for every sequence.
 
 `--impl reference` times the reference's CPU path (the oracle port: the
 reference is Swift over Apple frameworks and cannot be built here) with all
-host threads on a bounded sample of the same workload.
+host threads, in complete steps of rank 0's shard (at N=1 the whole job);
+when the host lacks memory or the W + K steps would overrun a fixed budget,
+a step covers fewer layers and the time is scaled, as the line states.
 
 Multi-GPU (torchrun): weak scaling -- every rank runs its own 64 sequences
-with its own pools; no collective on the hot path.  The NCCL output gather
-is timed separately (gather_ms_per_step) after the timed region.
+with its own pools; no collective on the hot path.  The e2e step adds the
+NCCL gather of the outputs into job order and rank 0's copy to the host.
 """
 from __future__ import annotations
 
@@ -51,6 +53,7 @@ from gadeon_b200.workload import (CONFIGS, append_bytes, contexts, decode_bytes,
 
 METRIC = "KV append+attend tok/s (paged GQA decode, config 2)"
 UNIT = "tok/s"
+REF_BUDGET_S = 150.0  # --impl reference: host seconds for its W + K steps
 
 
 # DRAM bytes (read + write) per algorithmic byte of the config-2 attend
@@ -71,10 +74,12 @@ NCU_C4_DRAM_PER_SEQ = (245.167104e6 + 103.359744e6) / 2
 NCU_C6_TRAFFIC_PER_ALGO_BYTE = (845496320 + 843880448 + 844162560) / (895729664 + 897515520 + 897826816)
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=20,
+                    help="steps per timed block (config 2's contexts grow by one per step, so long runs "
+                         "drift from the configured distribution)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=20251201)
@@ -101,7 +106,7 @@ def parse_args():
                          "4 prefill chunk, 5 long-context sharded decode; 6 = the GDN state rollback "
                          "that runs beside config 3's truncate; 7 = a whole MTP cycle (drafts on the drafter "
                          "pool, verify, truncate, GDN rollback, drafter rewind)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def peaks():
@@ -233,29 +238,141 @@ def cpu_sample(seed: int, n_seqs: int, steps: int, threads: int, cfg, ctx_all):
     return per_token_key, desc, sum(times)
 
 
+def host_mem_available() -> int:
+    """Bytes this process may still allocate on the host: MemAvailable,
+    capped by the cgroup's limit when one is set."""
+    avail = 8 << 30
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    avail = int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    try:
+        with open("/sys/fs/cgroup/memory.max") as f:
+            lim = f.read().strip()
+        with open("/sys/fs/cgroup/memory.current") as f:
+            cur = int(f.read())
+        if lim != "max":
+            avail = min(avail, int(lim) - cur)
+    except (OSError, ValueError):
+        pass
+    return avail
+
+
+def config2_dict(S: int, L: int, world: int, ctx, cfg) -> dict:
+    """The `config` object of a config-2 line (both arms print the same)."""
+    return {
+        "workload": (f"config2 decode step: {S} seqs/GPU x {L} layers, append 1 + paged GQA decode attend"
+                     + ("" if (S, L) == (cfg.seqs, cfg.layers) else " (REDUCED profiling case)")),
+        "seqs_per_gpu": S, "layers": L, "n_heads": cfg.n_heads, "kv_heads": cfg.kv_heads,
+        "head_dim": cfg.head_dim, "page_tokens": cfg.page_tokens,
+        "ctx": ("U[1024,32768]: %d x %d job sequences token-balanced over the GPUs" % (S, world)
+                if world > 1 else "U[1024,32768]"), "ctx_mean": float(np.mean(ctx)),
+        "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)"
+              % (float(np.sum(ctx)) * L * cfg.kv_heads * cfg.head_dim * 4 / 1e9),
+        "parallelism": f"dp{world} (sequences sharded, no hot-path collective)",
+    }
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the oracle port of the reference's CPU path with all
-    host threads, each step a bounded sample of the job's step."""
+    """--impl reference: the oracle port of the reference's CPU path
+    (PagePool.append, then hostFlashDecode with its fp32 mirror, per
+    sequence; PagedAttention.swift:85-94, :46-77, :317-366) on all host
+    threads, sequences spread over them.  Each timed step is a complete
+    config-2 step of rank 0's shard -- append one row to every sequence and
+    attend, layer after layer -- timed with the host clock.  At N=1 the
+    shard is the whole job, so the line is measured as is; at N>1 one host
+    runs the whole job, so its rate is the shard step's time scaled by the
+    job's attended keys over the shard's.  When the host cannot hold every
+    layer's pool and mirror, the step runs as many layers as fit and the
+    time is scaled by the layer count (stated in the line)."""
     if rank != 0:
         return
+    from oracle import oracle as O
     cfg = CONFIGS[2]
-    ctx_all = weak_job_contexts(2, args.seed, cfg.seqs, world)
+    S, L, KVH, dh, P, G, nH = cfg.seqs, cfg.layers, cfg.kv_heads, cfg.head_dim, cfg.page_tokens, cfg.group, cfg.n_heads
+    S, L = args.seqs or S, args.layers or L
+    W, K = args.warmup, args.steps
+    ctx = weak_rank_contexts(2, args.seed, S, world, 0)
+    job = weak_job_contexts(2, args.seed, S, world)
     threads = os.cpu_count() or 1
-    steps = args.warmup + args.steps
-    per_key, desc, cpu_s = cpu_sample(args.seed + 7, 16, steps, threads, cfg, ctx_all)
-    job_keys = float(ctx_all.sum()) * cfg.layers
-    step_s = per_key * job_keys
-    value = len(ctx_all) / step_s
+    grow = W + K + 4
+    n_pages = pool_pages(ctx, P, grow)
+    # pages (fp16 K and V) + the fp32 mirror, whose capacity doubles from 64 rows
+    mirror_rows = sum(64 << max(0, math.ceil(math.log2((int(c) + grow) / 64))) for c in ctx)
+    per_layer = n_pages * KVH * P * dh * 2 * 2 + mirror_rows * KVH * dh * 4 * 2
+    avail = host_mem_available()
+    L_mem = max(1, min(L, int(0.7 * avail // per_layer)))
+    rng = np.random.default_rng(args.seed + 7)
+    span = int(ctx.max()) + 4096
+    block = rng.standard_normal((2, KVH, span, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+    t_setup = time.perf_counter()
+    pools, ids = [], []
+    for layer in range(L_mem):
+        pool = O.OraclePool(KVH, dh, P, n_pages, args.seed * 31 + layer)
+        lids = []
+        for c in ctx:
+            c, off = int(c), int(rng.integers(0, 4096))
+            s = pool.seq_create()
+            assert pool.seed(s, np.ascontiguousarray(block[0, :, off:off + c]),
+                             np.ascontiguousarray(block[1, :, off:off + c]), c) == 0
+            lids.append(s)
+        pools.append(pool)
+        ids.append(lids)
+    # per-step rows and queries, drawn before the clock starts
+    rows = [rng.standard_normal((2, S, KVH, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+            for _ in range(4)]
+    qs = [rng.standard_normal((S, 1, nH, dh), dtype=np.float32).astype(np.float16).view(np.uint16)
+          for _ in range(4)]
+    scale = dh ** -0.5
+
+    def step(i, layers):
+        kv, q = rows[i % 4], qs[i % 4]
+        for layer in range(layers):
+            assert pools[layer].append(ids[layer], [1] * S, kv[0], kv[1]) == 0
+            pools[layer].attend_causal(ids[layer], 1, q, G, scale, n_threads=threads)
+
+    step(0, L_mem)  # builds every sequence's fp32 mirror (floats32's first call)
+    t0 = time.perf_counter()
+    step(1, L_mem)
+    per_layer_s = (time.perf_counter() - t0) / L_mem
+    setup_s = time.perf_counter() - t_setup
+    # as many layers per step as keep the W + K steps within the budget
+    L_run = max(1, min(L_mem, int(REF_BUDGET_S // ((W + K) * per_layer_s))))
+    for i in range(W):
+        step(2 + i, L_run)
+    t0 = time.perf_counter()
+    for i in range(K):
+        step(2 + W + i, L_run)
+    step_s = (time.perf_counter() - t0) / K
+    key_scale = float(job.sum()) / float(ctx.sum())
+    job_step_s = step_s * (L / L_run) * key_scale
+    value = len(job) / job_step_s
+    measured = (f"rank 0's shard: {S} sequences x {L_run} of {L} layers, complete steps (append 1 row to every "
+                f"sequence, then hostFlashDecode of every sequence) on {threads} threads, {K} timed steps after "
+                f"{W} warm-up steps; setup {setup_s:.0f} s (pools, the fp32 mirror, one probe step)")
+    scaled = []
+    if L_run < L:
+        scaled.append(f"x{L / L_run:g} for the layers left out (%s)" %
+                      ("host memory" if L_run == L_mem else f"the {REF_BUDGET_S:.0f} s budget for {W + K} steps"))
+    if world > 1:
+        scaled.append(f"x{key_scale:.3f} (the job's attended keys over the shard's): one host runs the whole job")
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 storage)", "data": "synthetic",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": step_s * 1e3, "job_ms_per_step": job_step_s * 1e3,
+        "timing": "host clock around the K timed steps; ms_per_step is one timed step of the run, "
+                  "job_ms_per_step the job's step it stands for",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (fp16 storage, fp32 mirror)", "data": "synthetic (seeded N(0,1) fp16)",
         "impl": "reference",
-        "config": {"workload": "config2 decode step: 64 seqs/GPU x 6 layers, ctx ~U[1024,32768], "
-                               "nH=8 KVH=2 dh=256 P=16", "seqs": int(len(ctx_all)), "layers": cfg.layers},
+        "config": config2_dict(S, L, world, ctx, cfg),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": desc + f"; every step repeats the sample ({cpu_s:.1f} s CPU total)"},
+                         "sample": measured + ("; scaled " + ", ".join(scaled) if scaled else
+                                               "; the whole job, no scaling")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "host_mem_gb": {"available": avail / 1e9, "per_layer": per_layer / 1e9},
     }
     print(json.dumps(line), flush=True)
 
@@ -520,15 +637,7 @@ def run_ours(args, rank, world, local):
                   "with CUDA events (max over ranks); ms_per_step is the median block's",
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
-        "config": {
-            "workload": (f"config2 decode step: {S} seqs/GPU x {L} layers, append 1 + paged GQA decode attend"
-                         + ("" if (S, L) == (cfg.seqs, cfg.layers) else " (REDUCED profiling case)")),
-            "seqs_per_gpu": S, "layers": L, "n_heads": nH, "kv_heads": KVH, "head_dim": dh,
-            "page_tokens": P, "ctx": ("U[1024,32768]: %d x %d job sequences token-balanced over the GPUs" % (S, world)
-                    if world > 1 else "U[1024,32768]"), "ctx_mean": float(ctx.mean()),
-            "l2": "inputs larger than L2 (%.1f GB of K/V per GPU)" % (float(ctx.sum()) * L * KVH * dh * 4 / 1e9),
-            "parallelism": f"dp{world} (sequences sharded, no hot-path collective)",
-        },
+        "config": config2_dict(S, L, world, ctx, cfg),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                      "traffic": NCU_C2_TRAFFIC_PER_ALGO_BYTE * bytes_per_launch,

@@ -137,6 +137,21 @@ void orc_f16_to_f32_array(const uint16_t *src, float *dst, int64_t n) {
     for (int64_t i = 0; i < n; i++) dst[i] = orc_f16_to_f32(src[i]);
 }
 
+/* orc_f16_to_f32 tabulated for all 65,536 inputs (filled once, from the
+ * function above, so the two agree bit for bit): widening the fp32 mirror
+ * is a table lookup per element. */
+static float f16_table[65536];
+static pthread_once_t f16_table_once = PTHREAD_ONCE_INIT;
+
+static void f16_table_fill(void) {
+    for (uint32_t h = 0; h < 65536; h++) f16_table[h] = orc_f16_to_f32((uint16_t)h);
+}
+
+static const float *f16_lut(void) {
+    pthread_once(&f16_table_once, f16_table_fill);
+    return f16_table;
+}
+
 void orc_f32_to_f16_array(const float *src, uint16_t *dst, int64_t n) {
     for (int64_t i = 0; i < n; i++) dst[i] = orc_f32_to_f16(src[i]);
 }
@@ -503,6 +518,7 @@ const uint16_t *orc_page_v(OrcPool *p, int32_t pid) { return vpage(p, pid); }
  * [f32len, n) of every kv head from the fp16 pages into the fp32 mirror. */
 static void grow_mirror(OrcPool *p, OrcSeq *s, int64_t n) {
     int KVH = p->kvh, dh = p->dh, P = p->P;
+    const float *lut = f16_lut();
     if (n > s->mcap) {
         int64_t cap = s->mcap ? s->mcap : 64;
         while (cap < n) cap *= 2;
@@ -528,8 +544,8 @@ static void grow_mirror(OrcPool *p, OrcSeq *s, int64_t n) {
             float *kd = s->kf + ((int64_t)h * s->mcap + t) * dh;
             float *vd = s->vf + ((int64_t)h * s->mcap + t) * dh;
             for (int d = 0; d < dh; d++) {
-                kd[d] = orc_f16_to_f32(kr[d]);
-                vd[d] = orc_f16_to_f32(vr[d]);
+                kd[d] = lut[kr[d]];
+                vd[d] = lut[vr[d]];
             }
         }
     if (n > s->f32len) s->f32len = n;
@@ -640,6 +656,24 @@ static void *causal_worker(void *arg) {
     return NULL;
 }
 
+/* Grows the mirror of batch entry b to its sequence's length; an id that
+ * appears earlier in the batch is left to that entry's job. */
+static void *grow_worker(void *arg) {
+    CausalJob *J = (CausalJob *)arg;
+    for (;;) {
+        pthread_mutex_lock(&J->mu);
+        int64_t b = J->next++;
+        pthread_mutex_unlock(&J->mu);
+        if (b >= J->n) break;
+        int first = 1;
+        for (int64_t e = 0; e < b && first; e++) first = J->ids[e] != J->ids[b];
+        if (!first) continue;
+        OrcSeq *s = get_seq(J->p, J->ids[b]);
+        grow_mirror(J->p, s, s->len);
+    }
+    return NULL;
+}
+
 static int attend_jobs(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
                        const int32_t *rows, int n_rows, const uint16_t *q, int G,
                        float scale, float *out, int n_threads) {
@@ -652,19 +686,23 @@ static int attend_jobs(OrcPool *p, int n, const int32_t *seq_ids, int n_q,
     }
     for (int i = 0; rows && i < n_rows; i++)
         if (rows[i] < 0 || rows[i] >= n_q) return ORC_ERR_INVALID;
-    /* the mirror grows once per sequence before the rows fan out */
-    for (int b = 0; b < n; b++) {
-        OrcSeq *s = get_seq(p, seq_ids[b]);
-        grow_mirror(p, s, s->len);
-    }
     CausalJob J = {p, n, n_q, G, seq_ids, rows, n_rows, q, scale, out, 0,
                    PTHREAD_MUTEX_INITIALIZER, max_len};
     if (n_threads < 1) n_threads = 1;
     if (n_threads == 1) {
+        /* the mirror grows once per sequence before the rows fan out */
+        for (int b = 0; b < n; b++) {
+            OrcSeq *s = get_seq(p, seq_ids[b]);
+            grow_mirror(p, s, s->len);
+        }
         causal_worker(&J);
         return ORC_OK;
     }
     pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * n_threads);
+    /* the same growth, one sequence per job over the threads, then the rows */
+    for (int i = 0; i < n_threads; i++) pthread_create(&th[i], NULL, grow_worker, &J);
+    for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
+    J.next = 0;
     for (int i = 0; i < n_threads; i++) pthread_create(&th[i], NULL, causal_worker, &J);
     for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
     free(th);
