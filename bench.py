@@ -450,8 +450,8 @@ def run_ours(args, rank, world, local):
     # capped token-balanced partition, rows of its outputs in shard order
     job_ctx = weak_job_contexts(2, args.seed, S, world)
     shards = capped_partition(job_ctx, world, S) if world > 1 else [list(range(S))]
-    n_legs = 0 if args.no_e2e else 3  # e2e: page-locked in place, staged copies, pageable arrays
-    steps_total = W + R * K + n_legs * K + 2
+    # every timed block is rewound to the contexts after the warm-up
+    steps_total = W + K + 4
     max_pps = int(math.ceil((int(ctx.max()) + steps_total) / P)) + 2
     n_pages = pool_pages(ctx, P, steps_total)
 
@@ -483,10 +483,6 @@ def run_ours(args, rank, world, local):
     outs = [torch.empty((S, 1, nH, dh), dtype=torch.float32, device=dev) for _ in range(L)]
     torch.cuda.synchronize()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     def step(i, ti):
         # one public call per layer: append the step's K/V row of every
         # sequence and attend (the append rides inside the attend kernel).
@@ -496,17 +492,14 @@ def run_ours(args, rank, world, local):
             pools[layer].append_attend(ids[layer], 1, G, k_all[i, layer], v_all[i, layer], q_all[i, layer],
                                        out=outs[layer])
 
-    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, R)
-    attend_avg_ms = ms / L  # back-to-back launches: gaps between them included
-    # algorithmic bytes of each timed attend launch (contexts after its append)
-    bytes_per_launch = mean_decode_bytes(ctx, cfg, W + 1, R * K) + append_bytes(S, cfg)
-    hbm_peak, peak_kind = peaks()
-    achieved = bytes_per_launch / (attend_avg_ms * 1e-3) / 1e9
-    job_bytes = bytes_per_launch * L
-    if world > 1:
-        t = torch.tensor([job_bytes], device=dev, dtype=torch.float64)
-        dist.all_reduce(t)
-        job_bytes = float(t.item())
+    def rewind():
+        # every timed block starts from the same contexts (those after the
+        # warm-up): drop the rows the block appended (host bookkeeping,
+        # outside the timed blocks)
+        for layer in range(L):
+            pools[layer].truncate(ids[layer], base_len)
+
+    base_len = [int(c) + W for c in ctx]
 
     def job_outputs():
         # every layer's outputs of the step, gathered over the GPUs into job
@@ -514,7 +507,8 @@ def run_ours(args, rank, world, local):
         local_out = torch.stack([o.reshape(S, -1) for o in outs], dim=1).reshape(S, -1)
         return gather_outputs(local_out, shards, rank)
 
-    # ---- end to end through the public call with host buffers
+    # ---- the same step end to end through the public call with host buffers
+    legs = [step]
     e2e = None
     if not args.no_e2e:
         qh = q_all[W:].cpu().pin_memory()
@@ -529,65 +523,68 @@ def run_ours(args, rank, world, local):
             oh = torch.empty((K, n_job, L * nH * dh), dtype=torch.float32).pin_memory()
             op = torch.empty((K, n_job, L * nH * dh), dtype=torch.float32)
         qd, kd, vd = torch.empty_like(q_all[0, 0]), torch.empty_like(k_all[0, 0]), torch.empty_like(v_all[0, 0])
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-        def leg(body):
-            torch.cuda.synchronize()
-            barrier()
-            e0.record()
-            for i in range(K):
-                body(i)
-            e1.record()
-            torch.cuda.synchronize()
-            barrier()
-            return e0.elapsed_time(e1) / K
-
-        def zero_copy(i):
+        def zero_copy(i, ti):
             # the public call given page-locked host q/k/v (read in place by
             # the kernel over the host link); one GPU: out written in place to
             # host memory; N GPUs: out on the device, gathered in job order,
             # rank 0 copies the job's outputs to host memory
             for layer in range(L):
-                pools[layer].append_attend(ids[layer], 1, G, kh[i, layer], vh[i, layer], qh[i, layer],
-                                           out=oh[i, layer] if world == 1 else outs[layer])
+                pools[layer].append_attend(ids[layer], 1, G, kh[ti, layer], vh[ti, layer], qh[ti, layer],
+                                           out=oh[ti, layer] if world == 1 else outs[layer])
             if world > 1:
                 job = job_outputs()
                 if rank == 0:
-                    oh[i].copy_(job, non_blocking=True)
+                    oh[ti].copy_(job, non_blocking=True)
 
-        def staged(i):
+        def staged(i, ti):
             # explicit copy-engine H2D of q/k/v per layer, the call on device
             # buffers, D2H of the output (one GPU) or of the gathered job (N)
             for layer in range(L):
-                qd.copy_(qh[i, layer], non_blocking=True)
-                kd.copy_(kh[i, layer], non_blocking=True)
-                vd.copy_(vh[i, layer], non_blocking=True)
+                qd.copy_(qh[ti, layer], non_blocking=True)
+                kd.copy_(kh[ti, layer], non_blocking=True)
+                vd.copy_(vh[ti, layer], non_blocking=True)
                 pools[layer].append_attend(ids[layer], 1, G, kd, vd, qd, out=outs[layer])
                 if world == 1:
-                    oh[i, layer].copy_(outs[layer], non_blocking=True)
+                    oh[ti, layer].copy_(outs[layer], non_blocking=True)
             if world > 1:
                 job = job_outputs()
                 if rank == 0:
-                    oh[i].copy_(job, non_blocking=True)
+                    oh[ti].copy_(job, non_blocking=True)
 
-        def pageable(i):
+        def pageable(i, ti):
             # plain host arrays through the public call: the library stages
             # them (one cudaMemcpyAsync per buffer; the call returns with out
             # in place)
             for layer in range(L):
-                pools[layer].append_attend(ids[layer], 1, G, kp[i, layer], vp[i, layer], qp[i, layer],
-                                           out=op[i, layer] if world == 1 else outs[layer])
+                pools[layer].append_attend(ids[layer], 1, G, kp[ti, layer], vp[ti, layer], qp[ti, layer],
+                                           out=op[ti, layer] if world == 1 else outs[layer])
             if world > 1:
                 job = job_outputs()
                 if rank == 0:
-                    op[i].copy_(job)
+                    op[ti].copy_(job)
 
-        e2e_ms = leg(zero_copy)
-        e2e_copy_ms = leg(staged)
-        e2e_page_ms = leg(pageable)
+        legs += [zero_copy, staged, pageable]
+
+    times, clk = interleaved_blocks(torch, dist, world, W, K, legs, local, R, rewind)
+    blocks = times[0]
+    ms = statistics.median(blocks)
+    attend_avg_ms = ms / L  # back-to-back launches: gaps between them included
+    # algorithmic bytes of each timed attend launch (contexts after its append;
+    # every block runs the same K steps from the same contexts)
+    bytes_per_launch = mean_decode_bytes(ctx, cfg, W + 1, K) + append_bytes(S, cfg)
+    hbm_peak, peak_kind = peaks()
+    achieved = bytes_per_launch / (attend_avg_ms * 1e-3) / 1e9
+    job_bytes = bytes_per_launch * L
+    if world > 1:
+        t = torch.tensor([job_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        job_bytes = float(t.item())
+    if not args.no_e2e:
+        e2e_ms, e2e_copy_ms, e2e_page_ms = (statistics.median(b) for b in times[1:])
         h2d = L * (qd.numel() + kd.numel() + vd.numel()) * 2 * world
         d2h = (L * outs[0].numel() * 4) * world
-        e2e = [e2e_ms, h2d, d2h, e2e_copy_ms, e2e_page_ms]
+        e2e = [e2e_ms, h2d, d2h, e2e_copy_ms, e2e_page_ms, times[1], times[2], times[3]]
 
     # ---- the output gather on its own (N GPUs), after the timed region
     gather_ms = None
@@ -633,8 +630,11 @@ def run_ours(args, rank, world, local):
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "repeats": R, "ms_per_step": ms, "block_ms_per_step": blocks,
-        "timing": f"{R} blocks of exactly {K} steps, each between barrier + synchronize brackets and timed "
-                  "with CUDA events (max over ranks); ms_per_step is the median block's",
+        "timing": (f"{R} rounds; each times one block of exactly {K} steps of the device-resident step and then "
+                   f"of each e2e variant, between barrier + synchronize brackets with CUDA events (max over ranks), "
+                   f"and after every block drops the block's appended rows (gkv_truncate, outside the timed "
+                   f"blocks), so every block starts from the contexts after the warm-up; ms_per_step is the "
+                   f"median block's"),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 accumulate, fp16 K/V/Q storage", "data": "synthetic (seeded N(0,1) fp16)",
         "config": config2_dict(S, L, world, ctx, cfg),
@@ -658,6 +658,7 @@ def run_ours(args, rank, world, local):
                               + (" (out written in place to host memory)" if world == 1 else
                                  "; outputs gathered over NCCL into job order (shard.gather_outputs) and rank 0 "
                                  "copies the job's outputs to page-locked host memory, all inside each timed step")),
+                 "block_ms_per_step": e2e[5] if e2e_ms_max <= e2e_copy_max else e2e[6],
                  "in_place_value": tokens / (e2e_ms_max * 1e-3),
                  "staged_copy_value": tokens / (e2e_copy_max * 1e-3),
                  "staged_copy_note": "same step with cudaMemcpyAsync H2D/D2H around each call",
@@ -666,6 +667,8 @@ def run_ours(args, rank, world, local):
                                   "through a pool-owned page-locked bounce buffer read and written in place"}
                 if e2e else None),
         "gpu_launches": K * L * R,
+        "gpu_launches_note": "attend launches in the timed blocks of the device-resident step; each e2e "
+                             "variant launches as many in its own blocks",
         "clocks": clk,
         "host_cores_near_gpu": host_cores,
     }
@@ -759,6 +762,50 @@ def timed_loop(torch, dist, world, W, K, step, local, repeats=1):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     blocks = t.tolist()
     return statistics.median(blocks), blocks, clk
+
+
+def interleaved_blocks(torch, dist, world, W, K, legs, local, repeats, rewind):
+    """Times several variants of one step under the same conditions: W
+    untimed steps of legs[0]; one untimed step of every other leg (its first
+    call's set-up), each followed by rewind(); then `repeats` rounds, each
+    timing one block of exactly K steps of every leg in turn, between
+    barrier + synchronize brackets with CUDA events on the launching stream,
+    and calling rewind() after every block so that every block starts from
+    the same state.  Clocks are sampled over the rounds.  Returns (per leg,
+    the blocks' ms per step, each the max over ranks; clocks)."""
+    for i in range(W):
+        legs[0](i, None)
+    torch.cuda.synchronize()
+    for leg in legs[1:]:
+        leg(W, 0)
+        torch.cuda.synchronize()
+        rewind()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = [[] for _ in legs]
+    for _ in range(repeats):
+        for li, leg in enumerate(legs):
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            start.record()
+            for i in range(K):
+                leg(W + i, i)
+            end.record()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            times[li].append(start.elapsed_time(end) / K)
+            rewind()
+    clk = clocks.stop()
+    t = torch.tensor(times, device=torch.device("cuda", local), dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist(), clk
 
 
 def max_over_ranks(torch, dist, world, local, x):
