@@ -937,21 +937,33 @@ def measure_config4(args, rank, world, local, W, K, repeats, seqs=None):
     kk = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     vv = torch.randn((S * nq, KVH, dh), generator=gen, device=dev, dtype=torch.float16)
     out = torch.empty((S, nq, nH, dh), dtype=torch.float32, device=dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
     rows = [nq] * S
+    # events around each chunk launch of the last timed block, per variant
+    ev = {pf: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K * L)]
+          for pf in (False, True)}
 
-    def step(i, ti):
-        for layer in range(L):
-            pools[layer].append(ids[layer], rows, kk, vv)
-            if ti is not None:
-                ev[ti * L + layer][0].record()
-            pools[layer].attend(ids[layer], nq, G, q, out=out)
-            if ti is not None:
-                ev[ti * L + layer][1].record()
-            pools[layer].truncate(ids[layer], ctx)
+    def make_step(pf):
+        # pf: GKV_ATTEND_P_F16 (softmax weights rounded once to fp16)
+        def step(i, ti):
+            for layer in range(L):
+                pools[layer].append(ids[layer], rows, kk, vv)
+                if ti is not None:
+                    ev[pf][ti * L + layer][0].record()
+                pools[layer].attend(ids[layer], nq, G, q, out=out, p_f16=pf)
+                if ti is not None:
+                    ev[pf][ti * L + layer][1].record()
+                pools[layer].truncate(ids[layer], ctx)
+        return step
 
-    ms, blocks, clk = timed_loop(torch, dist, world, W, K, step, local, repeats)
-    launch_ms = max_over_ranks(torch, dist, world, local, statistics.mean(a.elapsed_time(b) for a, b in ev))
+    # the default and the P_F16 variant in alternating blocks (the same clock
+    # conditions); every step truncates its chunk away, so nothing to rewind
+    times, clk = interleaved_blocks(torch, dist, world, W, K, [make_step(False), make_step(True)], local,
+                                    repeats, lambda: None)
+    blocks, blocks16 = times
+    ms, ms16 = statistics.median(blocks), statistics.median(blocks16)
+    launch_ms, launch16 = (max_over_ranks(torch, dist, world, local,
+                                          statistics.mean(a.elapsed_time(b) for a, b in ev[pf]))
+                           for pf in (False, True))
     fl = chunk_flops(ctx, nq, cfg)
     peak, kind = tensor_peak(sustained=True)
     for p in pools:
@@ -959,6 +971,7 @@ def measure_config4(args, rank, world, local, W, K, repeats, seqs=None):
     del pools
     torch.cuda.empty_cache()
     achieved = fl / (launch_ms * 1e-3) / 1e12
+    achieved16 = fl / (launch16 * 1e-3) / 1e12
     return {
         "metric": "prefill chunk ingest tok/s (config 4)", "value": S * nq * world / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": K, "warmup": W, "repeats": repeats, "ms_per_step": ms, "block_ms_per_step": blocks,
@@ -978,6 +991,12 @@ def measure_config4(args, rank, world, local, W, K, repeats, seqs=None):
                                    "correction (1.5x these flops)",
                      "issued_tflops": 1.5 * achieved, "launch_ms": launch_ms,
                      "launch_timing": "CUDA events around each chunk launch (the last timed block)"},
+        "p_f16": {"what": "the same steps with GKV_ATTEND_P_F16: the softmax weights rounded once to fp16 and "
+                          "one P.V per key tile, the arithmetic of the reference's Metal attn_batch_mm; each "
+                          "output element within 2^-10 x sum_i w_i |V_i| of the exact result instead of the "
+                          "element-wise tolerance of the default; timed in blocks alternating with the default's",
+                  "value": S * nq * world / (ms16 * 1e-3), "ms_per_step": ms16, "block_ms_per_step": blocks16,
+                  "launch_ms": launch16, "achieved_tflops": achieved16, "frac": achieved16 / peak},
         "gpu_launches": K * L * 2 * repeats, "clocks": clk}
 
 

@@ -9,6 +9,7 @@ from .kv import (  # noqa: F401
     EXPORTED,
     GKV_ATTEND_HEAD_MAJOR,
     GKV_ATTEND_OUT_F16,
+    GKV_ATTEND_P_F16,
     GKV_ERR_BAD_SEQ,
     GKV_ERR_CAPACITY,
     GKV_ERR_CUDA,

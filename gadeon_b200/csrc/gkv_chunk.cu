@@ -16,8 +16,13 @@
 //   warps 0-3  softmax: thread r owns row r.  It stages its Q row in tensor
 //              memory (the A operand of Q K^T), reads its S row (128 keys)
 //              from tensor memory, applies the causal mask and the online
-//              softmax (exp2 domain), writes P (fp16) to shared memory for
-//              the P.V MMA.  The running max is raised only when it grows by
+//              softmax (exp2 domain), writes P to shared memory for the P.V
+//              MMA as two fp16 parts, P_hi = fp16(p) and P_lo = fp16(p -
+//              P_hi), so P.V = P_lo.V + P_hi.V keeps ~22 significant bits of
+//              every weight (PLO); with GKV_ATTEND_P_F16 (PLO = false), as P
+//              rounded once to fp16 and one P.V -- the arithmetic of the
+//              reference's Metal attn_batch_mm, whose P is a half tile
+//              multiplied by half V into fp32 (Kernels.metal:1891-1912).  The running max is raised only when it grows by
 //              more than 2^8; only then is that row of O rescaled in tensor
 //              memory.
 //   warps 4, 5 TMA loads of K tiles (warp 4) and V tiles (warp 5), one lane
@@ -65,7 +70,7 @@ constexpr int kTile = 2 * kHalf;  // keys per tile (tcgen05 N of Q K^T)
 constexpr uint32_t kTmemMaxCols = 512;  // tensor memory columns per SM
 constexpr int kSmemLimit = 227 * 1024;
 
-template <int DH, bool PAIR>
+template <int DH, bool PAIR, bool PLO>
 struct ChunkCfg {
     static constexpr int NCB = DH / 64;
     static_assert(!PAIR || NCB >= 2, "a CTA pair splits V by 64-column blocks");
@@ -82,15 +87,16 @@ struct ChunkCfg {
     static constexpr int STAGE_BYTES = NCB * CB_K;
     static_assert(STAGE_BYTES == V_NCB * CB_V, "K and V parts fill the same stage");
     // P as P_hi and P_lo (fp16 each, two 64-key atoms each): P.V runs as
-    // P_hi.V + P_lo.V so the weights keep ~22 significant bits
+    // P_hi.V + P_lo.V so the weights keep ~22 significant bits (PLO); or P
+    // rounded once to fp16 and one P.V (GKV_ATTEND_P_F16)
     static constexpr int P_ONE = kChunkRows * kTile * 2;
-    static constexpr int P_BYTES = 2 * P_ONE;
+    static constexpr int P_BYTES = PLO ? 2 * P_ONE : P_ONE;
     static constexpr int NS_FIT = (kSmemLimit - 2048 - P_BYTES) / STAGE_BYTES;
     static constexpr int NS = NS_FIT < 8 ? NS_FIT : 8;      // ring depth
     static_assert(NS >= 3, "the ring needs three stages");
     static constexpr int OFF_STAGE = 0;
     static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;  // P_hi
-    static constexpr int OFF_PL = OFF_P + P_ONE;                  // P_lo
+    static constexpr int OFF_PL = OFF_P + P_ONE;                  // P_lo (PLO only)
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
     static constexpr int NBARS = 2 * NS + 5;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
@@ -109,11 +115,11 @@ struct ChunkCfg {
     static_assert(SMEM_ALLOC <= kSmemLimit, "fits the per-CTA shared memory limit");
 };
 
-template <int DH, bool PAIR>
+template <int DH, bool PAIR, bool PLO>
 __global__ void __launch_bounds__(kChunkThreads, 1)
     chunk_kernel(const __grid_constant__ ChunkParams p, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv) {
-    using C = ChunkCfg<DH, PAIR>;
+    using C = ChunkCfg<DH, PAIR, PLO>;
     constexpr int M = kChunkRows, TT = kTile, H = kHalf;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 tc_fence_after();
                 const uint32_t sV = smem_u32(stage(vi));
                 const uint32_t sP = smem_u32(smem + C::OFF_P);
-                const uint32_t sPl = smem_u32(smem + C::OFF_PL);
+                [[maybe_unused]] const uint32_t sPl = smem_u32(smem + C::OFF_PL);
 #pragma unroll
                 for (int kk = 0; kk < TT / 16; ++kk) {
                     // P atom kk/4 holds keys 64*(kk/4) .. +63; V is MN-major:
@@ -319,15 +325,22 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                     // bytes apart (SBO), 16 keys = 2048 bytes per K step.
                     const uint32_t patom = (kk >> 2) * M * 128 + (kk & 3) * 32;
                     const uint64_t a = umma_desc_sw128(sP + patom, 16, 1024);
-                    const uint64_t al = umma_desc_sw128(sPl + patom, 16, 1024);
+                    [[maybe_unused]] const uint64_t al = umma_desc_sw128(sPl + patom, 16, 1024);
                     const uint64_t bd = umma_desc_sw128(sV + kk * 16 * 128, C::CB_V, 1024);
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    if constexpr (PAIR) {
-                        umma_pair_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
-                        umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                    if constexpr (PLO) {
+                        if constexpr (PAIR) {
+                            umma_pair_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
+                            umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                        } else {
+                            umma_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
+                            umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                        }
                     } else {
-                        umma_f16(tmem + C::O_COL, al, bd, IDESC_PV, acc);
-                        umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, 1u);
+                        if constexpr (PAIR)
+                            umma_pair_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
+                        else
+                            umma_f16(tmem + C::O_COL, a, bd, IDESC_PV, acc);
                     }
                 }
                 commit(&empty[vi % C::NS]);
@@ -437,25 +450,32 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
                 }
             }
             uint8_t *sP = smem + C::OFF_P;
-            uint8_t *sPl = smem + C::OFF_PL;
+            [[maybe_unused]] uint8_t *sPl = smem + C::OFF_PL;
             // packed fp32x2 FMA / add (each lane rounded as fmaf / + would)
             float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                              make_float2(0.f, 0.f)};
             const float2 sl2 = make_float2(sl, sl), nmu2 = make_float2(nmu, nmu);
 #pragma unroll
             for (int ch = 0; ch < TT / 8; ++ch) {  // 16-byte chunks of 8 keys
-                uint32_t w4[4], w4l[4];
+                uint32_t w4[4];
+                [[maybe_unused]] uint32_t w4l[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float2 x = __ffma2_rn(make_float2(s[ch * 8 + 2 * u], s[ch * 8 + 2 * u + 1]), sl2, nmu2);
                     const float a0 = fast_exp2(x.x), a1 = fast_exp2(x.y);
                     ps2[u] = __fadd2_rn(ps2[u], make_float2(a0, a1));
-                    split_half2(a0, a1, w4[u], w4l[u]);
+                    if constexpr (PLO) {
+                        split_half2(a0, a1, w4[u], w4l[u]);
+                    } else {
+                        const __half2 h = __floats2half2_rn(a0, a1);
+                        w4[u] = *reinterpret_cast<const uint32_t *>(&h);
+                    }
                 }
                 // P atom (ch / 8) holds keys 64*(ch/8) .. +63 of all rows
                 const int at = (ch >> 3) * M * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
                 *reinterpret_cast<uint4 *>(sP + at) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                *reinterpret_cast<uint4 *>(sPl + at) = make_uint4(w4l[0], w4l[1], w4l[2], w4l[3]);
+                if constexpr (PLO)
+                    *reinterpret_cast<uint4 *>(sPl + at) = make_uint4(w4l[0], w4l[1], w4l[2], w4l[3]);
             }
             l = l * factor + (((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
                               ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y)));
@@ -529,11 +549,11 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     }
 }
 
-template <int DH, bool PAIR>
+template <int DH, bool PAIR, bool PLO>
 cudaError_t launch_chunk_t(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv,
                            cudaStream_t s) {
-    auto kern = chunk_kernel<DH, PAIR>;
-    constexpr int smem = ChunkCfg<DH, PAIR>::SMEM_ALLOC;
+    auto kern = chunk_kernel<DH, PAIR, PLO>;
+    constexpr int smem = ChunkCfg<DH, PAIR, PLO>::SMEM_ALLOC;
     static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
     int dev = 0;
     cudaGetDevice(&dev);
@@ -573,15 +593,22 @@ bool chunk_supported(int dh, int P, int G) {
 // two halves of whole 64-column blocks; one CTA per block otherwise.  At dh
 // 256 always pairs (a lone block's partner has no rows): one CTA's 64 KB
 // stages would leave room for only two beside P_hi and P_lo.
-cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int dh,
-                         cudaStream_t s) {
+template <bool PLO>
+cudaError_t launch_chunk_p(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int dh,
+                           cudaStream_t s) {
     const bool pair = p.n_qblocks >= 2;
     switch (dh) {
-        case 64: return launch_chunk_t<64, false>(p, tk, tv, s);
-        case 128: return pair ? launch_chunk_t<128, true>(p, tk, tv, s) : launch_chunk_t<128, false>(p, tk, tv, s);
-        case 256: return launch_chunk_t<256, true>(p, tk, tv, s);
+        case 64: return launch_chunk_t<64, false, PLO>(p, tk, tv, s);
+        case 128:
+            return pair ? launch_chunk_t<128, true, PLO>(p, tk, tv, s) : launch_chunk_t<128, false, PLO>(p, tk, tv, s);
+        case 256: return launch_chunk_t<256, true, PLO>(p, tk, tv, s);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_chunk(const ChunkParams &p, const CUtensorMap *tk, const CUtensorMap *tv, int dh,
+                         cudaStream_t s) {
+    return p.p_f16 ? launch_chunk_p<false>(p, tk, tv, dh, s) : launch_chunk_p<true>(p, tk, tv, dh, s);
 }
 
 }  // namespace gkv

@@ -184,6 +184,7 @@ struct ChunkParams {
     void *out;          // q's layout; fp32, or fp16 when out_f16
     int32_t head_major;
     int32_t out_f16;
+    int32_t p_f16;      // P rounded once to fp16 (GKV_ATTEND_P_F16), else P_hi + P_lo
     int32_t *status;
     int32_t n_q, G, kvh, P, num_pages;
     int32_t qtok;       // query tokens per CTA

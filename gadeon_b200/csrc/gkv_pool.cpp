@@ -499,6 +499,7 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
                    const void *v_new = nullptr, const gkv::ProducerArgs *prod = nullptr) {
     const int32_t head_major = (flags & GKV_ATTEND_HEAD_MAJOR) ? 1 : 0;
     const int32_t out_f16 = (flags & GKV_ATTEND_OUT_F16) ? 1 : 0;
+    const int32_t p_f16 = (flags & GKV_ATTEND_P_F16) ? 1 : 0;
     if (n == 0) return GKV_OK;
     const int TK = pool->tile_keys, KVH = pool->cfg.kv_heads;
     const bool chunk = (int64_t)n_q * group > 16;  // many rows per kv head: tcgen05 chunk kernel
@@ -541,6 +542,7 @@ int enqueue_attend(gkv_pool *pool, int32_t n, const int32_t *ids, int32_t n_q, i
         c.out = out;
         c.head_major = head_major;
         c.out_f16 = out_f16;
+        c.p_f16 = p_f16;
         c.status = pool->d_status;
         c.n_q = n_q;
         c.G = group;
@@ -941,7 +943,7 @@ int gkv_seed(gkv_pool *pool, int32_t seq_id, const void *K, const void *V, int64
 int gkv_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
                   const void *q, void *out, float scale, uint32_t flags, void *stream) {
     if (!pool) return fail(GKV_ERR_INVALID, "null pool");
-    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16))
+    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16 | GKV_ATTEND_P_F16))
         return fail(GKV_ERR_INVALID, "unknown flags 0x%x", flags);
     int rc = check_batch(pool, n_seqs, seq_ids);
     if (rc) return rc;
@@ -971,7 +973,7 @@ int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                          const void *k, const void *v, const void *q, void *out, float scale, uint32_t flags,
                          void *stream) {
     if (!pool) return fail(GKV_ERR_INVALID, "null pool");
-    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16))
+    if (flags & ~(uint32_t)(GKV_ATTEND_HEAD_MAJOR | GKV_ATTEND_OUT_F16 | GKV_ATTEND_P_F16))
         return fail(GKV_ERR_INVALID, "unknown flags 0x%x", flags);
     int rc = check_batch(pool, n_seqs, seq_ids);
     if (rc) return rc;

@@ -42,6 +42,7 @@ GKV_ERR_CAPACITY = 6
 # gkv_attend_ex / gkv_append_attend_ex flags
 GKV_ATTEND_HEAD_MAJOR = 1  # q / out [n, kv_heads, n_q, group, head_dim]; k / v [n, kv_heads, n_q, head_dim]
 GKV_ATTEND_OUT_F16 = 2     # out fp16, rounded to nearest even
+GKV_ATTEND_P_F16 = 4       # chunk path: softmax weights rounded once to fp16 (the Metal attn_batch_mm arithmetic)
 
 # Every entry point include/gadeon_kv.h declares.
 EXPORTED = (
@@ -217,6 +218,11 @@ def _stream_ptr(stream) -> Optional[int]:
     return stream.cuda_stream
 
 
+def _attend_flags(head_major: bool, out_f16: bool, p_f16: bool) -> int:
+    return ((GKV_ATTEND_HEAD_MAJOR if head_major else 0) | (GKV_ATTEND_OUT_F16 if out_f16 else 0)
+            | (GKV_ATTEND_P_F16 if p_f16 else 0))
+
+
 class BlockPool:
     """One full-attention layer's page pool on one GPU (``gkv_pool``)."""
 
@@ -307,25 +313,26 @@ class BlockPool:
 
     def attend(self, seq_ids: Sequence[int], n_q: int, group: int, q, out=None,
                scale: Optional[float] = None, stream=None, head_major: bool = False,
-               out_f16: bool = False):
+               out_f16: bool = False, p_f16: bool = False):
         """q: [n, n_q, kv_heads*group, head_dim] fp16 (head_major: the
         reference's [n, kv_heads, n_q, group, head_dim]); returns the result
         in q's layout, fp32 (out_f16: fp16).  Row r of a sequence sees keys
-        [0, length - n_q + r]."""
+        [0, length - n_q + r].  p_f16: the chunk path (n_q * group > 16)
+        rounds the softmax weights once to fp16 (GKV_ATTEND_P_F16)."""
         ids = _i32(seq_ids)
         qshape = self._qo_shape(len(ids), n_q, group, head_major)
         _check_shape("q", q, qshape, _F16)
         out = self._out(out, qshape, q, out_f16)
         if scale is None:
             scale = self.head_dim ** -0.5
-        flags = (GKV_ATTEND_HEAD_MAJOR if head_major else 0) | (GKV_ATTEND_OUT_F16 if out_f16 else 0)
+        flags = _attend_flags(head_major, out_f16, p_f16)
         _check(_lib.gkv_attend_ex(self._h, len(ids), _p32(ids), n_q, group, _dev_ptr(q),
                                   _dev_ptr(out), float(scale), flags, _stream_ptr(stream)))
         return out
 
     def append_attend(self, seq_ids: Sequence[int], n_q: int, group: int, k, v, q, out=None,
                       scale: Optional[float] = None, stream=None, head_major: bool = False,
-                      out_f16: bool = False):
+                      out_f16: bool = False, p_f16: bool = False):
         """Append n_q rows per sequence, then attend those n_q query rows.
         k, v: [n * n_q, kv_heads, head_dim] (head_major: [n, kv_heads, n_q,
         head_dim]); q / out as for :meth:`attend`."""
@@ -339,7 +346,7 @@ class BlockPool:
         out = self._out(out, qshape, q, out_f16)
         if scale is None:
             scale = self.head_dim ** -0.5
-        flags = (GKV_ATTEND_HEAD_MAJOR if head_major else 0) | (GKV_ATTEND_OUT_F16 if out_f16 else 0)
+        flags = _attend_flags(head_major, out_f16, p_f16)
         _check(_lib.gkv_append_attend_ex(self._h, n, _p32(ids), n_q, group, _dev_ptr(k),
                                          _dev_ptr(v), _dev_ptr(q), _dev_ptr(out), float(scale), flags,
                                          _stream_ptr(stream)))

@@ -150,7 +150,17 @@ enum gkv_attend_flags {
     GKV_ATTEND_HEAD_MAJOR = 1,
     /* out holds fp16: each fp32 result rounded to nearest even (verifyAttn
      * stores Float16(flat[...]), Engine.swift:2637) */
-    GKV_ATTEND_OUT_F16 = 2
+    GKV_ATTEND_OUT_F16 = 2,
+    /* The tensor-core chunk path (n_q * group > 16) multiplies V by the
+     * softmax weights rounded once to fp16, as the reference's Metal
+     * attn_batch_mm does (half P tile times half V into fp32,
+     * Kernels.metal:1891-1912), instead of by an fp16 pair P_hi + P_lo: a
+     * third fewer tensor-core operations, and each output element within
+     * 2^-10 x sum_i w_i |V_i| (+ fp32 rounding) of the exact result rather
+     * than within the element-wise tolerance of the fp32 host path.  The
+     * decode / verify path (n_q * group <= 16) ignores it: its split costs no
+     * MMA there. */
+    GKV_ATTEND_P_F16 = 4
 };
 
 /* gkv_attend with `flags` (gkv_attend_flags) choosing the layout of q and
