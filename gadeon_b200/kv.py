@@ -583,7 +583,7 @@ def host_flash_decode(q, pool: PagePool, G: int, stream=None):
 
 
 def paged_flash_batched(q, pool: PagePool, s0_global_pos: int, s_count: int, G: int, out=None,
-                        stream=None):
+                        stream=None, p_f16: bool = False):
     """``pagedFlashBatched(q:pool:tile:s0GlobalPos:sCount:G:)``
     (PagedAttention.swift:376-416) on the GPU: the S = s_count query rows
     q [kv_heads, S, G, head_dim] fp16 at global positions s0_global_pos + s,
@@ -591,7 +591,9 @@ def paged_flash_batched(q, pool: PagePool, s0_global_pos: int, s_count: int, G: 
     :512-529), scale = head_dim^-0.5.  Returns the normalized
     [kv_heads, S, G, head_dim] fp32 result (the Swift returns it flat).  The
     rows must be the pool's last S positions (the chunk appended first, as
-    Engine.batchedAttn does, Engine.swift:1797-1820)."""
+    Engine.batchedAttn does, Engine.swift:1797-1820).  p_f16: the softmax
+    weights rounded once to fp16 on the tensor-core path (GKV_ATTEND_P_F16,
+    the arithmetic of the Metal attn_batch_mm)."""
     bp = pool.block_pool
     if s0_global_pos + s_count != pool.length:
         raise GkvError(GKV_ERR_INVALID, f"rows {s0_global_pos}..{s0_global_pos + s_count - 1} are not the "
@@ -600,7 +602,7 @@ def paged_flash_batched(q, pool: PagePool, s0_global_pos: int, s_count: int, G: 
     if out is not None:
         out = out.reshape(1, bp.kv_heads, s_count, G, bp.head_dim)
     res = bp.attend([pool.seq_id], s_count, G, qq, out=out, scale=bp.head_dim ** -0.5, stream=stream,
-                    head_major=True)
+                    head_major=True, p_f16=p_f16)
     return res.reshape(bp.kv_heads, s_count, G, bp.head_dim)
 
 

@@ -298,9 +298,11 @@ public func hostFlashDecode(q: [UInt16], pool: PagePool, G: Int) -> [Float] {
 /// fp16 at global positions s0GlobalPos + s, each seeing keys
 /// [0, s0GlobalPos + s]; returns the normalized [kvHeads, sCount, G, dh]
 /// fp32 result.  The rows must be the pool's last sCount positions (append
-/// the chunk first, as Engine.batchedAttn does).
+/// the chunk first, as Engine.batchedAttn does).  pF16: the softmax weights
+/// rounded once to fp16 on the tensor-core path (GKV_ATTEND_P_F16), as the
+/// Metal attn_batch_mm computes them (Kernels.metal:1891-1912).
 public func pagedFlashBatched(q: [UInt16], pool: PagePool, s0GlobalPos: Int, sCount: Int,
-                              G: Int) throws -> [Float] {
+                              G: Int, pF16: Bool = false) throws -> [Float] {
     guard let bound = pool.ids, s0GlobalPos + sCount == pool.length else {
         throw GKVError(code: 1, message: "rows must be the pool's last \(sCount) positions")
     }
@@ -308,7 +310,7 @@ public func pagedFlashBatched(q: [UInt16], pool: PagePool, s0GlobalPos: Int, sCo
     var out = [Float](repeating: 0, count: pool.kvHeads * sCount * G * pool.dh)
     var seq = id
     let scale = Float(1.0 / Double(pool.dh).squareRoot())
-    let flags = UInt32(GKV_ATTEND_HEAD_MAJOR.rawValue)
+    let flags = UInt32(GKV_ATTEND_HEAD_MAJOR.rawValue | (pF16 ? GKV_ATTEND_P_F16.rawValue : 0))
     try q.withUnsafeBytes { qb in
         try out.withUnsafeMutableBytes { ob in
             try gkvTry(gkv_attend_ex(h, 1, &seq, Int32(sCount), Int32(G), qb.baseAddress, ob.baseAddress, scale,
