@@ -969,6 +969,16 @@ int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n
     return gkv_attend_ex(pool, n_seqs, seq_ids, n_q, group, q, out, scale, 0u, stream);
 }
 
+int gkv_attend_decode(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t group, const void *q,
+                      float *out, float scale, void *stream) {
+    return gkv_attend_ex(pool, n_seqs, seq_ids, 1, group, q, out, scale, 0u, stream);
+}
+
+int gkv_attend_causal(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
+                      const void *q, float *out, float scale, void *stream) {
+    return gkv_attend_ex(pool, n_seqs, seq_ids, n_q, group, q, out, scale, 0u, stream);
+}
+
 int gkv_append_attend_ex(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids, int32_t n_q, int32_t group,
                          const void *k, const void *v, const void *q, void *out, float scale, uint32_t flags,
                          void *stream) {

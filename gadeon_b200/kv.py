@@ -55,7 +55,7 @@ EXPORTED = (
     "gkv_rope_table", "gkv_serialize", "gkv_deserialize", "gkv_state_header", "gkv_state_read_header",
     "gkv_rewind_append", "gkv_mtp_rollback_f16", "gkv_conv_rollback_f16", "gkv_check_bounded_wait",
     "gkv_tile_at", "gkv_gdn_rollback_f16", "gkv_gdn_rollback", "gkv_noalloc_status",
-    "gkv_attend_ex", "gkv_append_attend_ex",
+    "gkv_attend_ex", "gkv_append_attend_ex", "gkv_attend_decode", "gkv_attend_causal",
 )
 
 
@@ -100,6 +100,8 @@ def load_library(path: str = LIB_PATH):
         "gkv_append": (C.c_int, [P, i32, i32p, i32p, P, P, P]),
         "gkv_seed": (C.c_int, [P, i32, P, P, i64, P]),
         "gkv_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, P]),
+        "gkv_attend_decode": (C.c_int, [P, i32, i32p, i32, P, P, f32, P]),
+        "gkv_attend_causal": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, P]),
         "gkv_append_attend": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, P]),
         "gkv_attend_ex": (C.c_int, [P, i32, i32p, i32, i32, P, P, f32, C.c_uint32, P]),
         "gkv_append_attend_ex": (C.c_int, [P, i32, i32p, i32, i32, P, P, P, P, f32, C.c_uint32, P]),

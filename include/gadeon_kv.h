@@ -130,6 +130,19 @@ int gkv_attend(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
                int32_t n_q, int32_t group, const void *q, float *out,
                float scale, void *stream);
 
+/* The two attention forms under their own names, for callers that bind
+ * decode and causal attention separately: gkv_attend_decode is gkv_attend
+ * with n_q = 1 (hostFlashDecode, PagedAttention.swift:317-366; Metal
+ * attn_head, Kernels.metal:1423-1439); gkv_attend_causal is gkv_attend
+ * (verifyAttn, Engine.swift:2620-2646; pagedFlashBatched,
+ * PagedAttention.swift:376-416; Metal attn_batch, Kernels.metal:1767-1793). */
+int gkv_attend_decode(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                      int32_t group, const void *q, float *out, float scale,
+                      void *stream);
+int gkv_attend_causal(gkv_pool *pool, int32_t n_seqs, const int32_t *seq_ids,
+                      int32_t n_q, int32_t group, const void *q, float *out,
+                      float scale, void *stream);
+
 /* One decode / verify / chunk step in one call: gkv_append of n_q rows per
  * sequence followed by gkv_attend of those n_q rows (Engine.stepHidden's
  * append + hostFlashDecode, Engine.swift:1921-1927; verifyAttn, :2620-2646;

@@ -152,3 +152,34 @@ def test_reference_shaped_calls(cuda, oracle):
     assert got.shape == (kvh, S, G, dh) and got.dtype == np.float32
     want = orc.attend_causal([s], S, q, G, dh ** -0.5, n_threads=8)
     assert_attn_close(got, to_head_major(want, kvh, G)[0], "paged_flash_batched")
+
+
+def test_named_entry_points_equal_gkv_attend(cuda, oracle):
+    """gkv_attend_decode (n_q = 1) and gkv_attend_causal are gkv_attend under
+    the names a caller binding the two forms separately uses: same bits."""
+    import ctypes as C
+
+    from gadeon_b200 import kv
+    torch = cuda
+    lib = kv.load_library()
+    kvh, dh, G = 2, 256, 4
+    pr = Pair(torch, oracle, kvh=kvh, dh=dh, P=16, num_pages=3000)
+    ids = [pr.new_seq() for _ in range(4)]
+    pr.append(ids, [90, 700, 2000, 5000])
+    n = len(ids)
+    cids = (C.c_int32 * n)(*ids)
+    scale = dh ** -0.5
+    for n_q in (1, 4, 64):
+        q = dev_f16(torch, oracle.normal_f16(81, n_q, (n, n_q, kvh * G, dh)))
+        ref = pr.gpu.attend(ids, n_q, G, q, scale=scale)
+        got = torch.full_like(ref, float("nan"))
+        if n_q == 1:
+            rc = lib.gkv_attend_decode(pr.gpu._h, n, cids, G, q.data_ptr(), got.data_ptr(), scale, None)
+            assert rc == 0, lib.gkv_last_error()
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int32), ref.view(torch.int32))
+            got.fill_(float("nan"))
+        rc = lib.gkv_attend_causal(pr.gpu._h, n, cids, n_q, G, q.data_ptr(), got.data_ptr(), scale, None)
+        assert rc == 0, lib.gkv_last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), n_q
