@@ -29,12 +29,38 @@ def imbalance(tokens: Sequence[int], shards: List[List[int]]) -> float:
     return max(loads) / mean if mean else 1.0
 
 
+# Device index of each job sequence's row in the gathered buffer, per
+# (partition, padded shard size, device): built and validated once.
+_ORDER_CACHE: dict = {}
+
+
+def _job_order(shards: List[List[int]], n_max: int, device):
+    import torch
+
+    key = (tuple(tuple(int(i) for i in s) for s in shards), n_max, str(device))
+    idx = _ORDER_CACHE.get(key)
+    if idx is None:
+        # the shards must partition 0..n_job-1 (checked here, before an index
+        # ever reaches a device kernel)
+        n_all = sum(len(s) for s in shards)
+        if sorted(i for s in key[0] for i in s) != list(range(n_all)):
+            raise ValueError("shards do not partition the job's sequence indices 0..n-1")
+        src = np.empty(n_all, dtype=np.int64)
+        for r, s in enumerate(key[0]):
+            src[np.asarray(s, dtype=np.int64)] = r * n_max + np.arange(len(s), dtype=np.int64)
+        idx = torch.as_tensor(src, device=device)
+        _ORDER_CACHE[key] = idx
+    return idx
+
+
 def gather_outputs(local, shards: List[List[int]], rank: int, group=None):
     """All-gather every rank's per-sequence outputs (rows in the order of
     its shard) and return them in job order: a tensor [n_job, *row_shape].
 
     Ranks hold different numbers of sequences, so each pads to the largest
-    shard before one all_gather_into_tensor (NCCL) / all_gather (gloo)."""
+    shard before one all_gather_into_tensor (NCCL) / all_gather (gloo); one
+    index_select then puts the rows in job order, with an index built once
+    per partition (no host-device transfer on later calls)."""
     import torch
     import torch.distributed as dist
 
@@ -43,24 +69,17 @@ def gather_outputs(local, shards: List[List[int]], rank: int, group=None):
     row_shape = tuple(local.shape[1:])
     if local.shape[0] != len(shards[rank]):
         raise ValueError(f"rank {rank} holds {local.shape[0]} rows for a shard of {len(shards[rank])}")
-    # the shards must partition 0..n_job-1 (checked here, before an index
-    # ever reaches a device kernel)
-    n_all = sum(len(s) for s in shards)
-    if sorted(i for s in shards for i in s) != list(range(n_all)):
-        raise ValueError("shards do not partition the job's sequence indices 0..n-1")
-    padded = torch.zeros((n_max,) + row_shape, dtype=local.dtype, device=local.device)
-    padded[: local.shape[0]] = local
+    order = _job_order(shards, n_max, local.device)
+    if local.shape[0] == n_max and local.is_contiguous():
+        padded = local
+    else:
+        padded = torch.zeros((n_max,) + row_shape, dtype=local.dtype, device=local.device)
+        padded[: local.shape[0]] = local
     if dist.get_backend(group) == "nccl":
         out = torch.empty((world * n_max,) + row_shape, dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(out, padded, group=group)
-        parts = list(out.view((world, n_max) + row_shape))
     else:
         parts = [torch.empty_like(padded) for _ in range(world)]
         dist.all_gather(parts, padded, group=group)
-    n_job = sum(len(s) for s in shards)
-    job = torch.empty((n_job,) + row_shape, dtype=local.dtype, device=local.device)
-    for r, s in enumerate(shards):
-        if s:
-            idx = torch.as_tensor(np.asarray(s, dtype=np.int64), device=local.device)
-            job[idx] = parts[r][: len(s)]
-    return job
+        out = torch.cat(parts, 0)
+    return out.index_select(0, order)
