@@ -78,10 +78,11 @@ def test_pinned_host_buffers_match_device_buffers(cuda, oracle):
 
 def test_pageable_host_buffers_staged(cuda, oracle):
     """Plain (pageable) host arrays -- what a Swift [Float] or a numpy array
-    is -- are staged by the library through device memory of the pool: the
-    call copies them in and the output back (one cudaMemcpyAsync each) and
-    returns with the result in place.  Every hot-path call gives the same
-    bits as with device buffers, and the cache state stays bit-exact."""
+    is -- are staged by the library through a page-locked bounce buffer the
+    pool owns: the call copies them in, the kernels read and write the
+    bounce buffer in place, and the call returns with the output copied back
+    in place.  Every hot-path call gives the same bits as with device
+    buffers, and the cache state stays bit-exact."""
     import gadeon_b200 as gk
     torch = cuda
     G, dh, P, kvh = 4, 128, 16, 2
@@ -157,6 +158,48 @@ def test_pageable_host_buffers_staged(cuda, oracle):
     torch.cuda.synchronize()
     dev.check_state()
     host.check_state()
+
+
+def test_pageable_megabyte_buffers(cuda, oracle):
+    """Staged copies of a few MB (the bounce buffer grows to hold them): a
+    6,000-row append from pageable k/v, a compact into pageable K/V, and a
+    64-sequence decode with pageable q and out, each bit-exact against the
+    oracle or the device-buffer call."""
+    import gadeon_b200 as gk
+    torch = cuda
+    G, dh, P, kvh = 4, 256, 16, 2
+    nH = kvh * G
+    dev = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=2000, max_seqs=80, seed=9)
+    host = Pair(cuda, oracle, kvh=kvh, dh=dh, P=P, num_pages=2000, max_seqs=80, seed=9)
+    ids = [dev.new_seq() for _ in range(64)]
+    assert [host.new_seq() for _ in range(64)] == ids
+    lib = gk.load_library()
+    idarr = np.array(ids, dtype=np.int32)
+    pid = idarr.ctypes.data_as(C.POINTER(C.c_int32))
+    ctx = np.full(64, 8, dtype=np.int32)
+    ctx[5] = 6000
+    k, v = dev.rows(int(ctx.sum()))  # 6.4 MB each
+    dev.gpu.append(ids, ctx, dev_f16(torch, k), dev_f16(torch, v))
+    kp, vp = np.array(k, copy=True), np.array(v, copy=True)
+    assert lib.gkv_append(host.gpu._h, 64, pid, ctx.ctypes.data_as(C.POINTER(C.c_int32)), kp.ctypes.data,
+                          vp.ctypes.data, None) == 0, lib.gkv_last_error()
+    for pr in (dev, host):
+        assert pr.orc.append(ids, ctx, k, v) == 0
+    Kp = np.zeros((kvh, 6000, dh), dtype=np.uint16)  # 6.1 MB each
+    Vp = np.zeros_like(Kp)
+    assert lib.gkv_compact_seq(host.gpu._h, ids[5], Kp.ctypes.data, Vp.ctypes.data, None) == 0
+    oK, oV = host.orc.compact(ids[5])
+    assert np.array_equal(Kp, oK) and np.array_equal(Vp, oV)
+    q = oracle.normal_f16(74, 0, (64, 1, nH, dh))  # 256 KB in, 512 KB out
+    want = dev.gpu.attend(ids, 1, G, dev_f16(torch, q)).cpu().numpy()
+    qp = np.array(q, copy=True)
+    outp = np.full((64, 1, nH, dh), np.nan, dtype=np.float32)
+    assert lib.gkv_attend(host.gpu._h, 64, pid, 1, G, qp.ctypes.data, outp.ctypes.data,
+                          C.c_float(dh ** -0.5), None) == 0, lib.gkv_last_error()
+    assert np.array_equal(outp, want)
+    torch.cuda.synchronize()
+    dev.check_state(pages=False)
+    host.check_state(pages=False)
 
 
 def test_gdn_rollback_refuses_host_memory(cuda, oracle):
