@@ -551,53 +551,59 @@ def run_ours(args, rank, world, local):
                 if rank == 0:
                     job_to_host(oh[ti], job, ti)
 
-        # staged copies: per-layer device buffers, H2D on one copy stream
-        # (layer l+1's inputs while layer l runs), D2H of each layer's output
-        # on another (while the next layer runs); events order every reuse
+        # staged copies: device buffers for two steps (by step parity).  The
+        # next step's q/k/v move on one copy stream while this step runs, each
+        # layer's output moves back on another while the next layer runs, and
+        # the launch stream waits on events once per step (so the launches of
+        # a step stay chained back to back).
         h2d_stream, d2h_stream = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-        qd_l = [torch.empty_like(qd) for _ in range(L)]
-        kd_l = [torch.empty_like(kd) for _ in range(L)]
-        vd_l = [torch.empty_like(vd) for _ in range(L)]
-        in_ready = [torch.cuda.Event() for _ in range(L)]
-        in_free = [torch.cuda.Event() for _ in range(L)]
-        out_free = [torch.cuda.Event() for _ in range(L)]
+        qd_s = [[torch.empty_like(qd) for _ in range(L)] for _ in range(2)]
+        kd_s = [[torch.empty_like(kd) for _ in range(L)] for _ in range(2)]
+        vd_s = [[torch.empty_like(vd) for _ in range(L)] for _ in range(2)]
+        od_s = [[torch.empty_like(outs[0]) for _ in range(L)] for _ in range(2)]
+        in_ready, in_free, out_free = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
         for ev_ in in_free + out_free:
             ev_.record()
 
-        def stage_in(ti, layer):
-            h2d_stream.wait_event(in_free[layer])  # the layer's previous launch has read them
+        def stage_step_in(ti):
+            sb = ti % 2
+            h2d_stream.wait_event(in_free[sb])  # the step two back has read these buffers
             with torch.cuda.stream(h2d_stream):
-                qd_l[layer].copy_(qh[ti, layer], non_blocking=True)
-                kd_l[layer].copy_(kh[ti, layer], non_blocking=True)
-                vd_l[layer].copy_(vh[ti, layer], non_blocking=True)
-                in_ready[layer].record(h2d_stream)
+                for layer in range(L):
+                    qd_s[sb][layer].copy_(qh[ti, layer], non_blocking=True)
+                    kd_s[sb][layer].copy_(kh[ti, layer], non_blocking=True)
+                    vd_s[sb][layer].copy_(vh[ti, layer], non_blocking=True)
+                in_ready[sb].record(h2d_stream)
 
         def staged(i, ti):
             # the call on device buffers that copy engines fill from and drain
-            # to page-locked host memory, overlapped with the neighbouring
-            # layers' launches; N GPUs: the gathered job's outputs instead
+            # to page-locked host memory; N GPUs: the gathered job's outputs
+            # go to the host instead of each layer's
             main = torch.cuda.current_stream()
-            stage_in(ti, 0)
+            sb = ti % 2
+            if ti == 0:
+                stage_step_in(0)  # a block's first step: nothing prefetched it
+            if ti + 1 < K:
+                stage_step_in(ti + 1)
+            main.wait_event(in_ready[sb])
+            if world == 1:
+                main.wait_event(out_free[sb])  # the outputs of the step two back are out
             for layer in range(L):
-                main.wait_event(in_ready[layer])
-                if world == 1:
-                    main.wait_event(out_free[layer])  # the previous step's copy of this output is out
-                pools[layer].append_attend(ids[layer], 1, G, kd_l[layer], vd_l[layer], qd_l[layer],
-                                           out=outs[layer])
-                in_free[layer].record(main)
-                if layer + 1 < L:
-                    stage_in(ti, layer + 1)
+                pools[layer].append_attend(ids[layer], 1, G, kd_s[sb][layer], vd_s[sb][layer], qd_s[sb][layer],
+                                           out=od_s[sb][layer] if world == 1 else outs[layer])
                 if world == 1:
                     d2h_stream.wait_stream(main)
                     with torch.cuda.stream(d2h_stream):
-                        oh[ti, layer].copy_(outs[layer], non_blocking=True)
-                        out_free[layer].record(d2h_stream)
+                        oh[ti, layer].copy_(od_s[sb][layer], non_blocking=True)
+            in_free[sb].record(main)
             if world > 1:
                 job = job_outputs()
                 if rank == 0:
                     job_to_host(oh[ti], job, ti)
-            elif ti == K - 1:
-                main.wait_stream(d2h_stream)  # the block ends with its last copy
+            else:
+                out_free[sb].record(d2h_stream)
+                if ti == K - 1:
+                    main.wait_stream(d2h_stream)  # the block ends with its last copy
 
         def pageable(i, ti):
             # plain host arrays through the public call: the library stages
@@ -705,7 +711,7 @@ def run_ours(args, rank, world, local):
                                  if e2e_ms_max <= e2e_copy_max else
                                  ("cudaMemcpyAsync of q/k/v to the device" + (" and of the outputs back" if world == 1
                                                                               else "")
-                                  + ", on copy streams overlapping the neighbouring layers' launches"))
+                                  + ", on copy streams overlapping the launches"))
                               + ("" if world == 1 else
                                  "; every step's outputs gathered over NCCL into job order (shard.gather_outputs) "
                                  "and copied by rank 0 to page-locked host memory on a copy stream that overlaps "
@@ -713,9 +719,9 @@ def run_ours(args, rank, world, local):
                  "block_ms_per_step": e2e[5] if e2e_ms_max <= e2e_copy_max else e2e[6],
                  "in_place_value": tokens / (e2e_ms_max * 1e-3),
                  "staged_copy_value": tokens / (e2e_copy_max * 1e-3),
-                 "staged_copy_note": "same step with cudaMemcpyAsync of q/k/v to per-layer device buffers and of "
-                                     "each output back, on two copy streams that overlap the neighbouring "
-                                     "layers' launches",
+                 "staged_copy_note": "same step with cudaMemcpyAsync of q/k/v to device buffers (the next step's "
+                                     "during this one) and of each layer's output back (during the next layer), "
+                                     "on two copy streams; the launch stream waits on them once per step",
                  "pageable_value": tokens / (e2e_page_max * 1e-3),
                  "pageable_note": "same step given plain (pageable) host arrays, which the library copies "
                                   "through a pool-owned page-locked bounce buffer read and written in place"}
