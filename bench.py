@@ -620,6 +620,23 @@ def run_ours(args, rank, world, local):
         legs += [zero_copy, staged, pageable]
 
     times, clk = interleaved_blocks(torch, dist, world, W, K, legs, local, R, rewind)
+    # one GPU: every block ran the same K steps from the same contexts, so
+    # the host buffers the last e2e blocks wrote must equal, bit for bit, the
+    # outputs of the same steps run on device buffers
+    e2e_check = None
+    if not args.no_e2e and world == 1:
+        ref = torch.empty((K, L, S, 1, nH, dh), dtype=torch.float32, device=dev)
+        for ti in range(K):
+            step(W + ti, ti)
+            for layer in range(L):
+                ref[ti, layer].copy_(outs[layer])
+        rewind()
+        ref_h = ref.cpu()
+        e2e_check = {"what": "outputs of the last staged-copy and pageable blocks vs the same steps on device "
+                             "buffers, bit for bit",
+                     "staged_equal": bool(torch.equal(oh.view(torch.int32), ref_h.view(torch.int32))),
+                     "pageable_equal": bool(torch.equal(op.view(torch.int32), ref_h.view(torch.int32)))}
+        del ref, ref_h
     blocks = times[0]
     ms = statistics.median(blocks)
     attend_avg_ms = ms / L  # back-to-back launches: gaps between them included
@@ -723,6 +740,7 @@ def run_ours(args, rank, world, local):
                                      "during this one) and of each layer's output back (during the next layer), "
                                      "on two copy streams; the launch stream waits on them once per step",
                  "pageable_value": tokens / (e2e_page_max * 1e-3),
+                 "check": e2e_check,
                  "pageable_note": "same step given plain (pageable) host arrays, which the library copies "
                                   "through a pool-owned page-locked bounce buffer read and written in place"}
                 if e2e else None),
