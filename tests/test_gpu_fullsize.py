@@ -13,7 +13,8 @@ workload generators), with the element-wise tolerance of conftest.py:
   free list bit-exact after every cycle;
 * config 4 -- 2 sequences, each a seeded 16,384-token context plus one
   4,096-row chunk (the tensor-core chunk kernel); 512 rows of every head
-  checked (the first 64, the last 64 and 384 spread between);
+  checked (the first 64, the last 64 and 384 spread between); the same rows
+  again with GKV_ATTEND_P_F16, within that option's error bound;
 * config 5 -- 16 sequences of the long-context job, contexts log-uniform in
   [4096, 131072] (the longest of the job included), 4 fused decode steps.
 
@@ -166,3 +167,45 @@ def test_config5_full_size_long_context_decode(cuda, oracle):
         assert_attn_close(got, want, f"config 5 step {step}")
         check_state(pr, ids, f"config 5 step {step}")
     check_contents(pr, ids, "config 5")
+
+
+def test_config4_full_size_chunk_p_f16(cuda, oracle):
+    """The opt-in GKV_ATTEND_P_F16 at config 4's size: 2 sequences of 16,384
+    seeded rows plus a 4,096-row chunk; the same 512 rows of every head as
+    the default's test, each element within 2^-10 x sum_i w_i |V_i| + 1e-5
+    of the oracle (the bound computed on a twin oracle pool holding |V|)."""
+    from gadeon_b200 import BlockPool
+    from gadeon_b200 import workload as W
+    cfg = W.CONFIGS[4]
+    n_seqs, n_q = 2, cfg.n_q
+    kvh, dh, P, G = cfg.kv_heads, cfg.head_dim, cfg.page_tokens, cfg.group
+    lens = [int(c) + n_q for c in W.contexts(4, BENCH_SEED, n_seqs)]
+    pages = sum((n + P - 1) // P for n in lens) + 16
+    gpu = BlockPool(kvh, dh, P, pages, n_seqs + 1, pages, seed=4404)
+    orc = oracle.OraclePool(kvh, dh, P, pages, 4404)
+    absorc = oracle.OraclePool(kvh, dh, P, pages, 4404)
+
+    def gen(i):
+        return (oracle.normal_f16(4504, 2 * i, (kvh, lens[i], dh)),
+                oracle.normal_f16(4504, 2 * i + 1, (kvh, lens[i], dh)))
+
+    ids = []
+    with ThreadPoolExecutor(THREADS) as ex:
+        for i, (K, V) in enumerate(ex.map(gen, range(n_seqs))):
+            s = gpu.seq_create()
+            assert orc.seq_create() == s and absorc.seq_create() == s
+            gpu.seed(s, dev_f16(cuda, K), dev_f16(cuda, V), lens[i])
+            assert orc.seed(s, K, V, lens[i]) == 0
+            assert absorc.seed(s, K, V & np.uint16(0x7FFF), lens[i]) == 0
+            ids.append(s)
+    scale = dh ** -0.5
+    q = oracle.normal_f16(4604, 0, (n_seqs, n_q, cfg.n_heads, dh))
+    got = gpu.attend(ids, n_q, G, dev_f16(cuda, q), scale=scale, p_f16=True).cpu().numpy()
+    rows = np.unique(np.concatenate([np.arange(64), np.arange(n_q - 64, n_q),
+                                     np.linspace(64, n_q - 65, 384).astype(np.int64)]))
+    want = orc.attend_rows(ids, n_q, rows, q[:, rows], G, scale, n_threads=THREADS)
+    bound = absorc.attend_rows(ids, n_q, rows, q[:, rows], G, scale, n_threads=THREADS)
+    err = np.abs(got[:, rows] - want)
+    lim = 2.0 ** -10 * bound + 1e-5
+    assert np.all(err <= lim), f"max |d| {err.max():.3g}, max |d| / B {np.max(err / np.maximum(bound, 1e-30)):.3g}"
+    assert gpu.device_status() == 0
