@@ -503,7 +503,7 @@ def run_ours(args, rank, world, local):
 
     def job_outputs():
         # every layer's outputs of the step, gathered over the GPUs into job
-        # order (pad to the largest shard, one NCCL all-gather, reorder)
+        # order (one NCCL all-gather, one index_select)
         local_out = torch.stack([o.reshape(S, -1) for o in outs], dim=1).reshape(S, -1)
         return gather_outputs(local_out, shards, rank)
 
@@ -607,8 +607,8 @@ def run_ours(args, rank, world, local):
 
         def pageable(i, ti):
             # plain host arrays through the public call: the library stages
-            # them (one cudaMemcpyAsync per buffer; the call returns with out
-            # in place)
+            # them through its page-locked bounce buffer (the call returns with
+            # out in place)
             for layer in range(L):
                 pools[layer].append_attend(ids[layer], 1, G, kp[ti, layer], vp[ti, layer], qp[ti, layer],
                                            out=op[ti, layer] if world == 1 else outs[layer])
