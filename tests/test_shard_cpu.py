@@ -71,7 +71,13 @@ def _worker(rank, world, port, fail_rank, q):
         if rank == fail_rank:
             raise RuntimeError("rank failed before the gather")
         job = gather_outputs(local, shards, rank)
-        q.put((rank, "ok", job.numpy().tolist()))
+        # again with other rows on the same partition (the cached index), and
+        # on an equal-size partition (no padding copy)
+        job2 = gather_outputs(local * 10, shards, rank)
+        equal = [[0, 2, 5, 6], [1, 3, 4, 7]][:world] if world == 2 else None
+        job3 = (gather_outputs(torch.tensor([[float(i)] for i in equal[rank]]), equal, rank).numpy().tolist()
+                if equal else None)
+        q.put((rank, "ok", (job.numpy().tolist(), job2.numpy().tolist(), job3)))
     except Exception as e:  # the surviving rank must see an error, not hang
         q.put((rank, "error", type(e).__name__))
     finally:
@@ -104,9 +110,11 @@ def test_gather_outputs_job_order_gloo():
     res = _run(2, fail_rank=-1)
     want = [[float(i), float(i) * 2] for i in range(7)]
     for rank in range(2):
-        status, job = res[rank]
+        status, (job, job2, job3) = res[rank]
         assert status == "ok"
         assert job == want
+        assert job2 == [[10 * a, 10 * b] for a, b in want]
+        assert job3 == [[float(i)] for i in range(8)]
 
 
 def test_dead_rank_is_detected_by_the_collective():
